@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""Benchmark of the MoE-block hot path (QwenMoe._moe at Qwen1.5-MoE-A2.7B shapes).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill4096_int8_zipf|decode8_int8|gptq_asym_decode1|gptq_asym_prefill512]
+
+One step = one MoE block forward over one batch of seeded synthetic tokens
+(router -> top-4 -> routed experts -> combine + gated shared expert). Rank 0
+prints one JSON line. `value` is whole-job tokens/s with inputs resident in
+HBM; `e2e` is the same through the public API from pinned host buffers, with
+the host->device copy of the tokens and the device->host copy of the output
+inside the timed region. Each step is timed with CUDA events on the
+launching stream after an L2 flush (a 256 MiB write), and the dominant
+kernel is timed live through the block's stage events.
+
+--impl reference times the CPU implementation of the path (the oracle, a
+restatement of the reference's numpy/BLAS code) on this host's cores on the
+same workload; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+FLUSH_BYTES = 256 << 20
+CLOCK_FIELDS = (
+    "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default="prefill4096_int8_zipf")
+    ap.add_argument("--path", choices=("auto", "gemv", "gemm", "tc"), default="auto")
+    ap.add_argument("--act-dtype", choices=("f32", "bf16"), default="f32")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode-shape side measurement")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample budget")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {k: float(d[k]) for k in FALLBACK_PEAKS if k in d}, "measured"
+        except (ValueError, KeyError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def traffic_from_profiles(workload: str, stage: str) -> float | None:
+    """DRAM bytes per launch recorded from an ncu capture in profiles/*.md, as a
+    line `traffic_per_launch_bytes[<workload>/<stage>] = <bytes>`."""
+    key = f"traffic_per_launch_bytes[{workload}/{stage}]"
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            if key in line and "=" in line:
+                try:
+                    return float(line.split("=", 1)[1].strip().strip("`").split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling (200 ms) during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks-", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+            "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
+            "reasons": reasons,
+            "samples": len(rows),
+        }
+
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        info = [i for i in threadpool_info() if i.get("user_api") == "blas"]
+        if info:
+            return int(max(i.get("num_threads", 1) for i in info))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# workload accounting (algorithmic bytes and FLOPs)
+# ---------------------------------------------------------------------------
+
+
+def accounting(block, n: int, idx: np.ndarray, act_bytes: int) -> dict:
+    H, I, Is, E, k = block.hidden, block.inter, block.shared_inter, block.num_experts, block.top_k
+    lay, sh = block.layout, block.shared_layout
+    uniq = np.unique(idx)
+    U = len(uniq)
+    nk = n * k
+    # weight bytes each kernel must read once: gate+up (codes + scales (+ zeros)) and down
+    gu_w = sum(lay._weight_bytes(m) + lay._scale_bytes(m) + lay._zero_bytes(m) for m in ("gate_proj", "up_proj"))
+    dn_w = lay._weight_bytes("down_proj") + lay._scale_bytes("down_proj") + lay._zero_bytes("down_proj")
+    sh_gu = sum(sh._weight_bytes(m) + sh._scale_bytes(m) for m in ("gate_proj", "up_proj"))
+    sh_dn = sh._weight_bytes("down_proj") + sh._scale_bytes("down_proj")
+    gate_up_bytes = U * gu_w + sh_gu + n * H * act_bytes + (nk * I + n * Is) * 4
+    down_bytes = U * dn_w + sh_dn + (nk * I + n * Is) * 4 + (nk + n) * H * 4
+    block_weight_bytes = U * (gu_w + dn_w) + sh_gu + sh_dn + E * H * 4 + H * 4
+    return {
+        "unique_experts": int(U),
+        "gate_up_bytes": int(gate_up_bytes),
+        "down_bytes": int(down_bytes),
+        "block_weight_bytes": int(block_weight_bytes),
+        "gate_up_flops": int(2 * (nk * 2 * I * H + n * 2 * Is * H)),
+        "down_flops": int(2 * (nk * I * H + n * Is * H)),
+        "router_flops": int(2 * n * (E + 1) * H),
+        "block_flops": int(2 * (nk * 3 * I * H + n * 3 * Is * H + n * (E + 1) * H)),
+    }
+
+
+# ---------------------------------------------------------------------------
+# CPU side (oracle port of the reference's numpy path)
+# ---------------------------------------------------------------------------
+
+
+def cpu_baseline(block, x: np.ndarray, budget_s: float, max_tokens: int | None = None) -> dict:
+    from oracle import moe_oracle as O
+    from oracle.blocks import oracle_weights
+
+    w = oracle_weights(block)
+    n = x.shape[0] if max_tokens is None else min(x.shape[0], max_tokens)
+    xs = x[:n]
+    O.moe_block(xs[: min(n, 8)], w)  # warm BLAS / page in
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        O.moe_block(xs, w)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s or len(times) >= 5:
+            break
+    med = statistics.median(times)
+    return {
+        "value": n / med,
+        "unit": "tokens/s",
+        "cores": blas_threads(),
+        "kind": "port",
+        "sample": f"{len(times)} x {n} tokens of the same workload (median {med * 1e3:.1f} ms), numpy/BLAS float32 "
+                  f"restatement of QwenMoe._moe, blocked int8 kernel; host {cpu_model()}",
+    }
+
+
+# ---------------------------------------------------------------------------
+# the GPU arm
+# ---------------------------------------------------------------------------
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from expertrelay_b200 import synth
+
+    block, x = synth.make_workload(args.workload, seed=args.seed)
+    n = x.shape[0]
+    sample = n if args.steps + args.warmup <= 30 else min(n, 1024)
+    from oracle import moe_oracle as O
+    from oracle.blocks import oracle_weights
+
+    w = oracle_weights(block)
+    xs = x[:sample]
+    for _ in range(args.warmup):
+        O.moe_block(xs, w)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.moe_block(xs, w)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = sample * args.steps / total
+    line = {
+        "impl": "reference",
+        "metric": "MoE-block tokens/s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded N(0,0.02) weights in store encodings, N(0,1) activations",
+        "config": {"workload": args.workload, "tokens": n, "tokens_per_step": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+                         "sample": f"{sample} of {n} tokens per step; numpy/BLAS restatement of QwenMoe._moe "
+                                   f"(blocked int8 kernel) on {cpu_model()}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from expertrelay_b200 import _lib, synth
+    from expertrelay_b200.moe import MoeBlock
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    path = {"auto": _lib.PATH_AUTO, "gemv": _lib.PATH_GEMV, "gemm": _lib.PATH_GEMM, "tc": _lib.PATH_TC}[args.path]
+    act_dtype = torch.bfloat16 if args.act_dtype == "bf16" else torch.float32
+    act_bytes = 2 if args.act_dtype == "bf16" else 4
+
+    # weights are identical on every rank (same seed); each rank has its own tokens
+    block, x = synth.make_workload(args.workload, seed=args.seed)
+    if rank:
+        x = synth.make_tokens(args.seed + 7919 * rank, x.shape[0], block.hidden)
+    n = x.shape[0]
+    mb = MoeBlock.from_host_block(block, device=dev)
+    h_dev = torch.from_numpy(x).to(dev).to(act_dtype)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stage_ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(_lib.MOE_STAGES) + 1)]
+    for ev in stage_ev:
+        ev.record()
+    torch.cuda.synchronize()
+
+    # routing of this batch (for the accounting) and warm-up
+    _, _, idx, _ = mb.forward(h_dev, path=path, return_routing=True)
+    acct = accounting(block, n, idx.cpu().numpy(), act_bytes)
+    for _ in range(max(args.warmup, 3)):
+        mb.forward(h_dev, path=path)
+    torch.cuda.synchronize()
+
+    # timed region: K steps, each after an L2 flush, bracketed by barrier + sync
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stage_ms = {s: 0.0 for s in _lib.MOE_STAGES}
+    launches = C.c_int(0)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            mb.forward(h_dev, path=path, stage_events=stage_ev, launch_counter=launches)
+            ends[i].record()
+            stage_ev[-1].synchronize()
+            for j, s in enumerate(_lib.MOE_STAGES):
+                stage_ms[s] += stage_ev[j].elapsed_time(stage_ev[j + 1])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms_max = float(t.item())
+    value = world * n * args.steps / (total_ms_max / 1e3)
+    stage_avg = {s: v / args.steps for s, v in stage_ms.items()}
+
+    # end to end through the public API: pinned host tokens in, host output back
+    x_host = torch.from_numpy(x).to(act_dtype).pin_memory()
+    y_host = torch.empty((n, block.hidden), dtype=torch.float32).pin_memory()
+    e_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for _ in range(2):
+        y_host.copy_(mb.forward(x_host.to(dev, non_blocking=True), path=path), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        e_start[i].record()
+        hd = x_host.to(dev, non_blocking=True)
+        y_host.copy_(mb.forward(hd, path=path), non_blocking=True)
+        e_end[i].record()
+    torch.cuda.synchronize()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_start, e_end))
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    e2e_value = world * n * args.steps / (float(t.item()) / 1e3)
+
+    # roofline of the dominant stage
+    peaks, peak_src = load_peaks()
+    dom = max(("gate_up", "down"), key=lambda s: stage_avg[s])
+    tensor_bound = n >= 256
+    if tensor_bound:
+        work = acct["gate_up_flops"] if dom == "gate_up" else acct["down_flops"]
+        achieved = work / (stage_avg[dom] / 1e3) / 1e12
+        peak = peaks["bf16_tflops_sustained"]
+        roof = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dom, "algorithmic_flops_per_launch": work}
+    else:
+        work = acct["gate_up_bytes"] if dom == "gate_up" else acct["down_bytes"]
+        achieved = work / (stage_avg[dom] / 1e3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roof = {"bound": "hbm", "unit": "GB/s", "kernel": dom, "algorithmic_bytes_per_launch": work}
+    roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak, "peak_source": f"of {peak_src}",
+                 "traffic": traffic_from_profiles(args.workload, dom)})
+
+    line = {
+        "metric": "MoE-block tokens/s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32" if path in (_lib.PATH_GEMV, _lib.PATH_GEMM) or (path == _lib.PATH_AUTO) else "bf16",
+        "data": "synthetic: seeded N(0,0.02) weights in store encodings, N(0,1) activations",
+        "config": {
+            "workload": args.workload,
+            "tokens": n,
+            "hidden": block.hidden,
+            "experts": block.num_experts,
+            "top_k": block.top_k,
+            "expert_format": block.fmt,
+            "activations": args.act_dtype,
+            "path": args.path,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": "flushed before every timed step (256 MiB write)",
+        },
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(n * block.hidden * act_bytes),
+                "d2h_bytes_per_step": int(n * block.hidden * 4)},
+        "gpu_launches": int(launches.value),
+        "roofline": roof,
+        "stages_ms": stage_avg,
+        "block": {"weight_bytes": acct["block_weight_bytes"], "flops": acct["block_flops"],
+                  "unique_experts": acct["unique_experts"],
+                  "weight_GBps": acct["block_weight_bytes"] / (total_ms_max / args.steps / 1e3) / 1e9,
+                  "TFLOPs": acct["block_flops"] / (total_ms_max / args.steps / 1e3) / 1e12},
+        "clocks": clocks.summary(),
+    }
+    if block.meta.get("zipf"):
+        line["config"]["zipf_histogram"] = block.meta["zipf"]["realised"]
+
+    if rank == 0 and world == 1 and not args.no_decode and args.workload != "decode8_int8":
+        line["decode"] = decode_side(args, dev, mb, block, peaks, peak_src)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(block, x, args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def decode_side(args, dev, mb, block, peaks, peak_src) -> dict:
+    """Decode shape on the same experts (8 tokens, router without the Zipf
+    scaling): block tokens/s and the expert-weight streaming rate."""
+    import torch
+
+    from expertrelay_b200 import _lib, synth
+
+    base_router = block.meta.get("router_base")
+    if base_router is not None:
+        mb.router.copy_(torch.from_numpy(base_router).to(dev))
+    x = synth.make_tokens(args.seed, 8, block.hidden)
+    h = torch.from_numpy(x).to(dev)
+    _, _, idx, _ = mb.forward(h, path=_lib.PATH_GEMV, return_routing=True)
+    acct = accounting(block, 8, idx.cpu().numpy(), 4)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(_lib.MOE_STAGES) + 1)]
+    for e in ev:
+        e.record()
+    for _ in range(5):
+        mb.forward(h, path=_lib.PATH_GEMV)
+    torch.cuda.synchronize()
+    steps = max(args.steps, 20)
+    tot = 0.0
+    stage = {s: 0.0 for s in _lib.MOE_STAGES}
+    for _ in range(steps):
+        flush.zero_()
+        mb.forward(h, path=_lib.PATH_GEMV, stage_events=ev)
+        ev[-1].synchronize()
+        tot += ev[0].elapsed_time(ev[-1])
+        for j, s in enumerate(_lib.MOE_STAGES):
+            stage[s] += ev[j].elapsed_time(ev[j + 1])
+    ms = tot / steps
+    stage = {s: v / steps for s, v in stage.items()}
+    if base_router is not None:
+        mb.router.copy_(torch.from_numpy(block.router).to(dev))
+    gu_gbs = acct["gate_up_bytes"] / (stage["gate_up"] / 1e3) / 1e9
+    return {
+        "workload": "8 decode tokens, same int8 experts, unscaled router",
+        "tokens_per_s": 8 / (ms / 1e3),
+        "ms_per_block": ms,
+        "unique_experts": acct["unique_experts"],
+        "block_weight_GBps": acct["block_weight_bytes"] / (ms / 1e3) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "gate_up", "achieved": gu_gbs, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": gu_gbs / peaks["hbm_gbs"], "peak_source": f"of {peak_src}",
+                     "algorithmic_bytes_per_launch": acct["gate_up_bytes"]},
+        "stages_ms": stage,
+    }
+
+
+if __name__ == "__main__":
+    main()

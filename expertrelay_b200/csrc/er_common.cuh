@@ -1,0 +1,111 @@
+// er_common.cuh -- shared helpers for libexpertrelay_b200 (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/expertrelay_b200.h"
+
+namespace er {
+
+// ---- error reporting (er_capi.cu) ---------------------------------------
+int fail(int code, const char* fmt, ...);                 // records the message, returns code
+int cuda_check(cudaError_t e, const char* what);          // ER_OK or ER_ECUDA with the CUDA message
+inline int launch_check(const char* what) { return cuda_check(cudaGetLastError(), what); }
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 8;
+constexpr size_t kRecordAlign = 4096;  // store/unbuffered_io.py ALIGNMENT
+
+__host__ __device__ inline size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+// ---- expert record layout (store/layout.py:53-115, store/int4.py:165-244) ----
+// Matrices in on-disk order: gate [inter, hidden], up [inter, hidden],
+// down [hidden, inter]. Weights of all three first, then their scales, then
+// (ER_FMT_INT4_ZP only) their zero points, then zero padding to 4096 bytes.
+struct RecordGeom {
+  int fmt, hidden, inter, group;
+
+  __host__ __device__ int rows(int which) const { return which == 2 ? hidden : inter; }
+  __host__ __device__ int cols(int which) const { return which == 2 ? inter : hidden; }
+  __host__ __device__ size_t weight_bytes(int which) const {
+    size_t e = (size_t)rows(which) * cols(which);
+    return fmt == ER_FMT_INT8 ? e : e / 2;
+  }
+  __host__ __device__ size_t scale_bytes(int which) const {
+    return fmt == ER_FMT_INT8 ? (size_t)rows(which) * 4 : (size_t)rows(which) * (cols(which) / group) * 2;
+  }
+  __host__ __device__ size_t zero_bytes(int which) const {
+    return fmt == ER_FMT_INT4_ZP ? (size_t)rows(which) * (cols(which) / group) : 0;
+  }
+  __host__ __device__ size_t weight_offset(int which) const {
+    size_t off = 0;
+    for (int i = 0; i < which; ++i) off += weight_bytes(i);
+    return off;
+  }
+  __host__ __device__ size_t scale_offset(int which) const {
+    size_t off = weight_offset(3);
+    for (int i = 0; i < which; ++i) off += scale_bytes(i);
+    return off;
+  }
+  __host__ __device__ size_t zero_offset(int which) const {
+    size_t off = scale_offset(3);
+    for (int i = 0; i < which; ++i) off += zero_bytes(i);
+    return off;
+  }
+  __host__ __device__ size_t payload_bytes() const { return zero_offset(3); }
+  __host__ __device__ size_t record_bytes() const { return align_up(payload_bytes(), kRecordAlign); }
+};
+
+// ---- small device helpers -----------------------------------------------
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// SiLU and sigmoid exactly as the reference writes them
+// (runtime/qwen_moe.py:149-154): x / (1 + e^-x), 1 / (1 + e^-x).
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float half_bits_to_f32(uint16_t b) {
+  return __half2float(__ushort_as_half(b));
+}
+
+// Signed int8 lanes of a 32-bit word -> float.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* f) {
+  f[0] = (float)(int8_t)(w & 0xff);
+  f[1] = (float)(int8_t)((w >> 8) & 0xff);
+  f[2] = (float)(int8_t)((w >> 16) & 0xff);
+  f[3] = (float)(int8_t)(w >> 24);
+}
+
+// 8 nibbles of a 32-bit word (lowest first = lower input column) -> float codes 0..15.
+__device__ __forceinline__ void u4x8_to_f32(uint32_t w, float* f) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = (float)((w >> (4 * j)) & 0xf);
+}
+
+// Read-only, L1-bypassing 16-byte global load for weights read once.
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ld_stream_u2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+
+}  // namespace er

@@ -1,0 +1,108 @@
+// er_internal.cuh -- internal types and launchers shared by the .cu files.
+#pragma once
+
+#include "er_common.cuh"
+
+namespace er {
+
+constexpr int kRouterTok = 8;  // tokens per router CTA
+
+// A schedule enumerates work items over the active groups. Group g < E is
+// routed expert g (its tokens in expert-sorted order), group E is the shared
+// expert (all n tokens). Item count of group g = mtiles(g) * ntiles(g).
+struct SchedSpec {
+  int bm;     // tokens per item (0: all tokens of the group in one item)
+  int bn;     // output units per item
+  int which;  // 0: gate/up (units = intermediate columns), 1: down (units = hidden rows)
+};
+
+constexpr int kNumSched = 2;
+
+// Routing plan, written by plan_kernel into the workspace.
+struct Plan {
+  int n, E, k, nk;
+  int error;                           // nonzero: an expert id was out of range
+  int num_active;                      // groups with at least one token (shared last)
+  int counts[kMaxExperts + 1];         // tokens per group (counts[E] = n)
+  int offsets[kMaxExperts + 1];        // first expert-sorted position of each routed group
+  int active[kMaxExperts + 1];         // active group ids, ascending, shared last
+  int item_start[kNumSched][kMaxExperts + 2];  // prefix of items over active groups
+  SchedSpec sched[kNumSched];
+};
+
+// Everything a grouped expert kernel needs to find a group's tokens and weights.
+struct GroupArgs {
+  const Plan* plan;
+  const uint64_t* expert_records;  // device [E]
+  const uint8_t* shared_record;
+  int fmt;                         // routed format (shared is ER_FMT_INT8)
+  int H, I, Is, group, E, n;
+  const int32_t* perm_token;       // [nk] token of each expert-sorted position
+  const float* perm_w;             // [nk] routing weight of each position
+  const float* gate_sig;           // [n] sigmoid(shared gate logit)
+};
+
+struct GroupView {
+  const uint8_t* rec;
+  int fmt, inter, rows, row0;
+  bool shared;
+};
+
+__device__ __forceinline__ GroupView group_view(const GroupArgs& a, int g) {
+  GroupView v;
+  v.shared = (g == a.E);
+  v.rec = v.shared ? a.shared_record : reinterpret_cast<const uint8_t*>(a.expert_records[g]);
+  v.fmt = v.shared ? ER_FMT_INT8 : a.fmt;
+  v.inter = v.shared ? a.Is : a.I;
+  v.rows = a.plan->counts[g];
+  v.row0 = v.shared ? 0 : a.plan->offsets[g];
+  return v;
+}
+
+// Locate work item `item` of schedule `s`: returns the group id and the
+// item's index inside the group, or -1 past the end.
+__device__ __forceinline__ int find_item(const Plan* P, int s, int item, int* local) {
+  const int na = P->num_active;
+  if (item >= P->item_start[s][na]) return -1;
+  int lo = 0, hi = na - 1;  // largest a with item_start[a] <= item
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (P->item_start[s][mid] <= item)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  *local = item - P->item_start[s][lo];
+  return P->active[lo];
+}
+
+// launchers (each returns an ER_* status)
+int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
+                         float* logits, float* gate_logit, cudaStream_t st);
+int launch_router_topk(const float* logits, int n, int E, int k, int norm, int64_t* idx64, int32_t* idx32,
+                       float* wout, const float* gate_logit, float* gate_sig, cudaStream_t st);
+int launch_plan(const int32_t* idx, const float* w, int n, int k, int E, int H, int I, int Is,
+                const SchedSpec* specs, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of,
+                cudaStream_t st);
+// Upper bound of the items a schedule can produce (host side, for grid sizing).
+long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int I, int Is);
+
+int launch_gemv_grouped(const GroupArgs& a, int sched, int mode, const void* x, int x_dtype, float* act_r,
+                        float* act_s, float* out_r, float* out_s, long long items_bound, cudaStream_t st);
+int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void* x, int x_dtype,
+                             float* act_r, float* act_s, float* out_r, float* out_s,
+                             long long items_bound, cudaStream_t st);
+int launch_combine_plan(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k,
+                        int H, const Plan* plan, float* out, cudaStream_t st);
+
+// GEMV schedule geometry (er_gemv.cu): units per item
+constexpr int kGemvWarps = 8;
+constexpr int kGemvRowsPerWarp = 8;          // weight rows per warp
+constexpr int kGemvUnitsGU = kGemvWarps * kGemvRowsPerWarp / 2;  // 32 intermediate columns (gate+up rows)
+constexpr int kGemvUnitsDN = kGemvWarps * kGemvRowsPerWarp;      // 64 output rows
+constexpr int kGemvMaxTok = 8;               // tokens per pass
+// SIMT GEMM tile (er_gemm_simt.cu)
+constexpr int kSimtBM = 64;
+constexpr int kSimtBN = 64;
+
+}  // namespace er

@@ -1,0 +1,206 @@
+// er_moe.cu -- er_moe_block: the whole MoE block (runtime/qwen_moe.py:293-359)
+// as a fixed sequence of device launches with no host synchronisation, so
+// the call can be captured in a CUDA graph:
+//   K1 router logits (+ shared-gate logit) -> K1 softmax/top-k
+//   K2 plan: expert-sorted (token, slot) list and work-item schedules
+//   K3 gate/up + SwiGLU, K3 down (grouped GEMV for decode, GEMM otherwise)
+//   K4 combine in ascending expert order + gated shared expert
+#include "er_internal.cuh"
+
+namespace er {
+
+struct WsLayout {
+  size_t logits, gate_logit, gate_sig, idx32, topw, plan, perm_token, perm_w, pos_of, act_r, act_s, y_r, y_s, total;
+};
+
+static WsLayout ws_layout(const er_moe_weights* w, int n) {
+  WsLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  const size_t nk = (size_t)n * w->top_k;
+  L.logits = take((size_t)n * w->num_experts * 4);
+  L.gate_logit = take((size_t)n * 4);
+  L.gate_sig = take((size_t)n * 4);
+  L.idx32 = take(nk * 4);
+  L.topw = take(nk * 4);
+  L.plan = take(sizeof(Plan));
+  L.perm_token = take(nk * 4);
+  L.perm_w = take(nk * 4);
+  L.pos_of = take(nk * 4);
+  L.act_r = take(nk * w->inter * 4);
+  L.act_s = take((size_t)n * w->shared_inter * 4);
+  L.y_r = take(nk * w->hidden * 4);
+  L.y_s = take((size_t)n * w->hidden * 4);
+  L.total = off;
+  return L;
+}
+
+static int validate(const er_moe_weights* w) {
+  if (!w) return fail(ER_EINVAL, "er_moe: null weights");
+  if (w->hidden <= 0 || w->hidden % 16)
+    return fail(ER_EINVAL, "er_moe: hidden %d must be a positive multiple of 16", w->hidden);
+  if (w->inter <= 0 || w->inter % 16 || w->shared_inter <= 0 || w->shared_inter % 16)
+    return fail(ER_EINVAL, "er_moe: inter %d / shared_inter %d must be positive multiples of 16", w->inter,
+                w->shared_inter);
+  if (w->num_experts < 1 || w->num_experts > kMaxExperts)
+    return fail(ER_EINVAL, "er_moe: num_experts %d outside 1..%d", w->num_experts, kMaxExperts);
+  if (w->top_k < 1 || w->top_k > kMaxTopK || w->top_k > w->num_experts)
+    return fail(ER_EINVAL, "er_moe: top_k %d outside 1..min(%d, num_experts)", w->top_k, kMaxTopK);
+  if (w->expert_fmt != ER_FMT_INT8 && w->expert_fmt != ER_FMT_INT4 && w->expert_fmt != ER_FMT_INT4_ZP)
+    return fail(ER_EINVAL, "er_moe: unknown expert format %d", w->expert_fmt);
+  if (w->expert_fmt != ER_FMT_INT8) {
+    if (w->group <= 0 || w->group % 16 || w->hidden % w->group || w->inter % w->group)
+      return fail(ER_EINVAL, "er_moe: int4 group %d must be a multiple of 16 dividing hidden %d and inter %d",
+                  w->group, w->hidden, w->inter);
+  }
+  if (!w->router_w || !w->shared_gate_w || !w->expert_records || !w->shared_record)
+    return fail(ER_EINVAL, "er_moe: null weight pointer");
+  if (((uintptr_t)w->router_w | (uintptr_t)w->shared_gate_w) & 15)
+    return fail(ER_EINVAL, "er_moe: router / shared-gate weights must be 16-byte aligned");
+  if ((uintptr_t)w->shared_record & 255) return fail(ER_EINVAL, "er_moe: shared record must be 256-byte aligned");
+  return ER_OK;
+}
+
+static int pick_path(int path, int n) {
+  if (path != ER_PATH_AUTO) return path;
+  return n <= kGemvMaxTok ? ER_PATH_GEMV : ER_PATH_GEMM;
+}
+
+}  // namespace er
+
+using namespace er;
+
+extern "C" size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path) {
+  (void)path;
+  if (validate(w) != ER_OK || n < 0) return 0;
+  return ws_layout(w, n).total;
+}
+
+extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (int rc = validate(w)) return rc;
+  if (!io) return fail(ER_EINVAL, "er_moe_block: null io");
+  const int n = io->n;
+  if (n < 0) return fail(ER_EINVAL, "er_moe_block: negative n");
+  if (n == 0) return ER_OK;
+  if (!io->h || !io->y) return fail(ER_EINVAL, "er_moe_block: null h or y");
+  if (io->h_dtype != ER_DTYPE_F32 && io->h_dtype != ER_DTYPE_BF16)
+    return fail(ER_EINVAL, "er_moe_block: unknown activation dtype %d", io->h_dtype);
+  if (((uintptr_t)io->h | (uintptr_t)io->y) & 15) return fail(ER_EINVAL, "er_moe_block: h and y must be 16-byte aligned");
+  const int path = pick_path(io->path, n);
+  if (path != ER_PATH_GEMV && path != ER_PATH_GEMM)
+    return fail(ER_EINVAL, "er_moe_block: path %d is not available in this build", io->path);
+  const WsLayout L = ws_layout(w, n);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(ER_ENOSPACE, "er_moe_block: workspace %zu bytes, need %zu", workspace_bytes, L.total);
+  if ((uintptr_t)workspace & 255) return fail(ER_EINVAL, "er_moe_block: workspace must be 256-byte aligned");
+
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = static_cast<char*>(workspace);
+  int launches = 0;
+  auto mark = [&](int i) -> int {
+    if (!io->stage_events) return ER_OK;
+    return cuda_check(cudaEventRecord((cudaEvent_t)io->stage_events[i], st), "cudaEventRecord");
+  };
+  if (int rc = mark(0)) return rc;
+  const int H = w->hidden, E = w->num_experts, k = w->top_k;
+  float* logits = io->logits_out ? io->logits_out : reinterpret_cast<float*>(ws + L.logits);
+  float* gate_logit = reinterpret_cast<float*>(ws + L.gate_logit);
+  float* gate_sig = reinterpret_cast<float*>(ws + L.gate_sig);
+  int32_t* idx32 = reinterpret_cast<int32_t*>(ws + L.idx32);
+  float* topw = reinterpret_cast<float*>(ws + L.topw);
+  Plan* plan = reinterpret_cast<Plan*>(ws + L.plan);
+  int32_t* perm_token = reinterpret_cast<int32_t*>(ws + L.perm_token);
+  float* perm_w = reinterpret_cast<float*>(ws + L.perm_w);
+  int32_t* pos_of = reinterpret_cast<int32_t*>(ws + L.pos_of);
+  float* act_r = reinterpret_cast<float*>(ws + L.act_r);
+  float* act_s = reinterpret_cast<float*>(ws + L.act_s);
+  float* y_r = reinterpret_cast<float*>(ws + L.y_r);
+  float* y_s = reinterpret_cast<float*>(ws + L.y_s);
+
+  // K1: router (or only the shared-gate row when the caller supplies logits)
+  const float* lg = logits;
+  if (io->logits_in) {
+    if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit, st))
+      return rc;
+    lg = io->logits_in;
+    if (io->logits_out && io->logits_out != io->logits_in) {
+      if (int rc = cuda_check(cudaMemcpyAsync(io->logits_out, io->logits_in, (size_t)n * E * 4,
+                                              cudaMemcpyDeviceToDevice, st),
+                              "copy logits"))
+        return rc;
+    }
+  } else {
+    if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, w->router_w, w->shared_gate_w, E, logits, gate_logit,
+                                      st))
+      return rc;
+  }
+  if (int rc = launch_router_topk(lg, n, E, k, w->norm_topk_prob, io->topk_idx_out, idx32, topw, gate_logit, gate_sig,
+                                  st))
+    return rc;
+  launches += 2;
+  if (io->topk_w_out) {
+    if (int rc = cuda_check(cudaMemcpyAsync(io->topk_w_out, topw, (size_t)n * k * 4, cudaMemcpyDeviceToDevice, st),
+                            "copy top-k weights"))
+      return rc;
+  }
+
+  // K2: plan
+  SchedSpec specs[kNumSched];
+  if (path == ER_PATH_GEMV) {
+    specs[0] = SchedSpec{0, kGemvUnitsGU, 0};
+    specs[1] = SchedSpec{0, kGemvUnitsDN, 1};
+  } else {
+    specs[0] = SchedSpec{kSimtBM, kSimtBN, 0};
+    specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
+  }
+  if (int rc = mark(1)) return rc;
+  if (int rc = launch_plan(idx32, topw, n, k, E, H, w->inter, w->shared_inter, specs, plan, perm_token, perm_w, pos_of,
+                           st))
+    return rc;
+  launches += 1;
+  if (int rc = mark(2)) return rc;
+
+  GroupArgs ga;
+  ga.plan = plan;
+  ga.expert_records = w->expert_records;
+  ga.shared_record = static_cast<const uint8_t*>(w->shared_record);
+  ga.fmt = w->expert_fmt;
+  ga.H = H;
+  ga.I = w->inter;
+  ga.Is = w->shared_inter;
+  ga.group = w->expert_fmt == ER_FMT_INT8 ? 1 : w->group;
+  ga.E = E;
+  ga.n = n;
+  ga.perm_token = perm_token;
+  ga.perm_w = perm_w;
+  ga.gate_sig = gate_sig;
+
+  const long long b0 = sched_items_bound(specs[0], n, k, E, H, w->inter, w->shared_inter);
+  const long long b1 = sched_items_bound(specs[1], n, k, E, H, w->inter, w->shared_inter);
+  // one int8 instance (the shared expert and int8 routed experts), plus one
+  // instance of the routed format when it is int4
+  const int per_stage = w->expert_fmt == ER_FMT_INT8 ? 1 : 2;
+  if (path == ER_PATH_GEMV) {
+    if (int rc = launch_gemv_grouped(ga, 0, 0, io->h, io->h_dtype, act_r, act_s, nullptr, nullptr, b0, st)) return rc;
+    if (int rc = mark(3)) return rc;
+    if (int rc = launch_gemv_grouped(ga, 1, 1, nullptr, ER_DTYPE_F32, act_r, act_s, y_r, y_s, b1, st)) return rc;
+  } else {
+    if (int rc = launch_gemm_simt_grouped(ga, 0, 0, io->h, io->h_dtype, act_r, act_s, nullptr, nullptr, b0, st))
+      return rc;
+    if (int rc = mark(3)) return rc;
+    if (int rc = launch_gemm_simt_grouped(ga, 1, 1, nullptr, ER_DTYPE_F32, act_r, act_s, y_r, y_s, b1, st))
+      return rc;
+  }
+  launches += 2 * per_stage;
+  if (int rc = mark(4)) return rc;
+  // K4
+  if (int rc = launch_combine_plan(y_r, y_s, pos_of, idx32, n, k, H, plan, io->y, st)) return rc;
+  launches += 1;
+  if (io->launch_count) *io->launch_count += launches;
+  return mark(5);
+}

@@ -1,0 +1,199 @@
+"""MoeBlock: one MoE layer resident in HBM, run by er_moe_block.
+
+Drop-in for `QwenMoe._moe` (runtime/qwen_moe.py:293-359): given the
+post-attention RMSNorm output h [n, 2048] it returns
+routed + sigmoid(h @ w_g^T) * shared, with the router, top-4 selection,
+expert dispatch and combine all on the GPU. Expert weights are store records
+in HBM; the device pointer table `expert_table` says where each expert's
+record is, so an HBM expert cache can remap experts between calls without
+copying.
+
+PyTorch provides device memory and the current stream; the arithmetic is
+the CUDA library's.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import MoeIO, MoeWeights
+from .store import FMT_INT8, RecordLayout
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+
+
+class MoeBlock:
+    """One layer's MoE block on a CUDA device.
+
+    router      [E, H] float32 (mlp.gate.weight)
+    shared_gate [1, H] or [H] float32 (mlp.shared_expert_gate.weight)
+    shared      {"gate_proj", "up_proj", "down_proj"} -> (int8 q, float32 scales)
+    records     [E, record_size] uint8 routed-expert records (layout `layout`),
+                host or device; or None when an expert table is set later
+    """
+
+    def __init__(
+        self,
+        *,
+        router: np.ndarray,
+        shared_gate: np.ndarray,
+        shared: dict,
+        layout: RecordLayout,
+        shared_inter: int,
+        records: np.ndarray | torch.Tensor | None = None,
+        top_k: int = 4,
+        norm_topk_prob: bool = False,
+        device: str | torch.device = "cuda",
+    ):
+        if not torch.cuda.is_available():
+            raise RuntimeError("MoeBlock needs a CUDA device (the B200 path has no CPU fallback)")
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.layout = layout
+        self.num_experts, self.hidden = int(router.shape[0]), int(router.shape[1])
+        self.inter, self.shared_inter, self.top_k = layout.inter, int(shared_inter), int(top_k)
+        dev = self.device
+        self.router = torch.as_tensor(np.ascontiguousarray(router, dtype=np.float32)).to(dev)
+        self.shared_gate = torch.as_tensor(np.ascontiguousarray(shared_gate, dtype=np.float32).reshape(-1)).to(dev)
+        from .store import serialize_record
+
+        sh_layout = RecordLayout(FMT_INT8, self.hidden, self.shared_inter)
+        self.shared_record = torch.as_tensor(serialize_record(sh_layout, shared)).to(dev)
+        self.records: torch.Tensor | None = None
+        self.expert_table = torch.zeros(self.num_experts, dtype=torch.int64, device=dev)
+        if records is not None:
+            self.set_records(records)
+        self._w = MoeWeights(
+            hidden=self.hidden,
+            num_experts=self.num_experts,
+            top_k=self.top_k,
+            inter=self.inter,
+            shared_inter=self.shared_inter,
+            expert_fmt=layout.fmt,
+            group=layout.group,
+            norm_topk_prob=int(norm_topk_prob),
+            router_w=self.router.data_ptr(),
+            shared_gate_w=self.shared_gate.data_ptr(),
+            expert_records=self.expert_table.data_ptr(),
+            shared_record=self.shared_record.data_ptr(),
+        )
+        self._ws: torch.Tensor | None = None
+
+    @classmethod
+    def from_host_block(cls, block, device: str | torch.device = "cuda") -> MoeBlock:
+        """From an expertrelay_b200.synth.HostBlock."""
+        return cls(
+            router=block.router,
+            shared_gate=block.shared_gate,
+            shared=block.shared,
+            layout=block.layout,
+            shared_inter=block.shared_inter,
+            records=block.records(),
+            top_k=block.top_k,
+            device=device,
+        )
+
+    def set_records(self, records: np.ndarray | torch.Tensor) -> None:
+        """Upload (or adopt) all E records back to back and point the table at them."""
+        rs = self.layout.record_size
+        t = torch.as_tensor(records)
+        if t.dtype != torch.uint8 or t.numel() != self.num_experts * rs:
+            raise ValueError(f"records: expected {self.num_experts} x {rs} uint8, got {tuple(t.shape)} {t.dtype}")
+        self.records = t.reshape(self.num_experts, rs).to(self.device).contiguous()
+        base = self.records.data_ptr()
+        self.set_expert_table(torch.arange(self.num_experts, dtype=torch.int64, device=self.device) * rs + base)
+
+    def set_expert_table(self, addresses: torch.Tensor) -> None:
+        """Device addresses of each expert's record (e.g. HBM cache slots)."""
+        if addresses.numel() != self.num_experts:
+            raise ValueError("one address per expert")
+        self.expert_table.copy_(addresses.to(self.device, torch.int64), non_blocking=True)
+
+    def workspace_bytes(self, n: int, path: int = _lib.PATH_AUTO) -> int:
+        return int(_lib.lib().er_moe_workspace_bytes(C.byref(self._w), int(n), int(path)))
+
+    def _workspace(self, n: int, path: int) -> torch.Tensor:
+        need = self.workspace_bytes(n, path)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward(
+        self,
+        h: torch.Tensor,
+        *,
+        logits: torch.Tensor | None = None,
+        out: torch.Tensor | None = None,
+        path: int = _lib.PATH_AUTO,
+        return_routing: bool = False,
+        stage_events: list | None = None,
+        launch_counter: C.c_int | None = None,
+    ):
+        """h [n, H] float32 or bfloat16 CUDA tensor -> y [n, H] float32. With
+        `logits` ([n, E] float32) the routing uses those router logits. With
+        return_routing, also returns (logits [n, E], top-k ids [n, k] int64,
+        top-k weights [n, k] float32). `stage_events` (len(MOE_STAGES) + 1
+        timing-enabled torch.cuda.Event, already recorded once) are recorded
+        around each stage; `launch_counter` accumulates the kernel launches."""
+        _require_cuda(h, "h")
+        if h.dim() != 2 or h.shape[1] != self.hidden:
+            raise ValueError(f"h: expected [n, {self.hidden}], got {tuple(h.shape)}")
+        if h.dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"h: float32 or bfloat16, got {h.dtype}")
+        h = h.contiguous()
+        n = h.shape[0]
+        y = out if out is not None else torch.empty((n, self.hidden), dtype=torch.float32, device=self.device)
+        lg_out = idx_out = w_out = None
+        if return_routing:
+            lg_out = torch.empty((n, self.num_experts), dtype=torch.float32, device=self.device)
+            idx_out = torch.empty((n, self.top_k), dtype=torch.int64, device=self.device)
+            w_out = torch.empty((n, self.top_k), dtype=torch.float32, device=self.device)
+        if logits is not None:
+            _require_cuda(logits, "logits")
+            logits = logits.to(torch.float32).contiguous()
+            if tuple(logits.shape) != (n, self.num_experts):
+                raise ValueError(f"logits: expected [{n}, {self.num_experts}], got {tuple(logits.shape)}")
+        ws = self._workspace(n, path)
+        io = MoeIO(
+            h=h.data_ptr(),
+            h_dtype=_lib.DTYPE_BF16 if h.dtype == torch.bfloat16 else _lib.DTYPE_F32,
+            n=n,
+            logits_in=_ptr(logits),
+            y=y.data_ptr(),
+            logits_out=_ptr(lg_out),
+            topk_idx_out=_ptr(idx_out),
+            topk_w_out=_ptr(w_out),
+            path=int(path),
+        )
+        if stage_events is not None:
+            if len(stage_events) != len(_lib.MOE_STAGES) + 1:
+                raise ValueError(f"stage_events: need {len(_lib.MOE_STAGES) + 1} events")
+            handles = (C.c_void_p * len(stage_events))(*[ev.cuda_event for ev in stage_events])
+            io.stage_events = C.cast(handles, C.POINTER(C.c_void_p))
+        if launch_counter is not None:
+            io.launch_count = C.pointer(launch_counter)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = _lib.lib().er_moe_block(C.byref(self._w), C.byref(io), ws.data_ptr(), ws.numel(), stream)
+        _lib.check(rc, "er_moe_block")
+        if return_routing:
+            return y, lg_out, idx_out, w_out
+        return y
+
+    __call__ = forward
+
+    def moe_numpy(self, h: np.ndarray) -> np.ndarray:
+        """The reference's calling convention: numpy float32 in, new numpy float32 out."""
+        hd = torch.from_numpy(np.ascontiguousarray(h, dtype=np.float32)).to(self.device, non_blocking=False)
+        return self.forward(hd).cpu().numpy()

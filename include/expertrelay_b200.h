@@ -1,0 +1,148 @@
+/*
+ * expertrelay_b200.h -- C ABI of libexpertrelay_b200.so, the sm_100a (B200)
+ * implementation of ExpertRelay's MoE-block hot path.
+ *
+ * Every entry point takes plain pointers and sizes (device pointers unless
+ * stated), an optional CUDA stream (NULL = legacy default stream), returns
+ * an int status (ER_OK = 0) and never allocates device memory: callers pass
+ * any scratch space as a workspace pointer, sized by the matching *_bytes()
+ * query. On failure er_last_error() returns a message for the calling
+ * thread. Launches are asynchronous on `stream`; a kernel fault surfaces as
+ * ER_ECUDA on a later call or synchronisation.
+ *
+ * Reference interfaces replaced (paths inside the ExpertRelay project):
+ *   er_linear_f32      runtime/backends.py:57-59, 86-88   Backend.linear
+ *   er_int8_linear     runtime/backends.py:47-51, 78-81   Backend.int8_linear
+ *                      runtime/int8_linear.py:106-138     int8_linear()
+ *   er_int4_linear     runtime/backends.py:53-55, 83-84   Backend.int4_linear
+ *                      runtime/int4_linear.py:88-122      int4_linear()
+ *   er_attention       runtime/backends.py:61-67, 90-95   Backend.attention
+ *   er_router_topk     runtime/qwen_moe.py:303-308        router softmax + top-k
+ *   er_dequant_int8    store/quantize.py:45-46            dequantize_rowwise_int8
+ *   er_dequant_int4    store/int4.py:142-144              dequantize_groupwise_int4
+ *   er_moe_block       runtime/qwen_moe.py:293-359        QwenMoe._moe
+ *   er_record_*        store/layout.py:53-115, store/int4.py:165-244
+ *                                                         expert record layouts
+ */
+#ifndef EXPERTRELAY_B200_H
+#define EXPERTRELAY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ER_API __attribute__((visibility("default")))
+#else
+#define ER_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define ER_OK 0
+#define ER_EINVAL 1    /* bad argument: shape, alignment, null pointer, size */
+#define ER_ECUDA 2     /* a CUDA runtime call or launch failed */
+#define ER_ETIMEOUT 3  /* a bounded device-side wait gave up */
+#define ER_ENOSPACE 4  /* workspace (or fixed scratch) too small */
+
+/* ---- activation dtypes ------------------------------------------------- */
+#define ER_DTYPE_F32 0
+#define ER_DTYPE_BF16 1
+
+/* ---- routed-expert record formats (store/layout.py, store/int4.py) ----- */
+#define ER_FMT_INT8 0      /* [gate q][up q][down q][gate s f32][up s][down s][pad] */
+#define ER_FMT_INT4 1      /* [gate p][up p][down p][gate s f16][up s][down s][pad], value = nibble - 8 */
+#define ER_FMT_INT4_ZP 2   /* ER_FMT_INT4 + [gate z u8][up z][down z] after the scales, value = nibble - z */
+
+/* ---- expert-matrix execution paths ------------------------------------- */
+#define ER_PATH_AUTO 0     /* stream weights (GEMV) for small n, tiled GEMM otherwise */
+#define ER_PATH_GEMV 1     /* weight-streaming grouped GEMV, any n (slow for large n) */
+#define ER_PATH_GEMM 2     /* tiled grouped GEMM, fp32 FMA (exact-fp32 path) */
+#define ER_PATH_TC 3       /* tcgen05 tensor-core grouped GEMM (bf16 operands) */
+
+/* library identity / diagnostics */
+ER_API int er_version(void);                 /* e.g. 100 = 0.1.0 */
+ER_API const char* er_last_error(void);      /* message of the last failure on this thread */
+ER_API int er_device_sm_count(int* sms);     /* SMs of the current device */
+
+/* ---- record layout queries (store/layout.py:74-100, store/int4.py:194-220) ---- */
+/* byte size of one padded expert record (a multiple of 4096) */
+ER_API size_t er_record_bytes(int fmt, int hidden, int inter, int group);
+/* byte offset inside a record of matrix `which` (0 gate, 1 up, 2 down);
+ * part 0 = weights, 1 = scales, 2 = zero points (ER_FMT_INT4_ZP only) */
+ER_API size_t er_record_offset(int fmt, int hidden, int inter, int group, int which, int part);
+
+/* ---- Backend protocol ops (runtime/backends.py:44-67) ----------------------
+ * x [m, in] with row stride ldx elements (>= in), y [m, out] contiguous.
+ * bias may be NULL. All fp32 unless stated. */
+ER_API int er_linear_f32(const float* x, long long ldx, const float* w, const float* bias, float* y,
+                  int m, int out, int in, void* stream);
+ER_API int er_int8_linear(const float* x, long long ldx, const int8_t* q, const float* scales,
+                   const float* bias, float* y, int m, int out, int in, void* stream);
+/* packed uint8 [out, in/2] (even input column in the low nibble), scales f16 bits
+ * [out, in/group]; zeros (uint8 [out, in/group], 0..16) or NULL for the fixed 8 */
+ER_API int er_int4_linear(const float* x, long long ldx, const uint8_t* packed, const uint16_t* scales_f16,
+                   const uint8_t* zeros, int group, const float* bias, float* y, int m, int out,
+                   int in, void* stream);
+/* q [n, heads, d], keys/values [kv, heads, d], allowed [n, kv] (uint8 0/1) -> out [n, heads, d];
+ * scores scaled by d^-0.5, softmax in fp32 */
+ER_API int er_attention(const float* q, const float* keys, const float* values, const uint8_t* allowed,
+                 float* out, int n, int kv, int heads, int d, void* stream);
+
+/* ---- weight reconstruction (bit-exact fp32) ---------------------------- */
+ER_API int er_dequant_int8(const int8_t* q, const float* scales, float* w, int rows, int cols, void* stream);
+ER_API int er_dequant_int4(const uint8_t* packed, const uint16_t* scales_f16, const uint8_t* zeros, int group,
+                    float* w, int rows, int cols, void* stream);
+
+/* ---- router (runtime/qwen_moe.py:303-308) ----------------------------------
+ * logits [n, E] fp32 -> top-k expert ids (largest first, exact ties to the lower id)
+ * and their softmax probabilities (no renormalisation). idx64 or idx32 may be NULL. */
+ER_API int er_router_topk(const float* logits, int n, int num_experts, int k, int64_t* idx64, int32_t* idx32,
+                   float* probs_out, void* stream);
+
+/* ---- the MoE block (runtime/qwen_moe.py:293-359) ------------------------- */
+typedef struct er_moe_weights {
+  int hidden;                  /* H (2048) */
+  int num_experts;             /* E (60), <= 256 */
+  int top_k;                   /* k (4), <= 8 */
+  int inter;                   /* routed intermediate size I (1408) */
+  int shared_inter;            /* shared-expert intermediate size (5632) */
+  int expert_fmt;              /* ER_FMT_* of the routed-expert records */
+  int group;                   /* int4 group size along the input dim (128), ignored for int8 */
+  int norm_topk_prob;          /* 0 for Qwen1.5-MoE (weights are not renormalised) */
+  const float* router_w;       /* [E, H] fp32 (mlp.gate.weight) */
+  const float* shared_gate_w;  /* [H] fp32 (mlp.shared_expert_gate.weight) */
+  const uint64_t* expert_records; /* DEVICE array [E] of record base addresses (4096-aligned) */
+  const void* shared_record;   /* the shared expert as an ER_FMT_INT8 record with inter = shared_inter */
+} er_moe_weights;
+
+typedef struct er_moe_io {
+  const void* h;               /* [n, H] activations, dtype h_dtype */
+  int h_dtype;                 /* ER_DTYPE_F32 / ER_DTYPE_BF16 */
+  int n;                       /* tokens */
+  const float* logits_in;      /* optional [n, E]: use these router logits instead of h @ Wr^T */
+  float* y;                    /* [n, H] fp32 output */
+  float* logits_out;           /* optional [n, E] */
+  int64_t* topk_idx_out;       /* optional [n, k] */
+  float* topk_w_out;           /* optional [n, k] */
+  int path;                    /* ER_PATH_* */
+  /* optional instrumentation (NULL to skip): ER_MOE_STAGES + 1 cudaEvent_t handles,
+   * recorded on the stream before the router and after each stage (router, plan,
+   * gate/up, down, combine), so stage i took elapsed(events[i], events[i + 1]) */
+  void* const* stage_events;
+  int* launch_count;           /* optional: incremented by the number of kernels launched */
+} er_moe_io;
+
+#define ER_MOE_STAGES 5        /* router, plan, gate/up, down, combine */
+
+ER_API size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path);
+ER_API int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXPERTRELAY_B200_H */

@@ -1,0 +1,288 @@
+"""Generate the golden fixtures in tests/golden/ by running the reference.
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+Imports ExpertRelay from <reference>/src (read only: no bytecode is written
+and numba's cache goes to a temporary directory) and records its outputs on
+seeded inputs: the quantizers and packers, the GPTQ conversion and formula,
+the int8/int4 linear kernels (blocked and numba-fused), the record layouts,
+and QwenMoe._moe on a small block and on full Qwen1.5-MoE-A2.7B-shaped
+blocks built by expertrelay_b200.synth. Needs the reference, so it runs
+where the reference is mounted; the fixtures it writes are committed and
+are all the tests need.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+
+
+def _import_reference(ref: Path):
+    sys.dont_write_bytecode = True
+    os.environ.setdefault("NUMBA_CACHE_DIR", tempfile.mkdtemp(prefix="numba-ref-"))
+    sys.path.insert(0, str(ref / "src"))
+    sys.path.insert(0, str(ROOT))
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def quantizer_fixtures() -> dict:
+    from expertrelay.store.int4 import pack_int4, quantize_groupwise_int4, quantize_groupwise_int4_gptq_grid
+    from expertrelay.store.quantize import quantize_rowwise_int8
+
+    out = {}
+    rng = np.random.default_rng(0)
+    w = rng.normal(0, 0.02, (64, 128)).astype(np.float32)
+    w[3] *= 50
+    w[7] = 0  # all-zero row
+    out["i8_w"] = w
+    out["i8_q"], out["i8_s"] = quantize_rowwise_int8(w)
+
+    w4 = (np.random.default_rng(1).standard_t(3, (64, 256)) * 0.02).astype(np.float32)
+    w4[5, :32] = 0  # all-zero group
+    out["i4_w"] = w4
+    out["i4_q"], out["i4_s"] = quantize_groupwise_int4(w4, 32)
+    bump = np.zeros((1, 8), dtype=np.float32)
+    bump[0, 0] = 0.100006  # float16 rounding would shrink this group's scale
+    out["i4_bump_w"] = bump
+    out["i4_bump_q"], out["i4_bump_s"] = quantize_groupwise_int4(bump, 8)
+
+    wg = (np.random.default_rng(2).standard_t(3, (6, 64)) * 0.02).astype(np.float32)
+    wg[1, :16] = np.abs(wg[1, :16])
+    wg[2, 16:32] = 0
+    out["gg_w"] = wg
+    out["gg_q"], out["gg_s"] = quantize_groupwise_int4_gptq_grid(wg, 16)
+
+    pq = np.random.default_rng(3).integers(-8, 8, (5, 12)).astype(np.int8)
+    out["pack_q"] = pq
+    out["pack_p"] = pack_int4(pq)
+    return out
+
+
+def _pack_gptq_int32(codes: np.ndarray, axis: int) -> np.ndarray:
+    # element-by-element packer, independent of both implementations under test
+    codes = np.moveaxis(codes, axis, 0)
+    out = np.zeros((codes.shape[0] // 8, *codes.shape[1:]), dtype=np.uint32)
+    for i in range(codes.shape[0]):
+        out[i // 8] |= codes[i].astype(np.uint32) << np.uint32(4 * (i % 8))
+    return np.moveaxis(out, 0, axis).view(np.int32)
+
+
+def _gptq_layer(out_dim, in_dim, group, seed, zero=8):
+    rng = np.random.default_rng(seed)
+    codes = rng.integers(0, 16, (in_dim, out_dim))
+    codes[0, 0], codes[1, 0] = 0, 15
+    return {
+        "qweight": _pack_gptq_int32(codes, axis=0),
+        "qzeros": _pack_gptq_int32(np.full((in_dim // group, out_dim), zero - 1), axis=1),
+        "scales": rng.uniform(0.001, 0.05, (in_dim // group, out_dim)).astype(np.float16),
+        "g_idx": (np.arange(in_dim) // group).astype(np.int32),
+        "bias": np.zeros(out_dim, dtype=np.float16),
+    }
+
+
+def gptq_fixtures() -> dict:
+    from expertrelay.bench.gptq_conversion_check import reference_dequantize
+    from expertrelay.store.gptq import gptq_to_int4
+
+    out = {}
+    t = _gptq_layer(48, 64, 16, seed=0)
+    for k, v in t.items():
+        out[f"sym_{k}"] = v
+    out["sym_store_packed"], out["sym_store_scales"] = gptq_to_int4(*t.values(), group=16)
+    out["sym_ref_w"] = reference_dequantize(t["qweight"], t["qzeros"], t["scales"], t["g_idx"])
+    a = _gptq_layer(8, 16, 8, seed=1, zero=3)
+    a["g_idx"] = a["g_idx"][::-1].copy()
+    for k, v in a.items():
+        out[f"asym_{k}"] = v
+    out["asym_ref_w"] = reference_dequantize(a["qweight"], a["qzeros"], a["scales"], a["g_idx"])
+    b = _gptq_layer(304, 128, 32, seed=3)
+    for k, v in b.items():
+        out[f"k_{k}"] = v
+    out["k_ref_w"] = reference_dequantize(b["qweight"], b["qzeros"], b["scales"], b["g_idx"])
+    return out
+
+
+def linear_fixtures() -> dict:
+    from expertrelay.runtime.int4_linear import int4_linear
+    from expertrelay.runtime.int8_linear import int8_linear
+    from expertrelay.store.int4 import pack_int4, quantize_groupwise_int4
+    from expertrelay.store.quantize import quantize_rowwise_int8
+
+    out = {}
+    rng = np.random.default_rng(0)
+    q, s = quantize_rowwise_int8(rng.normal(0, 0.05, (300, 96)).astype(np.float32))
+    out["i8_q"], out["i8_s"] = q, s
+    out["i8_bias"] = rng.normal(0, 1, 300).astype(np.float32)
+    for n in (1, 3, 40):
+        x = rng.normal(0, 1, (n, 96)).astype(np.float32)
+        out[f"i8_x{n}"] = x
+        out[f"i8_y{n}_blocked"] = int8_linear(x, q, s, kernel="blocked")
+        out[f"i8_y{n}_fused"] = int8_linear(x, q, s, kernel="fused")
+        out[f"i8_y{n}_bias"] = int8_linear(x, q, s, out["i8_bias"], kernel="blocked")
+    rng = np.random.default_rng(3)
+    v, s4 = quantize_groupwise_int4(rng.normal(0, 0.05, (300, 128)).astype(np.float32), 32)
+    p = pack_int4(v)
+    out["i4_p"], out["i4_s"] = p, s4
+    for n in (1, 4, 20):
+        x = rng.normal(0, 1, (n, 128)).astype(np.float32)
+        out[f"i4_x{n}"] = x
+        out[f"i4_y{n}_blocked"] = int4_linear(x, p, s4, 32, kernel="blocked")
+        out[f"i4_y{n}_fused"] = int4_linear(x, p, s4, 32, kernel="fused")
+    return out
+
+
+def layout_fixtures(ref: Path) -> dict:
+    from expertrelay.store.int4 import Int4RecordLayout, pack_int4, quantize_groupwise_int4, serialize_int4_record
+    from expertrelay.store.layout import ExpertRecordLayout, serialize_expert_record
+    from expertrelay.store.quantize import quantize_rowwise_int8
+
+    cfg = {"moe_intermediate_size": 16, "hidden_size": 32}
+    rng = np.random.default_rng(4)
+    l8 = ExpertRecordLayout.from_config(cfg)
+    q8 = {
+        n: quantize_rowwise_int8(rng.normal(0, 0.1, s).astype(np.float32)) for n, s in l8.matrices
+    }
+    rec8 = np.frombuffer(bytes(serialize_expert_record(l8, q8)), dtype=np.uint8)
+    l4 = Int4RecordLayout.from_config(cfg, 8)
+    q4 = {}
+    for n, s in l4.matrices:
+        v, sc = quantize_groupwise_int4(rng.normal(0, 0.1, s).astype(np.float32), 8)
+        q4[n] = (pack_int4(v), sc)
+    rec4 = np.frombuffer(bytes(serialize_int4_record(l4, q4)), dtype=np.uint8)
+    out = {"rec8": rec8, "rec4": rec4}
+    for n, (qq, ss) in q8.items():
+        out[f"rec8_{n}_q"], out[f"rec8_{n}_s"] = qq, ss
+    for n, (pp, ss) in q4.items():
+        out[f"rec4_{n}_p"], out[f"rec4_{n}_s"] = pp, ss
+    manifests = {}
+    for d in sorted((ref / "benchmarks" / "stores").glob("*/store.json")):
+        manifests[d.parent.name] = json.loads(d.read_text())["expert_layout"]
+    return out, manifests
+
+
+def _run_moe(block, x, kernel="blocked"):
+    from expertrelay.runtime import int8_linear as i8mod
+    from expertrelay.runtime.qwen_moe import ForwardTrace, ModelConfig, QwenMoe, StepTimings
+    from expertrelay.runtime.weights import ExpertSource, Int4Matrix, Int8Matrix, ResidentWeights, SourceStats
+
+    class MemSource(ExpertSource):
+        def __init__(self, experts):
+            self._experts = experts
+            self.stats = SourceStats()
+
+        def load(self, layer, expert):
+            return self._experts[expert]
+
+    experts = []
+    for mats in block.experts:
+        d = {}
+        for name, t in mats.items():
+            if block.fmt == "int8":
+                d[name] = Int8Matrix(t[0], t[1])
+            elif block.fmt == "int4":
+                d[name] = Int4Matrix(t[0], t[1], t[0].shape[1] * 2 // t[1].shape[1])
+            else:
+                raise ValueError("the reference path has no zero-point int4 (store/gptq.py:67-69)")
+        experts.append(d)
+    p = "model.layers.0.mlp."
+    resident = ResidentWeights(
+        {
+            p + "gate.weight": block.router,
+            p + "shared_expert_gate.weight": block.shared_gate,
+            **{p + f"shared_expert.{m}.weight": Int8Matrix(*block.shared[m]) for m in block.shared},
+        },
+        0,
+    )
+    cfg = ModelConfig(151936, block.hidden, 1, 16, 16, block.num_experts, block.top_k, False, 1e-6, 1e6)
+    model = QwenMoe(cfg, resident, MemSource(experts))
+    before = i8mod.current_kernel()
+    i8mod.set_kernel(kernel)
+    try:
+        trace = ForwardTrace()
+        lg = model._linear(p + "gate.weight", x)
+        y = model._moe(0, x, StepTimings(), trace, None)
+    finally:
+        i8mod.set_kernel(before)
+    return y, lg, trace.selected_experts[0]
+
+
+def moe_fixtures() -> dict:
+    from expertrelay_b200 import synth
+
+    out = {}
+    # small block: every shape path of the kernels at a size the oracle runs in milliseconds
+    for fmt, group in (("int8", 0), ("int4", 16)):
+        blk = synth.make_block(11, hidden=64, inter=32, shared_inter=48, num_experts=8, top_k=4, fmt=fmt,
+                               group=group or 128, sigma=0.1)
+        x = synth.make_tokens(11, 5, 64)
+        y, lg, sel = _run_moe(blk, x)
+        tag = f"mini_{fmt}"
+        out[f"{tag}_x"], out[f"{tag}_y"], out[f"{tag}_logits"], out[f"{tag}_sel"] = x, y, lg, sel
+        out[f"{tag}_records"] = blk.records()
+        out[f"{tag}_shared_record"] = blk.shared_record()
+        out[f"{tag}_router"], out[f"{tag}_shared_gate"] = blk.router, blk.shared_gate
+    return out
+
+
+def full_fixtures() -> dict:
+    """Qwen-shaped blocks: outputs of the reference on the synth workloads.
+    The weights are regenerated from the seed; their digests pin them."""
+    from expertrelay_b200 import synth
+
+    out = {}
+    blk, x = synth.make_workload("decode8_int8", seed=0)
+    for kernel in ("blocked", "fused"):
+        y, lg, sel = _run_moe(blk, x, kernel=kernel)
+        out[f"decode8_y_{kernel}"] = y
+    out["decode8_x"], out["decode8_logits"], out["decode8_sel"] = x, lg, sel
+    out["decode8_records_sha"] = np.frombuffer(sha(blk.records()).encode(), dtype=np.uint8)
+    out["decode8_shared_sha"] = np.frombuffer(sha(blk.shared_record()).encode(), dtype=np.uint8)
+    out["decode8_router_sha"] = np.frombuffer(sha(blk.router).encode(), dtype=np.uint8)
+
+    blk, x = synth.make_workload("prefill4096_int8_zipf", seed=0)
+    y, lg, sel = _run_moe(blk, x)
+    out["prefill_sel"] = sel.astype(np.int8)
+    out["prefill_y_head"] = y[:32]
+    out["prefill_y_rownorm"] = np.linalg.norm(y.astype(np.float64), axis=1)
+    out["prefill_y_sum"] = np.array([y.astype(np.float64).sum()])
+    out["prefill_router_sha"] = np.frombuffer(sha(blk.router).encode(), dtype=np.uint8)
+    out["prefill_zipf_realised"] = np.array(blk.meta["zipf"]["realised"])
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--skip-full", action="store_true")
+    args = ap.parse_args()
+    ref = Path(args.reference)
+    _import_reference(ref)
+    np.savez_compressed(HERE / "quant.npz", **quantizer_fixtures())
+    np.savez_compressed(HERE / "gptq.npz", **gptq_fixtures())
+    np.savez_compressed(HERE / "linear.npz", **linear_fixtures())
+    lay, manifests = layout_fixtures(ref)
+    np.savez_compressed(HERE / "layout.npz", **lay)
+    (HERE / "store_manifests.json").write_text(json.dumps(manifests, indent=1, sort_keys=True))
+    np.savez_compressed(HERE / "moe_mini.npz", **moe_fixtures())
+    if not args.skip_full:
+        np.savez_compressed(HERE / "moe_qwen.npz", **full_fixtures())
+    for f in sorted(HERE.glob("*.npz")):
+        print(f"{f.name}: {f.stat().st_size / 1024:.1f} KiB")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,180 @@
+"""GPU: the whole MoE block (er_moe_block through MoeBlock) against the
+oracle and the reference's own outputs.
+
+Tolerances (relative L2 over the block output):
+  * fp32 activations: 1e-3 (the hot path's stated bound); the fp32-FMA
+    paths (GEMV, SIMT GEMM) are also held to 1e-4 to catch regressions;
+  * bf16 activations: 1e-2 against the fp32 oracle run on the same
+    bf16-rounded inputs.
+Top-k expert ids are compared exactly whenever both sides route from the
+same logits.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+from conftest import golden
+from helpers import gptq_oracle_weights, oracle_weights
+
+from expertrelay_b200 import _lib, synth
+from expertrelay_b200.moe import MoeBlock
+from expertrelay_b200.store import FMT_INT4, FMT_INT8, RecordLayout
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-3
+FP32_FMA_TOL = 1e-4
+BF16_TOL = 1e-2
+PATHS = {"gemv": _lib.PATH_GEMV, "gemm": _lib.PATH_GEMM}
+
+
+def _run(block: MoeBlock, x: np.ndarray, path: int, logits: np.ndarray | None = None, dtype=torch.float32):
+    dev = block.device
+    h = torch.from_numpy(x).to(dev).to(dtype)
+    lg = None if logits is None else torch.from_numpy(np.ascontiguousarray(logits, np.float32)).to(dev)
+    y, lo, idx, w = block.forward(h, logits=lg, path=path, return_routing=True)
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), lo.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy()
+
+
+def _mini_block(fmt: str, cuda) -> MoeBlock:
+    g = golden("moe_mini")
+    tag = f"mini_{fmt}"
+    lay = RecordLayout(FMT_INT8, 64, 32) if fmt == "int8" else RecordLayout(FMT_INT4, 64, 32, 16)
+    from expertrelay_b200.store import parse_record
+
+    sh = parse_record(RecordLayout(FMT_INT8, 64, 48), g[f"{tag}_shared_record"])
+    return MoeBlock(router=g[f"{tag}_router"], shared_gate=g[f"{tag}_shared_gate"], shared=sh, layout=lay,
+                    shared_inter=48, records=g[f"{tag}_records"], top_k=4, device=cuda)
+
+
+@pytest.mark.parametrize("path", list(PATHS))
+@pytest.mark.parametrize("fmt", ["int8", "int4"])
+def test_small_block_matches_reference(cuda, fmt, path):
+    g = golden("moe_mini")
+    blk = _mini_block(fmt, cuda)
+    x = g[f"mini_{fmt}_x"]
+    y, lg, idx, w = _run(blk, x, PATHS[path])
+    np.testing.assert_allclose(lg, g[f"mini_{fmt}_logits"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(idx, g[f"mini_{fmt}_sel"])
+    assert O.rel_l2(y, g[f"mini_{fmt}_y"]) < FP32_FMA_TOL
+
+
+@pytest.fixture(scope="module")
+def decode8(cuda):
+    blk, x = synth.make_workload("decode8_int8", seed=0)
+    g = golden("moe_qwen")
+    digest = hashlib.sha256(np.ascontiguousarray(blk.records()).tobytes()).hexdigest().encode()
+    assert digest == g["decode8_records_sha"].tobytes(), "synthetic weights differ from the fixture's"
+    return blk, x, MoeBlock.from_host_block(blk, device=cuda), g
+
+
+@pytest.mark.parametrize("path", list(PATHS))
+def test_decode8_matches_reference(decode8, path):
+    blk, x, dev, g = decode8
+    y, lg, idx, w = _run(dev, x, PATHS[path])
+    np.testing.assert_allclose(lg, g["decode8_logits"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_array_equal(idx, g["decode8_sel"])
+    assert O.rel_l2(y, g["decode8_y_blocked"]) < FP32_FMA_TOL
+    # routing pinned to the reference's logits: ids bit-exact, same output
+    y2, _, idx2, w2 = _run(dev, x, PATHS[path], logits=g["decode8_logits"])
+    np.testing.assert_array_equal(idx2, g["decode8_sel"])
+    np.testing.assert_allclose(w2, np.take_along_axis(O.softmax(g["decode8_logits"]), idx2, -1), rtol=1e-6)
+    assert O.rel_l2(y2, g["decode8_y_blocked"]) < FP32_FMA_TOL
+
+
+def test_decode8_bf16_activations(decode8):
+    blk, x, dev, g = decode8
+    xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    y, lg, idx, _ = _run(dev, x, _lib.PATH_GEMV, dtype=torch.bfloat16)
+    ref = O.moe_block(xb, oracle_weights(blk))
+    np.testing.assert_array_equal(idx, ref.selected)
+    assert O.rel_l2(y, ref.y) < BF16_TOL
+
+
+@pytest.mark.parametrize("n", [1, 3, 17])
+@pytest.mark.parametrize("path", list(PATHS))
+def test_decode_shapes_against_oracle(decode8, n, path):
+    blk, _, dev, _ = decode8
+    x = synth.make_tokens(100 + n, n)
+    ow = oracle_weights(blk)
+    y, lg, idx, _ = _run(dev, x, PATHS[path])
+    ref = O.moe_block(x, ow, logits=lg)  # same routing decision on both sides
+    np.testing.assert_array_equal(idx, ref.selected)
+    assert O.rel_l2(y, ref.y) < FP32_FMA_TOL
+
+
+def test_edge_routing_cases(decode8):
+    """Every token on the same experts (one group holds all rows, the rest
+    none), exact logit ties, and an empty batch."""
+    blk, _, dev, _ = decode8
+    n = 12
+    x = synth.make_tokens(5, n)
+    ow = oracle_weights(blk)
+    lg = np.full((n, 60), -3.0, dtype=np.float32)
+    lg[:, [59, 0, 31, 7]] = [4.0, 3.0, 2.0, 1.0]
+    for path in PATHS.values():
+        y, _, idx, _ = _run(dev, x, path, logits=lg)
+        assert (idx == [59, 0, 31, 7]).all()
+        assert O.rel_l2(y, O.moe_block(x, ow, logits=lg).y) < FP32_FMA_TOL
+    ties = np.zeros((n, 60), dtype=np.float32)
+    y, _, idx, w = _run(dev, x, _lib.PATH_GEMV, logits=ties)
+    assert (idx == [0, 1, 2, 3]).all()
+    ref = O.moe_block(x, ow, logits=ties, tie_rule="lower_index")
+    np.testing.assert_array_equal(idx, ref.selected)
+    assert O.rel_l2(y, ref.y) < FP32_FMA_TOL
+    empty = dev.forward(torch.empty((0, 2048), dtype=torch.float32, device=dev.device))
+    assert tuple(empty.shape) == (0, 2048)
+
+
+@pytest.fixture(scope="module")
+def gptq_block(cuda):
+    blk = synth.make_block(3, fmt="gptq_asym", group=128)
+    return blk, MoeBlock.from_host_block(blk, device=cuda), gptq_oracle_weights(blk)
+
+
+@pytest.mark.parametrize(("n", "path"), [(1, "gemv"), (1, "gemm"), (8, "gemv"), (64, "gemm")])
+def test_gptq_asym_block_against_gptq_formula(gptq_block, n, path):
+    """Asymmetric GPTQ experts: the oracle uses weights dequantized from the
+    raw GPTQ v1 tensors (qweight/qzeros/scales/g_idx), in float64."""
+    blk, dev, ow = gptq_block
+    x = synth.make_tokens(200 + n, n)
+    y, lg, idx, _ = _run(dev, x, PATHS[path])
+    exact = O.moe_block_f64(x, ow, logits=lg)
+    ref32 = O.moe_block(x, ow, logits=lg)
+    np.testing.assert_array_equal(idx, ref32.selected)
+    assert O.rel_l2(y, exact) < FP32_TOL
+    assert O.rel_l2(y, ref32.y) < FP32_FMA_TOL
+
+
+def test_int4_store_block(cuda):
+    """Symmetric int4 store records (value = nibble - 8, rtn_absmax7 g128)."""
+    blk = synth.make_block(4, fmt="int4", group=128, num_experts=16)
+    dev = MoeBlock.from_host_block(blk, device=cuda)
+    x = synth.make_tokens(4, 6)
+    for path in PATHS.values():
+        y, lg, idx, _ = _run(dev, x, path)
+        ref = O.moe_block(x, oracle_weights(blk), logits=lg)
+        np.testing.assert_array_equal(idx, ref.selected)
+        assert O.rel_l2(y, ref.y) < FP32_FMA_TOL
+
+
+def test_prefill4096_zipf_against_reference(cuda):
+    blk, x = synth.make_workload("prefill4096_int8_zipf", seed=0)
+    g = golden("moe_qwen")
+    dev = MoeBlock.from_host_block(blk, device=cuda)
+    y, lg, idx, _ = _run(dev, x, _lib.PATH_GEMM)
+    sel = g["prefill_sel"].astype(np.int64)
+    same = (idx == sel).all(axis=1)
+    assert same.mean() > 0.999, f"{(~same).sum()} tokens routed differently"
+    rows = np.nonzero(same[:32])[0]
+    assert O.rel_l2(y[rows], g["prefill_y_head"][rows]) < FP32_FMA_TOL
+    norms = np.linalg.norm(y.astype(np.float64), axis=1)
+    np.testing.assert_allclose(norms[same], g["prefill_y_rownorm"][same], rtol=1e-3)
+    counts = np.bincount(idx.ravel(), minlength=60)
+    assert counts.max() > 8 * np.median(counts)
