@@ -25,9 +25,7 @@ import ctypes as C
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -40,10 +38,6 @@ if str(ROOT) not in sys.path:
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 FLUSH_BYTES = 256 << 20
-CLOCK_FIELDS = (
-    "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-    "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
-)
 
 
 def parse_args():
@@ -93,48 +87,84 @@ def traffic_from_profiles(workload: str, stage: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi sampling (200 ms) during the timed region."""
+    """SM clock, power and clock-event reasons sampled through NVML every
+    20 ms while the timed region runs (the data nvidia-smi's clocks query
+    reports), for the GPU behind `device`."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = Path(tempfile.mkstemp(prefix="clocks-", suffix=".csv")[1])
+    REASONS = {
+        "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+        "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+        "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+        "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+        "hw_power_brake": "nvmlClocksEventReasonHwPowerBrakeSlowdown",
+    }
+
+    def __init__(self, device):
+        self.device = device
+        self.samples: list[tuple[float, float, int]] = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self, nv):
+        import torch
+
+        p = torch.cuda.get_device_properties(self.device)
+        try:
+            return nv.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0")
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.device.index or 0)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception as e:  # no NVML: report unsampled
+            self.error = f"{type(e).__name__}: {e}"
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                         nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                         int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                except Exception as e:
+                    self.error = f"{type(e).__name__}: {e}"
+                    return
+                self._stop.wait(0.02)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        rows = []
-        for line in self.path.read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0,
+                    "error": self.error}
+        import pynvml as nv
+
+        reasons = sorted(name for name, attr in self.REASONS.items()
+                         if any(r & getattr(nv, attr) for _, _, r in self.samples))
         return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-            "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
+            "sm_mhz": statistics.median(c for c, _, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "power_w_max": max(p for _, p, _ in self.samples),
             "reasons": reasons,
-            "samples": len(rows),
+            "samples": len(self.samples),
+            "source": "NVML, 20 ms period, during the timed steps",
         }
 
 
@@ -325,7 +355,7 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         for i in range(args.steps):
             flush.zero_()
             starts[i].record()

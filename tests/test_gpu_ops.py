@@ -123,20 +123,23 @@ def test_dequant_is_bit_exact(cuda):
     rng = np.random.default_rng(7)
     q, s = quant.int8_rowwise(rng.normal(0, 0.02, (300, 96)).astype(np.float32))
     w = torch.empty((300, 96), dtype=torch.float32, device=cuda)
-    _lib.check(L.er_dequant_int8(_t(q, cuda).data_ptr(), _t(s, cuda).data_ptr(), w.data_ptr(), 300, 96, None), "dq8")
+    # operands stay referenced until the asynchronous kernels have run
+    qd, sd = _t(q, cuda), _t(s, cuda)
+    _lib.check(L.er_dequant_int8(qd.data_ptr(), sd.data_ptr(), w.data_ptr(), 300, 96, None), "dq8")
     np.testing.assert_array_equal(w.cpu().numpy(), O.dequantize_rowwise_int8(q, s))
     v, s4 = quant.int4_rtn_absmax7(rng.normal(0, 0.02, (64, 256)).astype(np.float32), 32)
     p = quant.pack_nibbles(v)
     w4 = torch.empty((64, 256), dtype=torch.float32, device=cuda)
-    _lib.check(L.er_dequant_int4(_t(p, cuda).data_ptr(), _t(s4.view(np.uint16), cuda).data_ptr(), None, 32,
-                                 w4.data_ptr(), 64, 256, None), "dq4")
+    pd, s4d = _t(p, cuda), _t(s4.view(np.uint16), cuda)
+    _lib.check(L.er_dequant_int4(pd.data_ptr(), s4d.data_ptr(), None, 32, w4.data_ptr(), 64, 256, None), "dq4")
     np.testing.assert_array_equal(w4.cpu().numpy(), O.dequantize_groupwise_int4(p, s4, 32))
     # asymmetric GPTQ: bit-exact against the GPTQ formula itself
     t = quant.gptq_asym_rtn(rng.normal(0, 0.02, (48, 256)).astype(np.float32), 128)
     pk, sc, zr = quant.gptq_to_zp_matrix(t, 128)
     wz = torch.empty((48, 256), dtype=torch.float32, device=cuda)
-    _lib.check(L.er_dequant_int4(_t(pk, cuda).data_ptr(), _t(sc.view(np.uint16), cuda).data_ptr(),
-                                 _t(zr, cuda).data_ptr(), 128, wz.data_ptr(), 48, 256, None), "dqz")
+    pkd, scd, zrd = _t(pk, cuda), _t(sc.view(np.uint16), cuda), _t(zr, cuda)
+    _lib.check(L.er_dequant_int4(pkd.data_ptr(), scd.data_ptr(), zrd.data_ptr(), 128, wz.data_ptr(), 48, 256, None),
+               "dqz")
     np.testing.assert_array_equal(wz.cpu().numpy(), O.gptq_dequantize(t["qweight"], t["qzeros"], t["scales"], t["g_idx"]))
 
 
