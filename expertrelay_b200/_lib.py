@@ -79,6 +79,7 @@ SIGNATURES: dict[str, tuple] = {
     "er_router_topk": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "er_moe_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_block": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp, C.c_size_t, _vp]),
+    "er_moe_block_noalloc": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp]),
 }
 
 _lib: C.CDLL | None = None

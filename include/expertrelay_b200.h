@@ -138,6 +138,15 @@ typedef struct er_moe_io {
 #define ER_MOE_STAGES 5        /* router, plan, gate/up, down, combine */
 
 ER_API size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path);
+/* er_moe_block for callers that cannot allocate device memory (no counterpart
+ * in the reference): same weights and io, no workspace argument. The scratch
+ * is a fixed 8 MiB device array inside the library, held on each GPU from the
+ * first call there until exit; batches needing more (er_moe_workspace_bytes)
+ * fail with ER_ENOSPACE (97 tokens fit at Qwen1.5-MoE-A2.7B shapes). The
+ * first call on a device sets up the array's address: make it before any
+ * stream capture. All calls share the array, so calls that overlap on the GPU
+ * race and must be serialised by the caller. */
+ER_API int er_moe_block_noalloc(const er_moe_weights* w, const er_moe_io* io, void* stream);
 ER_API int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
                  void* stream);
 
