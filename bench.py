@@ -428,7 +428,9 @@ def main() -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32" if path in (_lib.PATH_GEMV, _lib.PATH_GEMM) or (path == _lib.PATH_AUTO) else "bf16",
+        # arithmetic: fp32 FMA (GEMV / SIMT GEMM) or int8 tensor-core MMA on int8 weights and two
+        # int8 activation slices with exact int32 accumulation (tcgen05 path)
+        "dtype": "i8" if path == _lib.PATH_TC else "f32",
         "data": "synthetic: seeded N(0,0.02) weights in store encodings, N(0,1) activations",
         "config": {
             "workload": args.workload,

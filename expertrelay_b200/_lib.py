@@ -39,6 +39,8 @@ class MoeWeights(C.Structure):
         ("shared_gate_w", _vp),
         ("expert_records", _vp),
         ("shared_record", _vp),
+        ("record_arena", _vp),
+        ("arena_slots", _i),
     ]
 
 

@@ -92,6 +92,14 @@ __device__ __forceinline__ void u4x8_to_f32(uint32_t w, float* f) {
   for (int j = 0; j < 8; ++j) f[j] = (float)((w >> (4 * j)) & 0xf);
 }
 
+// Four consecutive activations as fp32 (16-byte fp32 or 8-byte bf16 load).
+__device__ __forceinline__ float4 load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                     __uint_as_float(u.y & 0xffff0000u));
+}
+
 // Read-only, L1-bypassing 16-byte global load for weights read once.
 __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   uint4 r;

@@ -16,19 +16,6 @@
 
 namespace er {
 
-template <typename XT>
-__device__ __forceinline__ float4 ld4(const XT* p);
-template <>
-__device__ __forceinline__ float4 ld4<float>(const float* p) {
-  return *reinterpret_cast<const float4*>(p);
-}
-template <>
-__device__ __forceinline__ float4 ld4<__nv_bfloat16>(const __nv_bfloat16* p) {
-  const uint2 u = *reinterpret_cast<const uint2*>(p);
-  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
-                     __uint_as_float(u.y & 0xffff0000u));
-}
-
 template <int FMT, int MODE, typename XT>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(GroupArgs a, int sched, const XT* __restrict__ x,
                                                         float* act_r,
@@ -81,7 +68,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GroupArgs a, int sched, 
 
     for (int k0 = 0; k0 < K; k0 += BK) {
       float4 av = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (a_ok) av = MODE == 0 ? ld4<XT>(asrc_x + k0 + lk) : *reinterpret_cast<const float4*>(asrc_f + k0 + lk);
+      if (a_ok) av = MODE == 0 ? load4(asrc_x + k0 + lk) : *reinterpret_cast<const float4*>(asrc_f + k0 + lk);
       As[lk + 0][lrow] = av.x;
       As[lk + 1][lrow] = av.y;
       As[lk + 2][lrow] = av.z;

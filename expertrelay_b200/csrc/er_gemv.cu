@@ -21,23 +21,6 @@ namespace er {
 
 constexpr int kGemvSlab = 1024;  // K values staged per pass
 
-template <typename XT>
-__device__ __forceinline__ float4 load4(const XT* p);
-template <>
-__device__ __forceinline__ float4 load4<float>(const float* p) {
-  return *reinterpret_cast<const float4*>(p);
-}
-template <>
-__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
-  const uint2 u = *reinterpret_cast<const uint2*>(p);
-  float4 f;
-  f.x = __uint_as_float(u.x << 16);
-  f.y = __uint_as_float(u.x & 0xffff0000u);
-  f.z = __uint_as_float(u.y << 16);
-  f.w = __uint_as_float(u.y & 0xffff0000u);
-  return f;
-}
-
 template <int FMT, int MODE, typename XT>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_grouped_kernel(GroupArgs a, int sched,
                                                                        const XT* __restrict__ x,
@@ -92,7 +75,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_grouped_kernel(GroupArgs
           float4 val;
           if (MODE == 0) {
             const int tok = v.shared ? t0 + t : a.perm_token[v.row0 + t0 + t];
-            val = load4<XT>(x + (size_t)tok * a.H + k0 + kk);
+            val = load4(x + (size_t)tok * a.H + k0 + kk);
           } else {
             const float* src = v.shared ? act_s + (size_t)(t0 + t) * v.inter
                                         : act_r + (size_t)(v.row0 + t0 + t) * a.I;

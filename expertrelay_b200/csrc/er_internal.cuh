@@ -95,6 +95,27 @@ int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void
 int launch_combine_plan(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k,
                         int H, const Plan* plan, float* out, cudaStream_t st);
 
+// tcgen05 grouped GEMM (er_tc.cu)
+struct TcLaunch {
+  GroupArgs g;
+  int mode, sched;
+  const void* arena;           // routed records, arena_slots x record_bytes
+  int arena_slots;
+  size_t record_bytes;
+  int nk, n;
+  const int8_t *b0_r, *b1_r;   // B slices: mode 0 all nk + n rows of h; mode 1 routed act rows
+  const int8_t *b0_s, *b1_s;   // mode 1: shared act rows
+  const float *xscale_r, *xscale_s;
+  float *out_r, *out_s;
+  long long items_bound;
+};
+int launch_tc_grouped(const TcLaunch& L, cudaStream_t st);
+int launch_slice_rows(const void* src, int dtype, const int32_t* perm_token, int nk, int rows, int K, int src_mode,
+                      int8_t* s0, int8_t* s1, float* scale, cudaStream_t st);
+constexpr int kTcTokTileGU = 64;   // tokens per tcgen05 item, gate/up
+constexpr int kTcTokTileDN = 128;  // tokens per tcgen05 item, down
+constexpr int kTcUnits = 128;      // weight rows per tcgen05 item
+
 // GEMV schedule geometry (er_gemv.cu): units per item
 constexpr int kGemvWarps = 8;
 constexpr int kGemvRowsPerWarp = 8;          // weight rows per warp

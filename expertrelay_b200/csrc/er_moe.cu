@@ -10,10 +10,13 @@
 namespace er {
 
 struct WsLayout {
-  size_t logits, gate_logit, gate_sig, idx32, topw, plan, perm_token, perm_w, pos_of, act_r, act_s, y_r, y_s, total;
+  size_t logits, gate_logit, gate_sig, idx32, topw, plan, perm_token, perm_w, pos_of, act_r, act_s, y_r, y_s;
+  // tensor-core path: int8 activation slices and their row scales
+  size_t xs0, xs1, xscale, as0_r, as1_r, ascale_r, as0_s, as1_s, ascale_s;
+  size_t total;
 };
 
-static WsLayout ws_layout(const er_moe_weights* w, int n) {
+static WsLayout ws_layout(const er_moe_weights* w, int n, int path) {
   WsLayout L{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -35,6 +38,18 @@ static WsLayout ws_layout(const er_moe_weights* w, int n) {
   L.act_s = take((size_t)n * w->shared_inter * 4);
   L.y_r = take(nk * w->hidden * 4);
   L.y_s = take((size_t)n * w->hidden * 4);
+  if (path == ER_PATH_TC) {
+    const size_t rows = nk + n;
+    L.xs0 = take(rows * w->hidden);
+    L.xs1 = take(rows * w->hidden);
+    L.xscale = take(rows * 4);
+    L.as0_r = take(nk * w->inter);
+    L.as1_r = take(nk * w->inter);
+    L.ascale_r = take(nk * 4);
+    L.as0_s = take((size_t)n * w->shared_inter);
+    L.as1_s = take((size_t)n * w->shared_inter);
+    L.ascale_s = take((size_t)n * 4);
+  }
   L.total = off;
   return L;
 }
@@ -75,9 +90,8 @@ static int pick_path(int path, int n) {
 using namespace er;
 
 extern "C" size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path) {
-  (void)path;
   if (validate(w) != ER_OK || n < 0) return 0;
-  return ws_layout(w, n).total;
+  return ws_layout(w, n, pick_path(path, n)).total;
 }
 
 extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
@@ -92,9 +106,15 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     return fail(ER_EINVAL, "er_moe_block: unknown activation dtype %d", io->h_dtype);
   if (((uintptr_t)io->h | (uintptr_t)io->y) & 15) return fail(ER_EINVAL, "er_moe_block: h and y must be 16-byte aligned");
   const int path = pick_path(io->path, n);
-  if (path != ER_PATH_GEMV && path != ER_PATH_GEMM)
-    return fail(ER_EINVAL, "er_moe_block: path %d is not available in this build", io->path);
-  const WsLayout L = ws_layout(w, n);
+  if (path != ER_PATH_GEMV && path != ER_PATH_GEMM && path != ER_PATH_TC)
+    return fail(ER_EINVAL, "er_moe_block: unknown path %d", io->path);
+  if (path == ER_PATH_TC) {
+    if (w->expert_fmt != ER_FMT_INT8)
+      return fail(ER_EINVAL, "er_moe_block: the tensor-core path takes int8 expert records");
+    if (!w->record_arena || w->arena_slots < 1 || ((uintptr_t)w->record_arena & 15))
+      return fail(ER_EINVAL, "er_moe_block: the tensor-core path needs the record arena (record_arena, arena_slots)");
+  }
+  const WsLayout L = ws_layout(w, n, path);
   if (!workspace || workspace_bytes < L.total)
     return fail(ER_ENOSPACE, "er_moe_block: workspace %zu bytes, need %zu", workspace_bytes, L.total);
   if ((uintptr_t)workspace & 255) return fail(ER_EINVAL, "er_moe_block: workspace must be 256-byte aligned");
@@ -154,6 +174,9 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   if (path == ER_PATH_GEMV) {
     specs[0] = SchedSpec{0, kGemvUnitsGU, 0};
     specs[1] = SchedSpec{0, kGemvUnitsDN, 1};
+  } else if (path == ER_PATH_TC) {
+    specs[0] = SchedSpec{kTcTokTileGU, kTcUnits, 0};
+    specs[1] = SchedSpec{kTcTokTileDN, kTcUnits, 1};
   } else {
     specs[0] = SchedSpec{kSimtBM, kSimtBN, 0};
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
@@ -184,8 +207,55 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   const long long b1 = sched_items_bound(specs[1], n, k, E, H, w->inter, w->shared_inter);
   // one int8 instance (the shared expert and int8 routed experts), plus one
   // instance of the routed format when it is int4
-  const int per_stage = w->expert_fmt == ER_FMT_INT8 ? 1 : 2;
-  if (path == ER_PATH_GEMV) {
+  const int per_stage = (w->expert_fmt == ER_FMT_INT8 || path == ER_PATH_TC) ? 1 : 2;
+  if (path == ER_PATH_TC) {
+    const size_t nk = (size_t)n * k;
+    int8_t* xs0 = reinterpret_cast<int8_t*>(ws + L.xs0);
+    int8_t* xs1 = reinterpret_cast<int8_t*>(ws + L.xs1);
+    float* xscale = reinterpret_cast<float*>(ws + L.xscale);
+    int8_t* as0_r = reinterpret_cast<int8_t*>(ws + L.as0_r);
+    int8_t* as1_r = reinterpret_cast<int8_t*>(ws + L.as1_r);
+    float* ascale_r = reinterpret_cast<float*>(ws + L.ascale_r);
+    int8_t* as0_s = reinterpret_cast<int8_t*>(ws + L.as0_s);
+    int8_t* as1_s = reinterpret_cast<int8_t*>(ws + L.as1_s);
+    float* ascale_s = reinterpret_cast<float*>(ws + L.ascale_s);
+    TcLaunch tl{};
+    tl.g = ga;
+    tl.arena = w->record_arena;
+    tl.arena_slots = w->arena_slots;
+    tl.record_bytes = er_record_bytes(ER_FMT_INT8, H, w->inter, 0);
+    tl.nk = (int)nk;
+    tl.n = n;
+    if (int rc = launch_slice_rows(io->h, io->h_dtype, perm_token, (int)nk, (int)nk + n, H, 0, xs0, xs1, xscale, st))
+      return rc;
+    tl.mode = 0;
+    tl.sched = 0;
+    tl.b0_r = xs0;
+    tl.b1_r = xs1;
+    tl.xscale_r = xscale;
+    tl.out_r = act_r;
+    tl.out_s = act_s;
+    tl.items_bound = b0;
+    if (int rc = launch_tc_grouped(tl, st)) return rc;
+    if (int rc = mark(3)) return rc;
+    if (int rc = launch_slice_rows(act_r, ER_DTYPE_F32, nullptr, 0, (int)nk, w->inter, 1, as0_r, as1_r, ascale_r, st))
+      return rc;
+    if (int rc = launch_slice_rows(act_s, ER_DTYPE_F32, nullptr, 0, n, w->shared_inter, 1, as0_s, as1_s, ascale_s, st))
+      return rc;
+    tl.mode = 1;
+    tl.sched = 1;
+    tl.b0_r = as0_r;
+    tl.b1_r = as1_r;
+    tl.b0_s = as0_s;
+    tl.b1_s = as1_s;
+    tl.xscale_r = ascale_r;
+    tl.xscale_s = ascale_s;
+    tl.out_r = y_r;
+    tl.out_s = y_s;
+    tl.items_bound = b1;
+    if (int rc = launch_tc_grouped(tl, st)) return rc;
+    launches += 3;  // the three slice launches; the two GEMMs are counted below
+  } else if (path == ER_PATH_GEMV) {
     if (int rc = launch_gemv_grouped(ga, 0, 0, io->h, io->h_dtype, act_r, act_s, nullptr, nullptr, b0, st)) return rc;
     if (int rc = mark(3)) return rc;
     if (int rc = launch_gemv_grouped(ga, 1, 1, nullptr, ER_DTYPE_F32, act_r, act_s, y_r, y_s, b1, st)) return rc;

@@ -89,6 +89,7 @@ class MoeBlock:
             expert_records=self.expert_table.data_ptr(),
             shared_record=self.shared_record.data_ptr(),
         )
+        self._set_arena()
         self._ws: torch.Tensor | None = None
 
     @classmethod
@@ -114,6 +115,16 @@ class MoeBlock:
         self.records = t.reshape(self.num_experts, rs).to(self.device).contiguous()
         base = self.records.data_ptr()
         self.set_expert_table(torch.arange(self.num_experts, dtype=torch.int64, device=self.device) * rs + base)
+        if hasattr(self, "_w"):
+            self._set_arena()
+
+    def _set_arena(self, base: int | None = None, slots: int | None = None) -> None:
+        """Declare the array the routed records live in (the tensor-core path
+        addresses records as slots of one arena)."""
+        if base is None and self.records is not None:
+            base, slots = self.records.data_ptr(), self.num_experts
+        self._w.record_arena = base
+        self._w.arena_slots = int(slots or 0)
 
     def set_expert_table(self, addresses: torch.Tensor) -> None:
         """Device addresses of each expert's record (e.g. HBM cache slots)."""

@@ -60,7 +60,7 @@ extern "C" {
 #define ER_PATH_AUTO 0     /* stream weights (GEMV) for small n, tiled GEMM otherwise */
 #define ER_PATH_GEMV 1     /* weight-streaming grouped GEMV, any n (slow for large n) */
 #define ER_PATH_GEMM 2     /* tiled grouped GEMM, fp32 FMA (exact-fp32 path) */
-#define ER_PATH_TC 3       /* tcgen05 tensor-core grouped GEMM (bf16 operands) */
+#define ER_PATH_TC 3       /* tcgen05 grouped GEMM: int8 weights x two int8 activation slices, int32 accumulate */
 
 /* library identity / diagnostics */
 ER_API int er_version(void);                 /* e.g. 100 = 0.1.0 */
@@ -116,6 +116,11 @@ typedef struct er_moe_weights {
   const float* shared_gate_w;  /* [H] fp32 (mlp.shared_expert_gate.weight) */
   const uint64_t* expert_records; /* DEVICE array [E] of record base addresses (4096-aligned) */
   const void* shared_record;   /* the shared expert as an ER_FMT_INT8 record with inter = shared_inter */
+  /* optional (required by ER_PATH_TC): the routed records sit in one array of
+   * arena_slots records of er_record_bytes() each starting here (e.g. the HBM
+   * expert cache), and every expert_records[e] points at one of its slots */
+  const void* record_arena;
+  int arena_slots;
 } er_moe_weights;
 
 typedef struct er_moe_io {

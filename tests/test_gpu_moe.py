@@ -31,6 +31,9 @@ FP32_TOL = 1e-3
 FP32_FMA_TOL = 1e-4
 BF16_TOL = 1e-2
 PATHS = {"gemv": _lib.PATH_GEMV, "gemm": _lib.PATH_GEMM}
+# the tensor-core path (int8 records only): int8 weights x two int8 activation slices
+PATHS_INT8 = {**PATHS, "tc": _lib.PATH_TC}
+TOL = {"gemv": FP32_FMA_TOL, "gemm": FP32_FMA_TOL, "tc": FP32_TOL}
 
 
 def _run(block: MoeBlock, x: np.ndarray, path: int, logits: np.ndarray | None = None, dtype=torch.float32):
@@ -53,16 +56,15 @@ def _mini_block(fmt: str, cuda) -> MoeBlock:
                     shared_inter=48, records=g[f"{tag}_records"], top_k=4, device=cuda)
 
 
-@pytest.mark.parametrize("path", list(PATHS))
-@pytest.mark.parametrize("fmt", ["int8", "int4"])
+@pytest.mark.parametrize(("fmt", "path"), [("int8", p) for p in PATHS_INT8] + [("int4", p) for p in PATHS])
 def test_small_block_matches_reference(cuda, fmt, path):
     g = golden("moe_mini")
     blk = _mini_block(fmt, cuda)
     x = g[f"mini_{fmt}_x"]
-    y, lg, idx, w = _run(blk, x, PATHS[path])
+    y, lg, idx, w = _run(blk, x, PATHS_INT8[path])
     np.testing.assert_allclose(lg, g[f"mini_{fmt}_logits"], rtol=1e-5, atol=1e-5)
     np.testing.assert_array_equal(idx, g[f"mini_{fmt}_sel"])
-    assert O.rel_l2(y, g[f"mini_{fmt}_y"]) < FP32_FMA_TOL
+    assert O.rel_l2(y, g[f"mini_{fmt}_y"]) < TOL[path]
 
 
 @pytest.fixture(scope="module")
@@ -74,39 +76,42 @@ def decode8(cuda):
     return blk, x, MoeBlock.from_host_block(blk, device=cuda), g
 
 
-@pytest.mark.parametrize("path", list(PATHS))
+@pytest.mark.parametrize("path", list(PATHS_INT8))
 def test_decode8_matches_reference(decode8, path):
     blk, x, dev, g = decode8
-    y, lg, idx, w = _run(dev, x, PATHS[path])
+    y, lg, idx, w = _run(dev, x, PATHS_INT8[path])
     np.testing.assert_allclose(lg, g["decode8_logits"], rtol=1e-4, atol=1e-5)
     np.testing.assert_array_equal(idx, g["decode8_sel"])
-    assert O.rel_l2(y, g["decode8_y_blocked"]) < FP32_FMA_TOL
+    assert O.rel_l2(y, g["decode8_y_blocked"]) < TOL[path]
     # routing pinned to the reference's logits: ids bit-exact, same output
-    y2, _, idx2, w2 = _run(dev, x, PATHS[path], logits=g["decode8_logits"])
+    y2, _, idx2, w2 = _run(dev, x, PATHS_INT8[path], logits=g["decode8_logits"])
     np.testing.assert_array_equal(idx2, g["decode8_sel"])
     np.testing.assert_allclose(w2, np.take_along_axis(O.softmax(g["decode8_logits"]), idx2, -1), rtol=1e-6)
-    assert O.rel_l2(y2, g["decode8_y_blocked"]) < FP32_FMA_TOL
+    assert O.rel_l2(y2, g["decode8_y_blocked"]) < TOL[path]
 
 
-def test_decode8_bf16_activations(decode8):
+@pytest.mark.parametrize("path", ["gemv", "tc"])
+def test_decode8_bf16_activations(decode8, path):
     blk, x, dev, g = decode8
     xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
-    y, lg, idx, _ = _run(dev, x, _lib.PATH_GEMV, dtype=torch.bfloat16)
+    y, lg, idx, _ = _run(dev, x, PATHS_INT8[path], dtype=torch.bfloat16)
     ref = O.moe_block(xb, oracle_weights(blk))
     np.testing.assert_array_equal(idx, ref.selected)
     assert O.rel_l2(y, ref.y) < BF16_TOL
 
 
-@pytest.mark.parametrize("n", [1, 3, 17])
-@pytest.mark.parametrize("path", list(PATHS))
+@pytest.mark.parametrize("n", [1, 3, 17, 70, 300])
+@pytest.mark.parametrize("path", list(PATHS_INT8))
 def test_decode_shapes_against_oracle(decode8, n, path):
     blk, _, dev, _ = decode8
+    if n > 70 and path == "gemv":
+        pytest.skip("the weight-streaming path is for decode-sized batches")
     x = synth.make_tokens(100 + n, n)
     ow = oracle_weights(blk)
-    y, lg, idx, _ = _run(dev, x, PATHS[path])
+    y, lg, idx, _ = _run(dev, x, PATHS_INT8[path])
     ref = O.moe_block(x, ow, logits=lg)  # same routing decision on both sides
     np.testing.assert_array_equal(idx, ref.selected)
-    assert O.rel_l2(y, ref.y) < FP32_FMA_TOL
+    assert O.rel_l2(y, ref.y) < TOL[path]
 
 
 def test_edge_routing_cases(decode8):
@@ -118,10 +123,10 @@ def test_edge_routing_cases(decode8):
     ow = oracle_weights(blk)
     lg = np.full((n, 60), -3.0, dtype=np.float32)
     lg[:, [59, 0, 31, 7]] = [4.0, 3.0, 2.0, 1.0]
-    for path in PATHS.values():
+    for name, path in PATHS_INT8.items():
         y, _, idx, _ = _run(dev, x, path, logits=lg)
         assert (idx == [59, 0, 31, 7]).all()
-        assert O.rel_l2(y, O.moe_block(x, ow, logits=lg).y) < FP32_FMA_TOL
+        assert O.rel_l2(y, O.moe_block(x, ow, logits=lg).y) < TOL[name]
     ties = np.zeros((n, 60), dtype=np.float32)
     y, _, idx, w = _run(dev, x, _lib.PATH_GEMV, logits=ties)
     assert (idx == [0, 1, 2, 3]).all()
@@ -164,16 +169,21 @@ def test_int4_store_block(cuda):
         assert O.rel_l2(y, ref.y) < FP32_FMA_TOL
 
 
-def test_prefill4096_zipf_against_reference(cuda):
+@pytest.fixture(scope="module")
+def prefill(cuda):
     blk, x = synth.make_workload("prefill4096_int8_zipf", seed=0)
-    g = golden("moe_qwen")
-    dev = MoeBlock.from_host_block(blk, device=cuda)
-    y, lg, idx, _ = _run(dev, x, _lib.PATH_GEMM)
+    return blk, x, MoeBlock.from_host_block(blk, device=cuda), golden("moe_qwen")
+
+
+@pytest.mark.parametrize("path", ["gemm", "tc"])
+def test_prefill4096_zipf_against_reference(prefill, path):
+    blk, x, dev, g = prefill
+    y, lg, idx, _ = _run(dev, x, PATHS_INT8[path])
     sel = g["prefill_sel"].astype(np.int64)
     same = (idx == sel).all(axis=1)
     assert same.mean() > 0.999, f"{(~same).sum()} tokens routed differently"
     rows = np.nonzero(same[:32])[0]
-    assert O.rel_l2(y[rows], g["prefill_y_head"][rows]) < FP32_FMA_TOL
+    assert O.rel_l2(y[rows], g["prefill_y_head"][rows]) < TOL[path]
     norms = np.linalg.norm(y.astype(np.float64), axis=1)
     np.testing.assert_allclose(norms[same], g["prefill_y_rownorm"][same], rtol=1e-3)
     counts = np.bincount(idx.ravel(), minlength=60)
