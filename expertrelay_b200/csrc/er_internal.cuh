@@ -103,6 +103,7 @@ struct TcLaunch {
   int arena_slots;
   size_t record_bytes;
   int nk, n;
+  int tok_tile;                // tokens per work item: 16 (decode batches) or 128
   const int8_t *b0_r, *b1_r;   // B slices: mode 0 all nk + n rows of h; mode 1 routed act rows
   const int8_t *b0_s, *b1_s;   // mode 1: shared act rows
   const float *xscale_r, *xscale_s;
@@ -112,9 +113,10 @@ struct TcLaunch {
 int launch_tc_grouped(const TcLaunch& L, cudaStream_t st);
 int launch_slice_rows(const void* src, int dtype, const int32_t* perm_token, int nk, int rows, int K, int src_mode,
                       int8_t* s0, int8_t* s1, float* scale, cudaStream_t st);
-constexpr int kTcTokTileGU = 64;   // tokens per tcgen05 item, gate/up
-constexpr int kTcTokTileDN = 128;  // tokens per tcgen05 item, down
-constexpr int kTcUnits = 128;      // weight rows per tcgen05 item
+// tokens per tcgen05 work item: 16 when every group fits (n <= 16), else 128
+inline int tc_tok_tile(int n) { return n <= 16 ? 16 : 128; }
+constexpr int kTcUnitsGU = 64;    // intermediate columns per gate/up item (64 gate + 64 up rows)
+constexpr int kTcUnitsDN = 128;   // hidden rows per down item
 
 // GEMV schedule geometry (er_gemv.cu): units per item
 constexpr int kGemvWarps = 8;

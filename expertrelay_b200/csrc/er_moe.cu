@@ -175,8 +175,8 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     specs[0] = SchedSpec{0, kGemvUnitsGU, 0};
     specs[1] = SchedSpec{0, kGemvUnitsDN, 1};
   } else if (path == ER_PATH_TC) {
-    specs[0] = SchedSpec{kTcTokTileGU, kTcUnits, 0};
-    specs[1] = SchedSpec{kTcTokTileDN, kTcUnits, 1};
+    specs[0] = SchedSpec{tc_tok_tile(n), kTcUnitsGU, 0};
+    specs[1] = SchedSpec{tc_tok_tile(n), kTcUnitsDN, 1};
   } else {
     specs[0] = SchedSpec{kSimtBM, kSimtBN, 0};
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
@@ -226,6 +226,7 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.record_bytes = er_record_bytes(ER_FMT_INT8, H, w->inter, 0);
     tl.nk = (int)nk;
     tl.n = n;
+    tl.tok_tile = tc_tok_tile(n);
     if (int rc = launch_slice_rows(io->h, io->h_dtype, perm_token, (int)nk, (int)nk + n, H, 0, xs0, xs1, xscale, st))
       return rc;
     tl.mode = 0;

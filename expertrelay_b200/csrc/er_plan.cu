@@ -30,12 +30,16 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
   for (int e = tid; e < kMaxExperts; e += kPlanThreads) hist[e] = 0;
   if (tid == 0) bad = 0;
   __syncthreads();
-  for (int i = tid; i < nk; i += kPlanThreads) {
-    const int e = idx[i];
-    if (e >= 0 && e < E)
-      atomicAdd(&hist[e], 1);
-    else
+  // warp-aggregated histogram: one shared-memory atomic per distinct expert per warp
+  for (int i0 = 0; i0 < nk; i0 += kPlanThreads) {
+    const int i = i0 + tid;
+    int e = i < nk ? idx[i] : -1;
+    if (i < nk && (e < 0 || e >= E)) {
       bad = 1;
+      e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (__ffs(peers) - 1) == lane) atomicAdd(&hist[e], __popc(peers));
   }
   __syncthreads();
   if (tid == 0) {
@@ -72,6 +76,10 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
         acc += mt * nt;
       }
       plan->item_start[s][na] = acc;
+    }
+    if (bad) {  // no work items: nothing downstream may read the unfilled permutation
+      plan->num_active = 0;
+      for (int s = 0; s < kNumSched; ++s) plan->item_start[s][0] = 0;
     }
   }
   __syncthreads();

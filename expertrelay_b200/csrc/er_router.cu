@@ -8,53 +8,115 @@
 
 namespace er {
 
-// logits[t, e] = h[t] . W_r[e] for e < E and gate_logit[t] = h[t] . w_g (row E),
-// fp32 FMA. One CTA holds kTok tokens of h in shared memory; its warps walk
-// a slice of the E + 1 weight rows (grid.y slices split the rows for small n).
+// Decode-sized batches: one CTA per weight row r of [W_r; w_g] (E + 1 rows).
+// Thread i owns columns {4i + 1024j}; the row stays in registers while the
+// CTA walks the tokens kRouterTok at a time; fp32 FMA, then a block reduction.
 template <typename XT>
-__global__ void __launch_bounds__(256) router_logits_kernel(const XT* __restrict__ h, int n, int H,
-                                                            const float* __restrict__ wr,
-                                                            const float* __restrict__ wg, int E,
-                                                            float* __restrict__ logits,
-                                                            float* __restrict__ gate_logit,
-                                                            int rows_per_cta) {
+__global__ void __launch_bounds__(256) router_rows_kernel(const XT* __restrict__ h, int n, int H,
+                                                          const float* __restrict__ wr, const float* __restrict__ wg,
+                                                          int E, float* __restrict__ logits,
+                                                          float* __restrict__ gate_logit) {
   constexpr int kTok = kRouterTok;
-  extern __shared__ __align__(16) float hs[];  // [kTok][H]
-  const int t0 = blockIdx.x * kTok;
-  const int nt = min(kTok, n - t0);
-  for (int i = threadIdx.x; i < kTok * H; i += blockDim.x) {
-    const int t = i / H, k = i - t * H;
-    hs[i] = (t < nt) ? to_f32(h[(size_t)(t0 + t) * H + k]) : 0.f;
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const int r_begin = blockIdx.y * rows_per_cta;
-  const int r_end = min(E + 1, r_begin + rows_per_cta);
-  for (int r = r_begin + warp; r < r_end; r += nw) {
-    const float* w = (r < E) ? wr + (size_t)r * H : wg;
+  __shared__ float red[8][kTok];
+  const int r = blockIdx.x;
+  const float* w = (r < E) ? wr + (size_t)r * H : wg;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t0 = 0; t0 < n; t0 += kTok) {
+    const int nt = min(kTok, n - t0);
     float acc[kTok];
 #pragma unroll
     for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
-    for (int k = lane * 4; k < H; k += 128) {
+    for (int k = threadIdx.x * 4; k < H; k += 1024) {
       const float4 wv = *reinterpret_cast<const float4*>(w + k);
 #pragma unroll
       for (int t = 0; t < kTok; ++t) {
-        const float4 xv = *reinterpret_cast<const float4*>(hs + t * H + k);
-        acc[t] = fmaf(wv.x, xv.x, acc[t]);
-        acc[t] = fmaf(wv.y, xv.y, acc[t]);
-        acc[t] = fmaf(wv.z, xv.z, acc[t]);
-        acc[t] = fmaf(wv.w, xv.w, acc[t]);
+        if (t < nt) {
+          const float4 xv = load4(h + (size_t)(t0 + t) * H + k);
+          acc[t] = fmaf(wv.x, xv.x, acc[t]);
+          acc[t] = fmaf(wv.y, xv.y, acc[t]);
+          acc[t] = fmaf(wv.z, xv.z, acc[t]);
+          acc[t] = fmaf(wv.w, xv.w, acc[t]);
+        }
       }
     }
 #pragma unroll
-    for (int t = 0; t < kTok; ++t) acc[t] = warp_sum(acc[t]);
-    if (lane == 0) {
-      for (int t = 0; t < nt; ++t) {
-        if (r < E)
-          logits[(size_t)(t0 + t) * E + r] = acc[t];
-        else if (gate_logit)
-          gate_logit[t0 + t] = acc[t];
-      }
+    for (int t = 0; t < kTok; ++t) {
+      const float v = warp_sum(acc[t]);
+      if (lane == 0) red[warp][t] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < nt) {
+      float v = 0.f;
+      for (int w8 = 0; w8 < 8; ++w8) v += red[w8][threadIdx.x];
+      if (r < E)
+        logits[(size_t)(t0 + threadIdx.x) * E + r] = v;
+      else if (gate_logit)
+        gate_logit[t0 + threadIdx.x] = v;
+    }
+    __syncthreads();
+  }
+}
+
+// Large batches: a tiled fp32 GEMM, 32 tokens x 64 rows of [W_r; w_g] per
+// CTA (rows past E + 1 are zero), K in steps of 32 through shared memory;
+// each thread owns 2 tokens x 4 rows.
+template <typename XT>
+__global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__ h, int n, int H,
+                                                          const float* __restrict__ wr, const float* __restrict__ wg,
+                                                          int E, float* __restrict__ logits,
+                                                          float* __restrict__ gate_logit) {
+  constexpr int BM = 32, BN = 64, BK = 32;
+  __shared__ __align__(16) float As[BK][BM + 4];
+  __shared__ __align__(16) float Bs[BK][BN + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.x * BM;
+  const int rows = E + 1;
+  float acc[2][4] = {};
+  for (int k0 = 0; k0 < H; k0 += BK) {
+    {  // A: 32 tokens x 32 k, one float4 per thread
+      const int r = tid >> 3, kk = (tid & 7) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m0 + r < n && k0 + kk < H) v = load4(h + (size_t)(m0 + r) * H + k0 + kk);
+      As[kk + 0][r] = v.x;
+      As[kk + 1][r] = v.y;
+      As[kk + 2][r] = v.z;
+      As[kk + 3][r] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {  // B: 64 rows x 32 k, two float4 per thread
+      const int q = tid + 256 * i;
+      const int r = q >> 3, kk = (q & 7) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < rows && k0 + kk < H) v = *reinterpret_cast<const float4*>((r < E ? wr + (size_t)r * H : wg) + k0 + kk);
+      Bs[kk + 0][r] = v.x;
+      Bs[kk + 1][r] = v.y;
+      Bs[kk + 2][r] = v.z;
+      Bs[kk + 3][r] = v.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      const float2 a = *reinterpret_cast<const float2*>(&As[kk][ty * 2]);
+      const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float av[2] = {a.x, a.y}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int t = m0 + ty * 2 + i;
+    if (t >= n) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = tx * 4 + j;
+      if (r < E)
+        logits[(size_t)t * E + r] = acc[i][j];
+      else if (r == E && gate_logit)
+        gate_logit[t] = acc[i][j];
     }
   }
 }
@@ -150,37 +212,22 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
                          float* logits, float* gate_logit, cudaStream_t st) {
   if (n <= 0) return ER_OK;
-  const size_t smem = (size_t)kRouterTok * H * sizeof(float);
-  static thread_local int configured_dev[2] = {-1, -1};
-  int dev = 0;
-  if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
-  const int tiles = (n + kRouterTok - 1) / kRouterTok;
-  // few token tiles: split the E + 1 rows over CTAs so the launch fills the GPU
-  const int splits = tiles >= 64 ? 1 : 8;
-  const int rows_per_cta = (E + 1 + splits - 1) / splits;
-  dim3 grid(tiles, splits);
-  if (h_dtype == ER_DTYPE_F32) {
-    if (configured_dev[0] != dev) {
-      if (int rc = cuda_check(cudaFuncSetAttribute(router_logits_kernel<float>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
-                              "router smem attribute"))
-        return rc;
-      configured_dev[0] = dev;
-    }
-    router_logits_kernel<float><<<grid, 256, smem, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit,
-                                                         rows_per_cta);
-  } else {
-    if (configured_dev[1] != dev) {
-      if (int rc = cuda_check(cudaFuncSetAttribute(router_logits_kernel<__nv_bfloat16>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
-                              "router smem attribute"))
-        return rc;
-      configured_dev[1] = dev;
-    }
-    router_logits_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E,
-                                                                 logits, gate_logit, rows_per_cta);
+  // E == 0: only the shared-gate row (the caller supplies router logits)
+  if (n <= 64 || E + 1 > 64) {
+    if (h_dtype == ER_DTYPE_BF16)
+      router_rows_kernel<__nv_bfloat16><<<E + 1, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
+                                                                gate_logit);
+    else
+      router_rows_kernel<float><<<E + 1, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit);
+    return launch_check("router_rows_kernel");
   }
-  return launch_check("router_logits_kernel");
+  const int grid = (n + 31) / 32;
+  if (h_dtype == ER_DTYPE_BF16)
+    router_gemm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
+                                                            gate_logit);
+  else
+    router_gemm_kernel<float><<<grid, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit);
+  return launch_check("router_gemm_kernel");
 }
 
 int launch_router_topk(const float* logits, int n, int E, int k, int norm, int64_t* idx64, int32_t* idx32,

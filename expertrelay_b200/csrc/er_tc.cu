@@ -35,13 +35,10 @@
 
 namespace er {
 
-constexpr int kTcStages = 4;
-constexpr int kTcStageBytes = 48 * 1024;
-constexpr int kTcEpiWarps = 4;
+constexpr int kTcEpiWarps = 8;  // two per TMEM lane quadrant, splitting the token columns
 constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;
 constexpr int kTcAccCols = 256;  // TMEM columns per accumulator set (x2 buffers = 512)
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
-constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes + 2048;
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -203,10 +200,10 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ 
 // ---------------------------------------------------------------------------
 
 struct TcMaps {
-  CUtensorMap a_routed[2];  // mode 0: gate, up over the arena; mode 1: down in [0]
+  CUtensorMap a_routed[2];  // mode 0: gate, up (64-row boxes) over the arena; mode 1: down in [0]
   CUtensorMap a_shared[2];  // the same for the shared-expert record (2-D)
-  CUtensorMap b_routed[2];  // activation slices of the routed rows
-  CUtensorMap b_shared[2];  // activation slices of the shared rows (mode 1; mode 0 uses b_routed)
+  CUtensorMap b_routed[2];  // activation slices 0 / 1 of the routed rows (mode 0: all nk + n rows)
+  CUtensorMap b_shared[2];  // mode 1: activation slices of the shared rows
 };
 
 struct TcArgs {
@@ -222,29 +219,38 @@ struct TcArgs {
   Plan* plan_rw;             // error bits
 };
 
-template <int MODE>
+// TT = tokens per work item (128 for prefill, 16 for decode batches).
+// A tile: 128 weight rows x 128 bytes of K per stage (mode 0: 64 gate rows,
+// then the same 64 columns' up rows). B tile: slice 0 of TT token rows, then
+// slice 1 of the same rows, so ONE MMA with N = TT + npad covers both slices
+// and reads A once. The accumulator holds slice 0 in columns [0, TT) and
+// slice 1 in [TT, 2 TT).
+template <int MODE, int TT>
 struct TcGeom {
-  static constexpr int kTokTile = MODE == 0 ? kTcTokTileGU : kTcTokTileDN;  // B rows (tokens) per item
-  static constexpr int kNumAcc = MODE == 0 ? 4 : 2;      // accumulators per item
-  static constexpr int kABytes = MODE == 0 ? 32768 : 16384;
-  static constexpr int kBSliceBytes = kTokTile * 128;
-  static constexpr int kTxBytes = kABytes + 2 * kBSliceBytes;
+  static constexpr int kABytes = 16384;
+  static constexpr int kBSliceBytes = TT * 128;
+  static constexpr int kStageBytes = kABytes + 2 * kBSliceBytes;
+  static constexpr int kStages = TT >= 128 ? 4 : 9;
+  static constexpr int kUnits = MODE == 0 ? 64 : 128;  // intermediate columns / hidden rows per item
+  static constexpr size_t kRingBytes = (size_t)kStages * kStageBytes;
+  static constexpr size_t kXchBytes = MODE == 0 ? 4 * 2 * 16 * 32 * 4 : 0;  // gate/up exchange
+  static constexpr size_t kSmem = kRingBytes + kXchBytes + 2048;
 };
 
 struct TcItem {
   int g, shared, valid;
-  int unit0;   // first weight row of the tile (mode 0: intermediate column; mode 1: hidden row)
+  int unit0;   // first unit of the tile (mode 0: intermediate column; mode 1: hidden row)
   int tok0;    // first token of the tile within the group
   int nvalid;  // tokens in the tile
-  int npad;    // MMA N (multiple of 16)
+  int npad;    // tokens rounded up to 16
   int brow0;   // first B row in the operand matrix
   int slot;    // arena slot of the routed record
-  int units, K, nkb;
+  int units, nkb;
 };
 
-template <int MODE>
+template <int MODE, int TT>
 __device__ __forceinline__ bool tc_item(const TcArgs& t, int item, TcItem& it) {
-  using Geo = TcGeom<MODE>;
+  using Geo = TcGeom<MODE, TT>;
   int local = 0;
   const int g = find_item(t.g.plan, t.sched, item, &local);
   if (g < 0) return false;
@@ -253,13 +259,13 @@ __device__ __forceinline__ bool tc_item(const TcArgs& t, int item, TcItem& it) {
   it.shared = (g == t.g.E);
   const int inter = it.shared ? t.g.Is : t.g.I;
   it.units = MODE == 0 ? inter : t.g.H;
-  it.K = MODE == 0 ? t.g.H : inter;
-  it.nkb = (it.K + 127) / 128;
-  const int ntiles = (it.units + kTcUnits - 1) / kTcUnits;
+  const int K = MODE == 0 ? t.g.H : inter;
+  it.nkb = (K + 127) / 128;
+  const int ntiles = (it.units + Geo::kUnits - 1) / Geo::kUnits;
   const int rows = P->counts[g];
-  it.tok0 = (local / ntiles) * Geo::kTokTile;
-  it.unit0 = (local % ntiles) * kTcUnits;
-  it.nvalid = min(Geo::kTokTile, rows - it.tok0);
+  it.tok0 = (local / ntiles) * TT;
+  it.unit0 = (local % ntiles) * Geo::kUnits;
+  it.nvalid = min(TT, rows - it.tok0);
   it.npad = (it.nvalid + 15) & ~15;
   if (MODE == 0)
     it.brow0 = (it.shared ? P->nk : P->offsets[g]) + it.tok0;
@@ -279,22 +285,26 @@ __device__ __forceinline__ bool tc_item(const TcArgs& t, int item, TcItem& it) {
   return true;
 }
 
-template <int MODE>
+template <int MODE, int TT>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __grid_constant__ TcMaps maps, TcArgs t) {
-  using Geo = TcGeom<MODE>;
+  using Geo = TcGeom<MODE, TT>;
+  constexpr int S = Geo::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes);
-  uint64_t* empty = full + kTcStages;
-  uint64_t* acc_full = empty + kTcStages;
+  float* xch = reinterpret_cast<float*>(smem + Geo::kRingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Geo::kRingBytes + Geo::kXchBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* xfull = drain_bar + 1;   // [pair*2 + half][buffer]: u values written (32 arrivals)
+  uint64_t* xempty = xfull + 8;      // [pair*2 + half][buffer]: u values consumed (32 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -303,6 +313,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       mbar_init(&acc_empty[b], kTcEpiWarps * 32);
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < 8; ++i) {
+      mbar_init(&xfull[i], 32);
+      mbar_init(&xempty[i], 32);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -324,11 +338,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     bool ok = true;
     for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
       TcItem it;
-      if (!tc_item<MODE>(t, item, it)) break;
+      if (!tc_item<MODE, TT>(t, item, it)) break;
       if (!it.valid) continue;
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
-        const int s = kc % kTcStages;
-        const uint32_t ph = (kc / kTcStages) & 1;
+        const int s = kc % S;
+        const uint32_t ph = (kc / S) & 1;
         bool w = true;
         if (lane == 0) w = mbar_wait(&empty[s], ph ^ 1, abort_flag);
         if (!__shfl_sync(0xffffffffu, (int)w, 0)) {
@@ -336,40 +350,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           break;
         }
         if (lane == 0) {
-          uint8_t* st = smem + s * kTcStageBytes;
-          mbar_expect_tx(&full[s], Geo::kTxBytes);
+          uint8_t* st = smem + s * Geo::kStageBytes;
+          mbar_expect_tx(&full[s], Geo::kStageBytes);
           const int x = kb * 128;
           if (MODE == 0) {
             if (it.shared) {
               tma_load_2d(st, &maps.a_shared[0], &full[s], x, it.unit0);
-              tma_load_2d(st + 16384, &maps.a_shared[1], &full[s], x, it.unit0);
+              tma_load_2d(st + 8192, &maps.a_shared[1], &full[s], x, it.unit0);
             } else {
               tma_load_3d(st, &maps.a_routed[0], &full[s], x, it.unit0, it.slot);
-              tma_load_3d(st + 16384, &maps.a_routed[1], &full[s], x, it.unit0, it.slot);
+              tma_load_3d(st + 8192, &maps.a_routed[1], &full[s], x, it.unit0, it.slot);
             }
-            tma_load_2d(st + Geo::kABytes, &maps.b_routed[0], &full[s], x, it.brow0);
-            tma_load_2d(st + Geo::kABytes + Geo::kBSliceBytes, &maps.b_routed[1], &full[s], x, it.brow0);
           } else {
-            if (it.shared) {
+            if (it.shared)
               tma_load_2d(st, &maps.a_shared[0], &full[s], x, it.unit0);
-              tma_load_2d(st + Geo::kABytes, &maps.b_shared[0], &full[s], x, it.brow0);
-              tma_load_2d(st + Geo::kABytes + Geo::kBSliceBytes, &maps.b_shared[1], &full[s], x, it.brow0);
-            } else {
+            else
               tma_load_3d(st, &maps.a_routed[0], &full[s], x, it.unit0, it.slot);
-              tma_load_2d(st + Geo::kABytes, &maps.b_routed[0], &full[s], x, it.brow0);
-              tma_load_2d(st + Geo::kABytes + Geo::kBSliceBytes, &maps.b_routed[1], &full[s], x, it.brow0);
-            }
           }
+          const CUtensorMap* b = (MODE == 1 && it.shared) ? maps.b_shared : maps.b_routed;
+          tma_load_2d(st + Geo::kABytes, &b[0], &full[s], x, it.brow0);
+          tma_load_2d(st + Geo::kABytes + Geo::kBSliceBytes, &b[1], &full[s], x, it.brow0);
         }
         __syncwarp();
       }
     }
     if (!ok && lane == 0) {
       // aborted: let every stage this thread filled land before the CTA exits
-      for (int s = 0; s < kTcStages; ++s) {
+      for (int s = 0; s < S; ++s) {
         if (kc > (uint32_t)s) {
-          const uint32_t last = kc - 1 - ((kc - 1 - s) % kTcStages);
-          mbar_drain(&full[s], (last / kTcStages) & 1, 100000000ull);
+          const uint32_t last = kc - 1 - ((kc - 1 - s) % S);
+          mbar_drain(&full[s], (last / S) & 1, 100000000ull);
         }
       }
     }
@@ -380,7 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     bool ok = true;
     for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
       TcItem it;
-      if (!tc_item<MODE>(t, item, it)) break;
+      if (!tc_item<MODE, TT>(t, item, it)) break;
       if (!it.valid) continue;
       const int ab = ic & 1;
       const uint32_t aph = (ic >> 1) & 1;
@@ -388,11 +398,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       if (lane == 0) w = mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag);
       if (!__shfl_sync(0xffffffffu, (int)w, 0)) break;
       tc_fence_after();
-      const uint32_t d0 = tmem_base + ab * kTcAccCols;
-      const uint32_t idesc = idesc_i8(128, it.npad);
+      const uint32_t d = tmem_base + ab * kTcAccCols;
+      const uint32_t idesc = idesc_i8(128, TT + it.npad);
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
-        const int s = kc % kTcStages;
-        const uint32_t ph = (kc / kTcStages) & 1;
+        const int s = kc % S;
+        const uint32_t ph = (kc / S) & 1;
         if (lane == 0) w = mbar_wait(&full[s], ph, abort_flag);
         if (!__shfl_sync(0xffffffffu, (int)w, 0)) {
           ok = false;
@@ -400,27 +410,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t st = smem_u32(smem + s * kTcStageBytes);
+          const uint32_t st = smem_u32(smem + s * Geo::kStageBytes);
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
-            const uint64_t b0 = umma_desc_sw128(st + Geo::kABytes + ks * 32);
-            const uint64_t b1 = umma_desc_sw128(st + Geo::kABytes + Geo::kBSliceBytes + ks * 32);
-            const uint64_t a0 = umma_desc_sw128(st + ks * 32);
-            mma_i8(d0 + 0 * Geo::kTokTile, a0, b0, idesc, acc);
-            mma_i8(d0 + 1 * Geo::kTokTile, a0, b1, idesc, acc);
-            if (MODE == 0) {
-              const uint64_t a1 = umma_desc_sw128(st + 16384 + ks * 32);
-              mma_i8(d0 + 2 * Geo::kTokTile, a1, b0, idesc, acc);
-              mma_i8(d0 + 3 * Geo::kTokTile, a1, b1, idesc, acc);
-            }
-          }
+          for (int ks = 0; ks < 4; ++ks)
+            mma_i8(d, umma_desc_sw128(st + ks * 32), umma_desc_sw128(st + Geo::kABytes + ks * 32), idesc,
+                   (kb > 0 || ks > 0) ? 1u : 0u);
           umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
         }
         __syncwarp();
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&acc_full[ab]);  // accumulators ready for the epilogue
+      if (lane == 0) umma_commit(&acc_full[ab]);  // accumulator ready for the epilogue
       __syncwarp();
       ++ic;
     }
@@ -431,13 +431,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5, 128 threads = 128 TMEM lanes) ----------------
-    const int quad = warp & 3;              // TMEM lanes quad*32 .. +31 of this warp
-    const int r_local = quad * 32 + lane;   // weight row within the tile
-    uint32_t ic = 0;
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Warp w reads TMEM lanes 32*(w%4)..+31 and every other 16-token chunk
+    // (half = (w-2)/4). Mode 0: lanes 0..63 hold gate rows, 64..127 the up
+    // rows of the same columns; the up warp of each pair hands u to the gate
+    // warp through shared memory (named barrier per pair and half).
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int pair = quad & 1;
+    const bool up_warp = MODE == 0 && quad >= 2;
+    const int xpb = (pair * 2 + half) * 2;  // exchange barriers of this pair and half
+    uint32_t ic = 0, chunk = 0;
+    bool alive = true;
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
       TcItem it;
-      if (!tc_item<MODE>(t, item, it)) break;
+      if (!tc_item<MODE, TT>(t, item, it)) break;
       if (!it.valid) {
         if (threadIdx.x == 64) atomicOr(&t.plan_rw->error, 4);
         continue;
@@ -447,55 +455,75 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       const bool w = mbar_wait(&acc_full[ab], aph, abort_flag);
       if (!__all_sync(0xffffffffu, w)) break;
       tc_fence_after();
-      const int row = it.unit0 + r_local;
-      const bool row_ok = row < it.units;
+      // this thread's weight row: mode 0 -> intermediate column `col` of gate (or up);
+      // mode 1 -> hidden row
+      const int col = it.unit0 + (MODE == 0 ? pair * 32 + lane : quad * 32 + lane);
+      const bool row_ok = col < it.units;
       const uint8_t* rec = it.shared ? t.g.shared_record : reinterpret_cast<const uint8_t*>(t.g.expert_records[it.g]);
       const RecordGeom geo{ER_FMT_INT8, t.g.H, it.shared ? t.g.Is : t.g.I, 1};
-      float sw0 = 0.f, sw1 = 0.f;
-      if (row_ok) {
-        if (MODE == 0) {
-          sw0 = reinterpret_cast<const float*>(rec + geo.scale_offset(0))[row];
-          sw1 = reinterpret_cast<const float*>(rec + geo.scale_offset(1))[row];
-        } else {
-          sw0 = reinterpret_cast<const float*>(rec + geo.scale_offset(2))[row];
-        }
-      }
+      const int which = MODE == 0 ? (up_warp ? 1 : 0) : 2;
+      const float sw = row_ok ? reinterpret_cast<const float*>(rec + geo.scale_offset(which))[col] : 0.f;
       const uint32_t tbase = tmem_base + ab * kTcAccCols + ((uint32_t)(quad * 32) << 16);
-      const int inter = it.shared ? t.g.Is : t.g.I;
-      for (int c0 = 0; c0 < it.npad; c0 += 16) {
-        uint32_t v0[16], v1[16], v2[16], v3[16];
-        tmem_ld16(tbase + 0 * Geo::kTokTile + c0, v0);
-        tmem_ld16(tbase + 1 * Geo::kTokTile + c0, v1);
-        if (MODE == 0) {
-          tmem_ld16(tbase + 2 * Geo::kTokTile + c0, v2);
-          tmem_ld16(tbase + 3 * Geo::kTokTile + c0, v3);
+      const int ld_out = MODE == 0 ? (it.shared ? t.g.Is : t.g.I) : t.g.H;
+      float* out_base = it.shared ? t.out_s : t.out_r;
+      const int orow0 = (MODE == 0 && it.shared) ? it.tok0 : it.brow0;
+      const float* xsc = (MODE == 1 && it.shared) ? t.xscale_s : t.xscale_r;
+      const float* tokw = it.shared ? t.g.gate_sig : t.g.perm_w;
+      for (int c0 = half * 16; c0 < it.npad; c0 += 32, ++chunk) {
+        uint32_t v0[16], v1[16];
+        tmem_ld16(tbase + c0, v0);
+        tmem_ld16(tbase + TT + c0, v1);
+        float xs[16], tw[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int tk = c0 + j;
+          xs[j] = tk < it.nvalid ? __ldg(xsc + it.brow0 + tk) : 0.f;
+          if (MODE == 1) tw[j] = tk < it.nvalid ? __ldg(tokw + it.brow0 + tk) : 0.f;
         }
         tmem_ld_wait();
-        if (row_ok) {
+        float val[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int tk = c0 + j;
-            if (tk < it.nvalid) {
-              const int brow = it.brow0 + tk;
-              if (MODE == 0) {
-                const float xs = t.xscale_r[brow];
-                const float gv = ((float)(int)v0[j] + (float)(int)v1[j] * (1.f / 256.f)) * xs * sw0;
-                const float uv = ((float)(int)v2[j] + (float)(int)v3[j] * (1.f / 256.f)) * xs * sw1;
-                float* dst = it.shared ? t.out_s + (size_t)(it.tok0 + tk) * inter
-                                       : t.out_r + (size_t)brow * t.g.I;
-                dst[row] = silu_f(gv) * uv;
-              } else {
-                const float xs = it.shared ? t.xscale_s[brow] : t.xscale_r[brow];
-                const float yv = ((float)(int)v0[j] + (float)(int)v1[j] * (1.f / 256.f)) * xs * sw0;
-                if (it.shared)
-                  t.out_s[(size_t)brow * t.g.H + row] = yv * t.g.gate_sig[brow];
-                else
-                  t.out_r[(size_t)brow * t.g.H + row] = yv * t.g.perm_w[brow];
+        for (int j = 0; j < 16; ++j) val[j] = fmaf((float)(int)v1[j], 1.f / 256.f, (float)(int)v0[j]) * (xs[j] * sw);
+        if (MODE == 0) {
+          // hand u from the up warp to the gate warp of the pair: double-buffered,
+          // every wait bounded like the pipeline's
+          const int b = chunk & 1;
+          const uint32_t use_ph = (chunk >> 1) & 1;
+          float* xb = xch + (xpb + b) * (16 * 32);
+          if (up_warp) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&xempty[xpb + b], use_ph ^ 1, abort_flag))) {
+              alive = false;
+              break;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xb[j * 32 + lane] = val[j];
+            mbar_arrive(&xfull[xpb + b]);
+          } else {
+            if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xpb + b], use_ph, abort_flag))) {
+              alive = false;
+              break;
+            }
+            if (row_ok) {
+              float* dst = out_base + (size_t)(orow0 + c0) * ld_out + col;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (c0 + j < it.nvalid) {
+                  const float g = val[j], u = xb[j * 32 + lane];
+                  // SiLU(g) * u = g / (1 + e^-g) * u, with the fast exponential and reciprocal
+                  dst[(size_t)j * ld_out] = g * __frcp_rn(1.f + __expf(-g)) * u;
+                }
               }
             }
+            mbar_arrive(&xempty[xpb + b]);
           }
+        } else if (row_ok) {
+          float* dst = out_base + (size_t)(orow0 + c0) * ld_out + col;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < it.nvalid) dst[(size_t)j * ld_out] = val[j] * tw[j];
         }
       }
+      if (!alive) break;
       tc_fence_before();
       mbar_arrive(&acc_empty[ab]);
       ++ic;
@@ -549,18 +577,26 @@ static int make_map(CUtensorMap* m, const void* base, int rank, uint64_t k, uint
   return ER_OK;
 }
 
-template <int MODE>
+template <int MODE, int TT>
 static int configure_tc() {
   static int done_dev = -1;
   int dev = 0;
   if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
   if (done_dev == dev) return ER_OK;
-  if (int rc = cuda_check(cudaFuncSetAttribute(tc_expert_gemm_kernel<MODE>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem),
+  if (int rc = cuda_check(cudaFuncSetAttribute(tc_expert_gemm_kernel<MODE, TT>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)TcGeom<MODE, TT>::kSmem),
                           "tc smem attribute"))
     return rc;
   done_dev = dev;
   return ER_OK;
+}
+
+template <int MODE, int TT>
+static int launch_tc_mode(const TcMaps& maps, const TcArgs& t, int grid, cudaStream_t st) {
+  if (int rc = configure_tc<MODE, TT>()) return rc;
+  tc_expert_gemm_kernel<MODE, TT><<<grid, kTcThreads, TcGeom<MODE, TT>::kSmem, st>>>(maps, t);
+  return launch_check("tc_expert_gemm_kernel");
 }
 
 int launch_slice_rows(const void* src, int dtype, const int32_t* perm_token, int nk, int rows, int K, int src_mode,
@@ -578,41 +614,41 @@ int launch_slice_rows(const void* src, int dtype, const int32_t* perm_token, int
 
 int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
   const GroupArgs& a = L.g;
+  const int TT = L.tok_tile;
+  if (TT != 16 && TT != 128) return fail(ER_EINVAL, "tensor-core token tile %d (16 or 128)", TT);
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
   const RecordGeom rg{ER_FMT_INT8, a.H, a.I, 1};
   const RecordGeom sg{ER_FMT_INT8, a.H, a.Is, 1};
   const uint8_t* arena = static_cast<const uint8_t*>(L.arena);
   const uint8_t* shr = a.shared_record;
-  const int rows_b0 = L.nk + L.n;
   if (L.mode == 0) {
+    // 64 gate rows + the same 64 up rows per item
     if (int rc = make_map(&maps.a_routed[0], arena + rg.weight_offset(0), 3, a.H, a.I, L.arena_slots, a.H,
-                          L.record_bytes, 128, "gate"))
+                          L.record_bytes, 64, "gate"))
       return rc;
     if (int rc = make_map(&maps.a_routed[1], arena + rg.weight_offset(1), 3, a.H, a.I, L.arena_slots, a.H,
-                          L.record_bytes, 128, "up"))
+                          L.record_bytes, 64, "up"))
       return rc;
-    if (int rc = make_map(&maps.a_shared[0], shr + sg.weight_offset(0), 2, a.H, a.Is, 1, a.H, 0, 128, "shared gate"))
+    if (int rc = make_map(&maps.a_shared[0], shr + sg.weight_offset(0), 2, a.H, a.Is, 1, a.H, 0, 64, "shared gate"))
       return rc;
-    if (int rc = make_map(&maps.a_shared[1], shr + sg.weight_offset(1), 2, a.H, a.Is, 1, a.H, 0, 128, "shared up"))
+    if (int rc = make_map(&maps.a_shared[1], shr + sg.weight_offset(1), 2, a.H, a.Is, 1, a.H, 0, 64, "shared up"))
       return rc;
-    if (int rc = make_map(&maps.b_routed[0], L.b0_r, 2, a.H, rows_b0, 1, a.H, 0, TcGeom<0>::kTokTile, "x slice 0"))
-      return rc;
-    if (int rc = make_map(&maps.b_routed[1], L.b1_r, 2, a.H, rows_b0, 1, a.H, 0, TcGeom<0>::kTokTile, "x slice 1"))
-      return rc;
+    const int rows_b = L.nk + L.n;
+    if (int rc = make_map(&maps.b_routed[0], L.b0_r, 2, a.H, rows_b, 1, a.H, 0, TT, "x slice 0")) return rc;
+    if (int rc = make_map(&maps.b_routed[1], L.b1_r, 2, a.H, rows_b, 1, a.H, 0, TT, "x slice 1")) return rc;
   } else {
     if (int rc = make_map(&maps.a_routed[0], arena + rg.weight_offset(2), 3, a.I, a.H, L.arena_slots, a.I,
                           L.record_bytes, 128, "down"))
       return rc;
     if (int rc = make_map(&maps.a_shared[0], shr + sg.weight_offset(2), 2, a.Is, a.H, 1, a.Is, 0, 128, "shared down"))
       return rc;
-    const int tt = TcGeom<1>::kTokTile;
     if (L.nk > 0) {
-      if (int rc = make_map(&maps.b_routed[0], L.b0_r, 2, a.I, L.nk, 1, a.I, 0, tt, "act slice 0")) return rc;
-      if (int rc = make_map(&maps.b_routed[1], L.b1_r, 2, a.I, L.nk, 1, a.I, 0, tt, "act slice 1")) return rc;
+      if (int rc = make_map(&maps.b_routed[0], L.b0_r, 2, a.I, L.nk, 1, a.I, 0, TT, "act slice 0")) return rc;
+      if (int rc = make_map(&maps.b_routed[1], L.b1_r, 2, a.I, L.nk, 1, a.I, 0, TT, "act slice 1")) return rc;
     }
-    if (int rc = make_map(&maps.b_shared[0], L.b0_s, 2, a.Is, L.n, 1, a.Is, 0, tt, "shared act slice 0")) return rc;
-    if (int rc = make_map(&maps.b_shared[1], L.b1_s, 2, a.Is, L.n, 1, a.Is, 0, tt, "shared act slice 1")) return rc;
+    if (int rc = make_map(&maps.b_shared[0], L.b0_s, 2, a.Is, L.n, 1, a.Is, 0, TT, "shared act slice 0")) return rc;
+    if (int rc = make_map(&maps.b_shared[1], L.b1_s, 2, a.Is, L.n, 1, a.Is, 0, TT, "shared act slice 1")) return rc;
   }
   TcArgs t;
   t.g = a;
@@ -628,14 +664,8 @@ int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
   int sms = 148;
   if (int rc = er_device_sm_count(&sms)) return rc;
   const int grid = (int)(L.items_bound < sms ? (L.items_bound > 0 ? L.items_bound : 1) : sms);
-  if (L.mode == 0) {
-    if (int rc = configure_tc<0>()) return rc;
-    tc_expert_gemm_kernel<0><<<grid, kTcThreads, kTcSmem, st>>>(maps, t);
-  } else {
-    if (int rc = configure_tc<1>()) return rc;
-    tc_expert_gemm_kernel<1><<<grid, kTcThreads, kTcSmem, st>>>(maps, t);
-  }
-  return launch_check("tc_expert_gemm_kernel");
+  if (L.mode == 0) return TT == 16 ? launch_tc_mode<0, 16>(maps, t, grid, st) : launch_tc_mode<0, 128>(maps, t, grid, st);
+  return TT == 16 ? launch_tc_mode<1, 16>(maps, t, grid, st) : launch_tc_mode<1, 128>(maps, t, grid, st);
 }
 
 }  // namespace er
