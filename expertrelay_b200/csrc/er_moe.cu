@@ -227,6 +227,7 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.nk = (int)nk;
     tl.n = n;
     tl.tok_tile = tc_tok_tile(n);
+    // slices of h (and the act row maxima cleared for the gate/up epilogue)
     if (int rc = launch_slice_rows(io->h, io->h_dtype, perm_token, (int)nk, (int)nk + n, H, 0, xs0, xs1, xscale, st))
       return rc;
     tl.mode = 0;

@@ -12,7 +12,14 @@
 namespace er {
 
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanWarps = kPlanThreads / 32;
 
+// One CTA. Warp w owns the contiguous entries [w * span, (w + 1) * span) of the
+// row-major (token, slot) list. (1) each warp counts its entries per expert;
+// (2) per expert, an exclusive prefix over the warps; per-expert offsets and
+// the work-item schedules; (3) each warp walks its entries again and places
+// entry i at offsets[e] + (entries of e in earlier warps) + (earlier entries
+// of e in this warp): the same stable order as np.nonzero per expert.
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __restrict__ idx,
                                                             const float* __restrict__ w, int n, int k, int E,
                                                             int H, int I, int Is, SchedSpec s0, SchedSpec s1,
@@ -20,29 +27,69 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
                                                             int32_t* __restrict__ perm_token,
                                                             float* __restrict__ perm_w,
                                                             int32_t* __restrict__ pos_of) {
+  __shared__ int cnt[kPlanWarps][kMaxExperts];  // per-warp counts, then running bases
   __shared__ int hist[kMaxExperts];
   __shared__ int base[kMaxExperts];
-  __shared__ int chunk_total[kMaxExperts];
-  __shared__ int wcount[kPlanThreads / 32][kMaxExperts];
+  __shared__ int act[kMaxExperts + 1];
   __shared__ int bad;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nk = n * k;
-  for (int e = tid; e < kMaxExperts; e += kPlanThreads) hist[e] = 0;
+  const int span = (nk + kPlanWarps * 32 - 1) / (kPlanWarps * 32) * 32;
+  const int beg = warp * span, end = min(nk, beg + span);
+  for (int i = tid; i < kPlanWarps * kMaxExperts; i += kPlanThreads) cnt[i / kMaxExperts][i % kMaxExperts] = 0;
   if (tid == 0) bad = 0;
   __syncthreads();
-  // warp-aggregated histogram: one shared-memory atomic per distinct expert per warp
-  for (int i0 = 0; i0 < nk; i0 += kPlanThreads) {
-    const int i = i0 + tid;
-    int e = i < nk ? idx[i] : -1;
-    if (i < nk && (e < 0 || e >= E)) {
+  for (int i0 = beg; i0 < end; i0 += 32) {
+    const int i = i0 + lane;
+    int e = i < end ? idx[i] : -1;
+    if (i < end && (e < 0 || e >= E)) {
       bad = 1;
       e = -1;
     }
     const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && (__ffs(peers) - 1) == lane) atomicAdd(&hist[e], __popc(peers));
+    if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kPlanThreads) {
+    int run = 0;
+    for (int w2 = 0; w2 < kPlanWarps; ++w2) {
+      const int c = cnt[w2][e];
+      cnt[w2][e] = run;
+      run += c;
+    }
+    hist[e] = run;
   }
   __syncthreads();
   if (tid == 0) {
+    // reads only shared memory: no read-back of the global plan being written
+    int off = 0, na = 0;
+    for (int e = 0; e < E; ++e) {
+      base[e] = off;
+      off += hist[e];
+      if (hist[e] > 0) {
+        plan->active[na] = e;
+        act[na++] = e;
+      }
+    }
+    if (n > 0) {
+      plan->active[na] = E;
+      act[na++] = E;
+    }
+    const SchedSpec specs[kNumSched] = {s0, s1};
+    for (int s = 0; s < kNumSched; ++s) {
+      const SchedSpec sp = specs[s];
+      int acc = 0;
+      for (int a = 0; a < na; ++a) {
+        plan->item_start[s][a] = bad ? 0 : acc;
+        const int g = act[a];
+        const int rows = g == E ? n : hist[g];
+        const int units = sp.which == 0 ? (g == E ? Is : I) : H;
+        const int mt = sp.bm > 0 ? (rows + sp.bm - 1) / sp.bm : 1;
+        const int nt = (units + sp.bn - 1) / sp.bn;
+        acc += mt * nt;
+      }
+      plan->item_start[s][na] = bad ? 0 : acc;
+    }
     plan->n = n;
     plan->E = E;
     plan->k = k;
@@ -50,70 +97,31 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
     plan->error = bad;
     plan->sched[0] = s0;
     plan->sched[1] = s1;
-    int off = 0, na = 0;
-    for (int e = 0; e < E; ++e) {
-      plan->counts[e] = hist[e];
-      plan->offsets[e] = off;
-      base[e] = off;
-      off += hist[e];
-      if (hist[e] > 0) plan->active[na++] = e;
-    }
-    plan->counts[E] = n;
-    plan->offsets[E] = 0;
-    if (n > 0) plan->active[na++] = E;
-    plan->num_active = na;
-    const SchedSpec specs[kNumSched] = {s0, s1};
-    for (int s = 0; s < kNumSched; ++s) {
-      const SchedSpec sp = specs[s];
-      int acc = 0;
-      for (int a = 0; a < na; ++a) {
-        plan->item_start[s][a] = acc;
-        const int g = plan->active[a];
-        const int rows = plan->counts[g];
-        const int units = sp.which == 0 ? (g == E ? Is : I) : H;
-        const int mt = sp.bm > 0 ? (rows + sp.bm - 1) / sp.bm : 1;
-        const int nt = (units + sp.bn - 1) / sp.bn;
-        acc += mt * nt;
-      }
-      plan->item_start[s][na] = acc;
-    }
-    if (bad) {  // no work items: nothing downstream may read the unfilled permutation
-      plan->num_active = 0;
-      for (int s = 0; s < kNumSched; ++s) plan->item_start[s][0] = 0;
-    }
+    // no work items at all when an expert id was out of range: nothing
+    // downstream may read the unfilled permutation
+    plan->num_active = bad ? 0 : na;
   }
   __syncthreads();
+  for (int e = tid; e <= E; e += kPlanThreads) {
+    plan->counts[e] = e < E ? hist[e] : n;
+    plan->offsets[e] = e < E ? base[e] : 0;
+  }
   if (bad) return;
-  // stable expert-sorted positions, one chunk of kPlanThreads pairs at a time
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int c0 = 0; c0 < nk; c0 += kPlanThreads) {
-    const int i = c0 + tid;
-    const int e = (i < nk) ? idx[i] : -1;
-    for (int x = lane; x < E; x += 32) wcount[warp][x] = 0;
-    __syncthreads();
+  for (int i0 = beg; i0 < end; i0 += 32) {
+    const int i = i0 + lane;
+    const int e = i < end ? idx[i] : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(peers & lt_mask);
-    if (e >= 0 && rank == 0) wcount[warp][e] = __popc(peers);
-    __syncthreads();
-    for (int x = tid; x < E; x += kPlanThreads) {  // exclusive prefix over warps
-      int run = 0;
-      for (int w2 = 0; w2 < kPlanThreads / 32; ++w2) {
-        const int c = wcount[w2][x];
-        wcount[w2][x] = run;
-        run += c;
-      }
-      chunk_total[x] = run;
-    }
-    __syncthreads();
+    int p = 0;
+    if (e >= 0) p = base[e] + cnt[warp][e] + __popc(peers & lt_mask);
+    __syncwarp();
+    if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
+    __syncwarp();
     if (e >= 0) {
-      const int p = base[e] + wcount[warp][e] + rank;
       perm_token[p] = i / k;
       perm_w[p] = w[i];
       pos_of[i] = p;
     }
-    __syncthreads();
-    for (int x = tid; x < E; x += kPlanThreads) base[x] += chunk_total[x];
-    __syncthreads();
   }
 }
 

@@ -58,65 +58,95 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const XT* __restrict__
 }
 
 // Large batches: a tiled fp32 GEMM, 32 tokens x 64 rows of [W_r; w_g] per
-// CTA (rows past E + 1 are zero), K in steps of 32 through shared memory;
-// each thread owns 2 tokens x 4 rows.
+// CTA (rows past E + 1 are zero). The 256 threads form four K-groups of 64
+// that each walk a quarter of K through shared memory; a thread owns 4 tokens
+// x 8 rows (32 accumulators, three shared-memory vector loads per 32 FMAs).
+// The four partial sums are added in a fixed order.
 template <typename XT>
 __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__ h, int n, int H,
-                                                          const float* __restrict__ wr, const float* __restrict__ wg,
-                                                          int E, float* __restrict__ logits,
+                                                          const float* __restrict__ wr,
+                                                          const float* __restrict__ wg, int E,
+                                                          float* __restrict__ logits,
                                                           float* __restrict__ gate_logit) {
-  constexpr int BM = 32, BN = 64, BK = 32;
-  __shared__ __align__(16) float As[BK][BM + 4];
-  __shared__ __align__(16) float Bs[BK][BN + 4];
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  constexpr int BM = 32, BN = 64, BK = 16, KG = 4;
+  struct Tiles {
+    float A[KG][BK][BM + 4];
+    float B[KG][BK][BN + 4];
+  };
+  __shared__ __align__(16) union {
+    Tiles t;
+    float red[KG - 1][BM][BN];
+  } sm;
+  const int kg = threadIdx.x >> 6, tid = threadIdx.x & 63;
+  const int tx = tid & 7, ty = tid >> 3;  // rows 8tx..8tx+7, tokens 4ty..4ty+3
   const int m0 = blockIdx.x * BM;
   const int rows = E + 1;
-  float acc[2][4] = {};
-  for (int k0 = 0; k0 < H; k0 += BK) {
-    {  // A: 32 tokens x 32 k, one float4 per thread
-      const int r = tid >> 3, kk = (tid & 7) * 4;
+  const int kspan = (H + KG - 1) / KG;
+  const int kbeg = kg * kspan, kend = min(H, kbeg + kspan);
+  const int iters = (kspan + BK - 1) / BK;  // the same for every K-group (barriers inside)
+  float acc[4][8] = {};
+  for (int it = 0; it < iters; ++it) {
+    const int k0 = kbeg + it * BK;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {  // A: 32 tokens x 16 k = 128 float4
+      const int v4 = tid + 64 * q;
+      const int r = v4 >> 2, kk = (v4 & 3) * 4;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m0 + r < n && k0 + kk < H) v = load4(h + (size_t)(m0 + r) * H + k0 + kk);
-      As[kk + 0][r] = v.x;
-      As[kk + 1][r] = v.y;
-      As[kk + 2][r] = v.z;
-      As[kk + 3][r] = v.w;
+      if (m0 + r < n && k0 + kk < kend) v = load4(h + (size_t)(m0 + r) * H + k0 + kk);
+      sm.t.A[kg][kk + 0][r] = v.x;
+      sm.t.A[kg][kk + 1][r] = v.y;
+      sm.t.A[kg][kk + 2][r] = v.z;
+      sm.t.A[kg][kk + 3][r] = v.w;
     }
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {  // B: 64 rows x 32 k, two float4 per thread
-      const int q = tid + 256 * i;
-      const int r = q >> 3, kk = (q & 7) * 4;
+    for (int q = 0; q < 4; ++q) {  // B: 64 rows x 16 k = 256 float4
+      const int v4 = tid + 64 * q;
+      const int r = v4 >> 2, kk = (v4 & 3) * 4;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < rows && k0 + kk < H) v = *reinterpret_cast<const float4*>((r < E ? wr + (size_t)r * H : wg) + k0 + kk);
-      Bs[kk + 0][r] = v.x;
-      Bs[kk + 1][r] = v.y;
-      Bs[kk + 2][r] = v.z;
-      Bs[kk + 3][r] = v.w;
+      if (r < rows && k0 + kk < kend)
+        v = *reinterpret_cast<const float4*>((r < E ? wr + (size_t)r * H : wg) + k0 + kk);
+      sm.t.B[kg][kk + 0][r] = v.x;
+      sm.t.B[kg][kk + 1][r] = v.y;
+      sm.t.B[kg][kk + 2][r] = v.z;
+      sm.t.B[kg][kk + 3][r] = v.w;
     }
     __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
-      const float2 a = *reinterpret_cast<const float2*>(&As[kk][ty * 2]);
-      const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
-      const float av[2] = {a.x, a.y}, bv[4] = {b.x, b.y, b.z, b.w};
+      const float4 a = *reinterpret_cast<const float4*>(&sm.t.A[kg][kk][ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&sm.t.B[kg][kk][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&sm.t.B[kg][kk][tx * 8 + 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
   }
+  if (kg > 0) {
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int t = m0 + ty * 2 + i;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sm.red[kg - 1][ty * 4 + i][tx * 8 + j] = acc[i][j];
+  }
+  __syncthreads();
+  if (kg != 0) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = m0 + ty * 4 + i;
     if (t >= n) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = tx * 4 + j;
+    for (int j = 0; j < 8; ++j) {
+      const int r = tx * 8 + j;
+      float v = acc[i][j];
+#pragma unroll
+      for (int g = 0; g < KG - 1; ++g) v += sm.red[g][ty * 4 + i][r];
       if (r < E)
-        logits[(size_t)t * E + r] = acc[i][j];
+        logits[(size_t)t * E + r] = v;
       else if (r == E && gate_logit)
-        gate_logit[t] = acc[i][j];
+        gate_logit[t] = v;
     }
   }
 }
@@ -224,7 +254,7 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
   const int grid = (n + 31) / 32;
   if (h_dtype == ER_DTYPE_BF16)
     router_gemm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
-                                                            gate_logit);
+                                                             gate_logit);
   else
     router_gemm_kernel<float><<<grid, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit);
   return launch_check("router_gemm_kernel");

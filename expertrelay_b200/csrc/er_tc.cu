@@ -88,6 +88,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
   }
 }
+// One lane polls, the whole warp learns the outcome; the warp then syncs so
+// every lane's later accesses are ordered after the acquire.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int lane) {
+  bool w = true;
+  if (lane == 0) w = mbar_wait(bar, parity, abort_flag);
+  w = __shfl_sync(0xffffffffu, (int)w, 0) != 0;
+  __syncwarp();
+  return w;
+}
 // Bounded wait used while draining after an abort (no abort check).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned long long ns) {
   const unsigned long long t0 = globaltimer();
@@ -152,12 +161,14 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 
 // One warp per output row: s = max|x| / 127, x0 = rint(x/s), x1 = rint((x/s - x0) * 256)
 // clamped to +-127. src_mode 0: row p < nk is h[perm_token[p]], row nk + t is
-// h[t]; src_mode 1: row p is src[p] (contiguous rows of width K).
+// h[t]; src_mode 1: row p is src[p] (width K). Rows of up to 2048 values are
+// held in registers and read once; longer rows are read twice (max, then slices).
 template <typename XT>
 __global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ src, const int32_t* __restrict__ perm_token,
                                                          int nk, int rows, int K, int src_mode,
                                                          int8_t* __restrict__ s0, int8_t* __restrict__ s1,
                                                          float* __restrict__ scale) {
+  constexpr int kRegVec = 16;  // float4 per lane held in registers: K <= 2048
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -166,6 +177,44 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ 
     x = src + (size_t)(row < nk ? perm_token[row] : row - nk) * K;
   else
     x = src + (size_t)row * K;
+  int8_t* d0 = s0 + (size_t)row * K;
+  int8_t* d1 = s1 + (size_t)row * K;
+  auto emit = [&](int k, float4 v, float inv) {
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    int i0[4], i1[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float y = f[j] * inv;
+      const float q0 = rintf(y);
+      i0[j] = (int)q0;
+      i1[j] = max(-127, min(127, __float2int_rn((y - q0) * 256.f)));
+    }
+    // pack the low bytes of four ints (first in the lowest byte)
+    const uint32_t w0 = __byte_perm(__byte_perm(i0[0], i0[1], 0x0040), __byte_perm(i0[2], i0[3], 0x0040), 0x5410);
+    const uint32_t w1 = __byte_perm(__byte_perm(i1[0], i1[1], 0x0040), __byte_perm(i1[2], i1[3], 0x0040), 0x5410);
+    *reinterpret_cast<uint32_t*>(d0 + k) = w0;
+    *reinterpret_cast<uint32_t*>(d1 + k) = w1;
+  };
+  if (K <= 128 * kRegVec) {
+    float4 v[kRegVec];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRegVec; ++i) {
+      const int k = lane * 4 + 128 * i;
+      v[i] = k < K ? load4(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+#pragma unroll
+    for (int i = 0; i < kRegVec; ++i) {
+      const int k = lane * 4 + 128 * i;
+      if (k < K) emit(k, v[i], inv);
+    }
+    if (lane == 0) scale[row] = amax / 127.f;
+    return;
+  }
   float amax = 0.f;
   for (int k = lane * 4; k < K; k += 128) {
     const float4 v = load4(x + k);
@@ -173,26 +222,9 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ 
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float s = amax / 127.f;
   const float inv = amax > 0.f ? 127.f / amax : 0.f;
-  int8_t* d0 = s0 + (size_t)row * K;
-  int8_t* d1 = s1 + (size_t)row * K;
-  for (int k = lane * 4; k < K; k += 128) {
-    const float4 v = load4(x + k);
-    const float f[4] = {v.x, v.y, v.z, v.w};
-    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float y = f[j] * inv;
-      const float q0 = rintf(y);
-      const float q1 = fminf(fmaxf(rintf((y - q0) * 256.f), -127.f), 127.f);
-      w0 |= (uint32_t)((int)q0 & 0xff) << (8 * j);
-      w1 |= (uint32_t)((int)q1 & 0xff) << (8 * j);
-    }
-    *reinterpret_cast<uint32_t*>(d0 + k) = w0;
-    *reinterpret_cast<uint32_t*>(d1 + k) = w1;
-  }
-  if (lane == 0) scale[row] = s;
+  for (int k = lane * 4; k < K; k += 128) emit(k, load4(x + k), inv);
+  if (lane == 0) scale[row] = amax / 127.f;
 }
 
 // ---------------------------------------------------------------------------
@@ -297,8 +329,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
-  uint64_t* xfull = drain_bar + 1;   // [pair*2 + half][buffer]: u values written (32 arrivals)
-  uint64_t* xempty = xfull + 8;      // [pair*2 + half][buffer]: u values consumed (32 arrivals)
+  uint64_t* xfull = drain_bar + 1;   // [pair*2 + half][buffer]: u values written
+  uint64_t* xempty = xfull + 8;      // [pair*2 + half][buffer]: u values consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -310,12 +342,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kTcEpiWarps * 32);
+      mbar_init(&acc_empty[b], kTcEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(drain_bar, 1);
     for (int i = 0; i < 8; ++i) {
-      mbar_init(&xfull[i], 32);
-      mbar_init(&xempty[i], 32);
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], 1);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -452,8 +484,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       }
       const int ab = ic & 1;
       const uint32_t aph = (ic >> 1) & 1;
-      const bool w = mbar_wait(&acc_full[ab], aph, abort_flag);
-      if (!__all_sync(0xffffffffu, w)) break;
+      if (!warp_wait(&acc_full[ab], aph, abort_flag, lane)) break;
       tc_fence_after();
       // this thread's weight row: mode 0 -> intermediate column `col` of gate (or up);
       // mode 1 -> hidden row
@@ -491,30 +522,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           const uint32_t use_ph = (chunk >> 1) & 1;
           float* xb = xch + (xpb + b) * (16 * 32);
           if (up_warp) {
-            if (!__all_sync(0xffffffffu, mbar_wait(&xempty[xpb + b], use_ph ^ 1, abort_flag))) {
+            if (!warp_wait(&xempty[xpb + b], use_ph ^ 1, abort_flag, lane)) {
               alive = false;
               break;
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) xb[j * 32 + lane] = val[j];
-            mbar_arrive(&xfull[xpb + b]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xfull[xpb + b]);
           } else {
-            if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xpb + b], use_ph, abort_flag))) {
+            if (!warp_wait(&xfull[xpb + b], use_ph, abort_flag, lane)) {
               alive = false;
               break;
             }
+            float act[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float g = val[j], u = xb[j * 32 + lane];
+              // SiLU(g) * u = g / (1 + e^-g) * u, with the fast exponential and reciprocal
+              act[j] = row_ok ? g * __frcp_rn(1.f + __expf(-g)) * u : 0.f;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xempty[xpb + b]);
             if (row_ok) {
               float* dst = out_base + (size_t)(orow0 + c0) * ld_out + col;
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                if (c0 + j < it.nvalid) {
-                  const float g = val[j], u = xb[j * 32 + lane];
-                  // SiLU(g) * u = g / (1 + e^-g) * u, with the fast exponential and reciprocal
-                  dst[(size_t)j * ld_out] = g * __frcp_rn(1.f + __expf(-g)) * u;
-                }
-              }
+              for (int j = 0; j < 16; ++j)
+                if (c0 + j < it.nvalid) dst[(size_t)j * ld_out] = act[j];
             }
-            mbar_arrive(&xempty[xpb + b]);
           }
         } else if (row_ok) {
           float* dst = out_base + (size_t)(orow0 + c0) * ld_out + col;
@@ -525,7 +560,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       }
       if (!alive) break;
       tc_fence_before();
-      mbar_arrive(&acc_empty[ab]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
       ++ic;
     }
   }
