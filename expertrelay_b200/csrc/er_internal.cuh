@@ -77,10 +77,16 @@ __device__ __forceinline__ int find_item(const Plan* P, int s, int item, int* lo
 }
 
 // launchers (each returns an ER_* status)
+// Router logits; large batches write kRouterKSplit partial sums (K slices)
+// into logits / gate_logit (each n*E / n apart), *nparts says how many.
+constexpr int kRouterKSplit = 4;
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
-                         float* logits, float* gate_logit, cudaStream_t st);
-int launch_router_topk(const float* logits, int n, int E, int k, int norm, int64_t* idx64, int32_t* idx32,
-                       float* wout, const float* gate_logit, float* gate_sig, cudaStream_t st);
+                         float* logits, float* gate_logit, int* nparts, cudaStream_t st);
+// softmax + top-k over the sum of `nparts` partial logits (and `gparts` partial
+// shared-gate logits); logits_sum (optional) receives the summed logits
+int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
+                       int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
+                       cudaStream_t st);
 int launch_plan(const int32_t* idx, const float* w, int n, int k, int E, int H, int I, int Is,
                 const SchedSpec* specs, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of,
                 cudaStream_t st);

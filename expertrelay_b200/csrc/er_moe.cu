@@ -25,8 +25,8 @@ static WsLayout ws_layout(const er_moe_weights* w, int n, int path) {
     return o;
   };
   const size_t nk = (size_t)n * w->top_k;
-  L.logits = take((size_t)n * w->num_experts * 4);
-  L.gate_logit = take((size_t)n * 4);
+  L.logits = take((size_t)kRouterKSplit * n * w->num_experts * 4);  // partial sums of K slices
+  L.gate_logit = take((size_t)kRouterKSplit * n * 4);
   L.gate_sig = take((size_t)n * 4);
   L.idx32 = take(nk * 4);
   L.topw = take(nk * 4);
@@ -124,11 +124,13 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   int launches = 0;
   auto mark = [&](int i) -> int {
     if (!io->stage_events) return ER_OK;
-    return cuda_check(cudaEventRecord((cudaEvent_t)io->stage_events[i], st), "cudaEventRecord");
+    // external record: also timestamps when the call is captured into a CUDA graph
+    return cuda_check(cudaEventRecordWithFlags((cudaEvent_t)io->stage_events[i], st, cudaEventRecordExternal),
+                      "cudaEventRecord");
   };
   if (int rc = mark(0)) return rc;
   const int H = w->hidden, E = w->num_experts, k = w->top_k;
-  float* logits = io->logits_out ? io->logits_out : reinterpret_cast<float*>(ws + L.logits);
+  float* logits = reinterpret_cast<float*>(ws + L.logits);
   float* gate_logit = reinterpret_cast<float*>(ws + L.gate_logit);
   float* gate_sig = reinterpret_cast<float*>(ws + L.gate_sig);
   int32_t* idx32 = reinterpret_cast<int32_t*>(ws + L.idx32);
@@ -144,23 +146,22 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
 
   // K1: router (or only the shared-gate row when the caller supplies logits)
   const float* lg = logits;
+  int nparts = 1, gparts = 1;
+  float* logits_sum = io->logits_out;
   if (io->logits_in) {
-    if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit, st))
+    if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit,
+                                      &gparts, st))
       return rc;
-    lg = io->logits_in;
-    if (io->logits_out && io->logits_out != io->logits_in) {
-      if (int rc = cuda_check(cudaMemcpyAsync(io->logits_out, io->logits_in, (size_t)n * E * 4,
-                                              cudaMemcpyDeviceToDevice, st),
-                              "copy logits"))
-        return rc;
-    }
+    lg = io->logits_in;  // one whole set of logits
+    if (logits_sum == io->logits_in) logits_sum = nullptr;
   } else {
     if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, w->router_w, w->shared_gate_w, E, logits, gate_logit,
-                                      st))
+                                      &nparts, st))
       return rc;
+    gparts = nparts;
   }
-  if (int rc = launch_router_topk(lg, n, E, k, w->norm_topk_prob, io->topk_idx_out, idx32, topw, gate_logit, gate_sig,
-                                  st))
+  if (int rc = launch_router_topk(lg, nparts, gparts, n, E, k, w->norm_topk_prob, io->topk_idx_out, idx32, topw,
+                                  gate_logit, gate_sig, logits_sum, st))
     return rc;
   launches += 2;
   if (io->topk_w_out) {

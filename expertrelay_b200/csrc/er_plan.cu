@@ -39,15 +39,28 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
   for (int i = tid; i < kPlanWarps * kMaxExperts; i += kPlanThreads) cnt[i / kMaxExperts][i % kMaxExperts] = 0;
   if (tid == 0) bad = 0;
   __syncthreads();
-  for (int i0 = beg; i0 < end; i0 += 32) {
-    const int i = i0 + lane;
-    int e = i < end ? idx[i] : -1;
-    if (i < end && (e < 0 || e >= E)) {
-      bad = 1;
-      e = -1;
+  // the warp's entries are fetched kBatch rows of 32 at a time with independent
+  // loads, so a batch costs one memory round trip
+  constexpr int kBatch = 16;
+  for (int b0 = beg; b0 < end; b0 += 32 * kBatch) {
+    int ev[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = b0 + 32 * j + lane;
+      ev[j] = i < end ? __ldg(idx + i) : -1;
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = b0 + 32 * j + lane;
+      int e = ev[j];
+      if (i < end && (e < 0 || e >= E)) {
+        bad = 1;
+        e = -1;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
+      __syncwarp();
+    }
   }
   __syncthreads();
   for (int e = tid; e < E; e += kPlanThreads) {
@@ -60,46 +73,81 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
     hist[e] = run;
   }
   __syncthreads();
-  if (tid == 0) {
-    // reads only shared memory: no read-back of the global plan being written
-    int off = 0, na = 0;
-    for (int e = 0; e < E; ++e) {
-      base[e] = off;
-      off += hist[e];
-      if (hist[e] > 0) {
-        plan->active[na] = e;
-        act[na++] = e;
+  if (warp == 0) {
+    // Warp 0 builds the offsets, the active list and the schedules with
+    // warp scans (lane l owns entries 9l .. 9l+8, enough for E + 2 <= 258).
+    constexpr int kPer = 9;
+    auto warp_excl_scan = [&](int v) {  // exclusive prefix of v over the lanes; also returns the total
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      return incl - v;
+    };
+    int sum = 0, nact = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane * kPer + j;
+      if (e < E) {
+        sum += hist[e];
+        nact += hist[e] > 0;
       }
     }
-    if (n > 0) {
-      plan->active[na] = E;
-      act[na++] = E;
+    int off = warp_excl_scan(sum), pos = warp_excl_scan(nact);
+    const int na_routed = __shfl_sync(0xffffffffu, pos + nact, 31);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane * kPer + j;
+      if (e < E) {
+        base[e] = off;
+        off += hist[e];
+        if (hist[e] > 0) act[pos++] = e;
+      }
     }
+    const int na = na_routed + (n > 0 ? 1 : 0);
+    if (lane == 0 && n > 0) act[na_routed] = E;
+    __syncwarp();
+    for (int a = lane; a < na; a += 32) plan->active[a] = act[a];
     const SchedSpec specs[kNumSched] = {s0, s1};
+#pragma unroll
     for (int s = 0; s < kNumSched; ++s) {
       const SchedSpec sp = specs[s];
-      int acc = 0;
-      for (int a = 0; a < na; ++a) {
-        plan->item_start[s][a] = bad ? 0 : acc;
-        const int g = act[a];
-        const int rows = g == E ? n : hist[g];
-        const int units = sp.which == 0 ? (g == E ? Is : I) : H;
-        const int mt = sp.bm > 0 ? (rows + sp.bm - 1) / sp.bm : 1;
-        const int nt = (units + sp.bn - 1) / sp.bn;
-        acc += mt * nt;
+      int items[kPer], local = 0;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int a = lane * kPer + j;
+        items[j] = 0;
+        if (a < na) {
+          const int g = act[a];
+          const int rows = g == E ? n : hist[g];
+          const int units = sp.which == 0 ? (g == E ? Is : I) : H;
+          const int mt = sp.bm > 0 ? (rows + sp.bm - 1) / sp.bm : 1;
+          items[j] = mt * ((units + sp.bn - 1) / sp.bn);
+        }
+        local += items[j];
       }
-      plan->item_start[s][na] = bad ? 0 : acc;
+      int start_a = warp_excl_scan(local);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int a = lane * kPer + j;
+        if (a <= na) plan->item_start[s][a] = bad ? 0 : start_a;
+        start_a += items[j];
+      }
     }
-    plan->n = n;
-    plan->E = E;
-    plan->k = k;
-    plan->nk = nk;
-    plan->error = bad;
-    plan->sched[0] = s0;
-    plan->sched[1] = s1;
-    // no work items at all when an expert id was out of range: nothing
-    // downstream may read the unfilled permutation
-    plan->num_active = bad ? 0 : na;
+    if (lane == 0) {
+      plan->n = n;
+      plan->E = E;
+      plan->k = k;
+      plan->nk = nk;
+      plan->error = bad;
+      plan->sched[0] = s0;
+      plan->sched[1] = s1;
+      // no work items at all when an expert id was out of range: nothing
+      // downstream may read the unfilled permutation
+      plan->num_active = bad ? 0 : na;
+    }
   }
   __syncthreads();
   for (int e = tid; e <= E; e += kPlanThreads) {
@@ -108,19 +156,30 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
   }
   if (bad) return;
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int i0 = beg; i0 < end; i0 += 32) {
-    const int i = i0 + lane;
-    const int e = i < end ? idx[i] : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    int p = 0;
-    if (e >= 0) p = base[e] + cnt[warp][e] + __popc(peers & lt_mask);
-    __syncwarp();
-    if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
-    __syncwarp();
-    if (e >= 0) {
-      perm_token[p] = i / k;
-      perm_w[p] = w[i];
-      pos_of[i] = p;
+  for (int b0 = beg; b0 < end; b0 += 32 * kBatch) {
+    int ev[kBatch];
+    float wv[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = b0 + 32 * j + lane;
+      ev[j] = i < end ? __ldg(idx + i) : -1;
+      wv[j] = i < end ? __ldg(w + i) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = b0 + 32 * j + lane;
+      const int e = ev[j];
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      int p = 0;
+      if (e >= 0) p = base[e] + cnt[warp][e] + __popc(peers & lt_mask);
+      __syncwarp();
+      if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
+      __syncwarp();
+      if (e >= 0) {
+        perm_token[p] = i / k;
+        perm_w[p] = wv[j];
+        pos_of[i] = p;
+      }
     }
   }
 }

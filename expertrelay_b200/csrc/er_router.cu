@@ -58,10 +58,12 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const XT* __restrict__
 }
 
 // Large batches: a tiled fp32 GEMM, 32 tokens x 64 rows of [W_r; w_g] per
-// CTA (rows past E + 1 are zero). The 256 threads form four K-groups of 64
-// that each walk a quarter of K through shared memory; a thread owns 4 tokens
-// x 8 rows (32 accumulators, three shared-memory vector loads per 32 FMAs).
-// The four partial sums are added in a fixed order.
+// CTA (rows past E + 1 are zero). blockIdx.y picks one of gridDim.y slices of
+// K and the CTA writes that slice's partial logits (the top-k kernel adds the
+// slices in a fixed order). Inside, the 256 threads form four K-groups of 64
+// that each walk a quarter of the slice through shared memory, fetching the
+// next tile into registers while computing; a thread owns 4 tokens x 8 rows.
+// The four group sums are added in a fixed order.
 template <typename XT>
 __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__ h, int n, int H,
                                                           const float* __restrict__ wr,
@@ -81,36 +83,55 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__
   const int tx = tid & 7, ty = tid >> 3;  // rows 8tx..8tx+7, tokens 4ty..4ty+3
   const int m0 = blockIdx.x * BM;
   const int rows = E + 1;
-  const int kspan = (H + KG - 1) / KG;
-  const int kbeg = kg * kspan, kend = min(H, kbeg + kspan);
+  const int slice = (H + gridDim.y - 1) / gridDim.y;
+  const int s_beg = blockIdx.y * slice, s_end = min(H, s_beg + slice);
+  const int kspan = (slice + KG - 1) / KG;
+  const int kbeg = s_beg + kg * kspan, kend = min(s_end, kbeg + kspan);
   const int iters = (kspan + BK - 1) / BK;  // the same for every K-group (barriers inside)
+  logits += (size_t)blockIdx.y * n * E;
+  if (gate_logit) gate_logit += (size_t)blockIdx.y * n;
   float acc[4][8] = {};
-  for (int it = 0; it < iters; ++it) {
-    const int k0 = kbeg + it * BK;
+  // the next step's tiles are fetched into registers while this step computes
+  float4 ra[2], rb[4];
+  auto fetch = [&](int k0) {
 #pragma unroll
     for (int q = 0; q < 2; ++q) {  // A: 32 tokens x 16 k = 128 float4
       const int v4 = tid + 64 * q;
       const int r = v4 >> 2, kk = (v4 & 3) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m0 + r < n && k0 + kk < kend) v = load4(h + (size_t)(m0 + r) * H + k0 + kk);
-      sm.t.A[kg][kk + 0][r] = v.x;
-      sm.t.A[kg][kk + 1][r] = v.y;
-      sm.t.A[kg][kk + 2][r] = v.z;
-      sm.t.A[kg][kk + 3][r] = v.w;
+      ra[q] = (m0 + r < n && k0 + kk < kend) ? load4(h + (size_t)(m0 + r) * H + k0 + kk)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {  // B: 64 rows x 16 k = 256 float4
       const int v4 = tid + 64 * q;
       const int r = v4 >> 2, kk = (v4 & 3) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < rows && k0 + kk < kend)
-        v = *reinterpret_cast<const float4*>((r < E ? wr + (size_t)r * H : wg) + k0 + kk);
-      sm.t.B[kg][kk + 0][r] = v.x;
-      sm.t.B[kg][kk + 1][r] = v.y;
-      sm.t.B[kg][kk + 2][r] = v.z;
-      sm.t.B[kg][kk + 3][r] = v.w;
+      rb[q] = (r < rows && k0 + kk < kend)
+                  ? *reinterpret_cast<const float4*>((r < E ? wr + (size_t)r * H : wg) + k0 + kk)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  fetch(kbeg);
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int v4 = tid + 64 * q;
+      const int r = v4 >> 2, kk = (v4 & 3) * 4;
+      sm.t.A[kg][kk + 0][r] = ra[q].x;
+      sm.t.A[kg][kk + 1][r] = ra[q].y;
+      sm.t.A[kg][kk + 2][r] = ra[q].z;
+      sm.t.A[kg][kk + 3][r] = ra[q].w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int v4 = tid + 64 * q;
+      const int r = v4 >> 2, kk = (v4 & 3) * 4;
+      sm.t.B[kg][kk + 0][r] = rb[q].x;
+      sm.t.B[kg][kk + 1][r] = rb[q].y;
+      sm.t.B[kg][kk + 2][r] = rb[q].z;
+      sm.t.B[kg][kk + 3][r] = rb[q].w;
     }
     __syncthreads();
+    if (it + 1 < iters) fetch(kbeg + (it + 1) * BK);
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       const float4 a = *reinterpret_cast<const float4*>(&sm.t.A[kg][kk][ty * 4]);
@@ -155,12 +176,14 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__
 // divide) and top-k by logit value, largest first, exact ties to the lower
 // expert id. Ranking by the logits equals ranking by the probabilities
 // because every step of the softmax is monotone; NaN logits rank as -inf.
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int n, int E,
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int nparts, int gparts,
+                                                          int n, int E,
                                                           int k, int norm, int64_t* __restrict__ idx64,
                                                           int32_t* __restrict__ idx32,
                                                           float* __restrict__ wout,
                                                           const float* __restrict__ gate_logit,
-                                                          float* __restrict__ gate_sig) {
+                                                          float* __restrict__ gate_sig,
+                                                          float* __restrict__ logits_sum) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= n) return;
@@ -171,7 +194,13 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int e = lane + 32 * j;
-    v[j] = (e < E) ? l[e] : -INFINITY;
+    v[j] = -INFINITY;
+    if (e < E) {  // partial logits of K slices, added in slice order
+      float a = l[e];
+      for (int p = 1; p < nparts; ++p) a += l[(size_t)p * n * E + e];
+      v[j] = a;
+      if (logits_sum) logits_sum[(size_t)t * E + e] = a;
+    }
     mx = fmaxf(mx, v[j]);
   }
 #pragma unroll
@@ -235,12 +264,17 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       if (idx32) idx32[(size_t)t * k + r] = sel[r];
       if (wout) wout[(size_t)t * k + r] = w;
     }
-    if (gate_sig && gate_logit) gate_sig[t] = sigmoid_f(gate_logit[t]);
+    if (gate_sig && gate_logit) {
+      float gl = gate_logit[t];
+      for (int p = 1; p < gparts; ++p) gl += gate_logit[(size_t)p * n + t];
+      gate_sig[t] = sigmoid_f(gl);
+    }
   }
 }
 
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
-                         float* logits, float* gate_logit, cudaStream_t st) {
+                         float* logits, float* gate_logit, int* nparts, cudaStream_t st) {
+  *nparts = 1;
   if (n <= 0) return ER_OK;
   // E == 0: only the shared-gate row (the caller supplies router logits)
   if (n <= 64 || E + 1 > 64) {
@@ -251,7 +285,8 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
       router_rows_kernel<float><<<E + 1, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit);
     return launch_check("router_rows_kernel");
   }
-  const int grid = (n + 31) / 32;
+  *nparts = kRouterKSplit;
+  const dim3 grid((n + 31) / 32, kRouterKSplit);
   if (h_dtype == ER_DTYPE_BF16)
     router_gemm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
                                                              gate_logit);
@@ -260,13 +295,15 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
   return launch_check("router_gemm_kernel");
 }
 
-int launch_router_topk(const float* logits, int n, int E, int k, int norm, int64_t* idx64, int32_t* idx32,
-                       float* wout, const float* gate_logit, float* gate_sig, cudaStream_t st) {
+int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
+                       int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
+                       cudaStream_t st) {
   if (n <= 0) return ER_OK;
   const int warps_per_block = 8;
   const int blocks = (n + warps_per_block - 1) / warps_per_block;
-  router_topk_kernel<<<blocks, warps_per_block * 32, 0, st>>>(logits, n, E, k, norm, idx64, idx32, wout,
-                                                               gate_logit, gate_sig);
+  router_topk_kernel<<<blocks, warps_per_block * 32, 0, st>>>(logits, nparts, gparts, n, E, k, norm, idx64, idx32,
+                                                               wout,
+                                                               gate_logit, gate_sig, logits_sum);
   return launch_check("router_topk_kernel");
 }
 
@@ -280,6 +317,6 @@ extern "C" int er_router_topk(const float* logits, int n, int num_experts, int k
     return fail(ER_EINVAL, "er_router_topk: num_experts %d outside 1..%d", num_experts, kMaxExperts);
   if (k < 1 || k > kMaxTopK || k > num_experts)
     return fail(ER_EINVAL, "er_router_topk: k %d outside 1..min(%d, num_experts)", k, kMaxTopK);
-  return launch_router_topk(logits, n, num_experts, k, 0, idx64, idx32, probs_out, nullptr, nullptr,
+  return launch_router_topk(logits, 1, 1, n, num_experts, k, 0, idx64, idx32, probs_out, nullptr, nullptr, nullptr,
                             (cudaStream_t)stream);
 }

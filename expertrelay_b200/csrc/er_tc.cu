@@ -35,8 +35,17 @@
 
 namespace er {
 
-constexpr int kTcEpiWarps = 8;  // two per TMEM lane quadrant, splitting the token columns
-constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;
+// Warp roles. A warp runs on SM sub-partition (warp % 4) and may read TMEM
+// lanes 32 * (warp % 4) .. +31 only. The 8 epilogue warps are 4..11 (two per
+// lane quadrant); quadrants 2 and 3 hold the up rows, whose warps only hand
+// values over, so the MMA issuer (warp 2) and the TMA producer (warp 3) share
+// those two sub-partitions and are not held up by the gate warps' math.
+// Warps 0 and 1 have no role.
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcEpiWarp0 = 4;
+constexpr int kTcMmaWarp = 2;
+constexpr int kTcTmaWarp = 3;
+constexpr int kTcThreads = (kTcEpiWarp0 + kTcEpiWarps) * 32;
 constexpr int kTcAccCols = 256;  // TMEM columns per accumulator set (x2 buffers = 512)
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
@@ -352,7 +361,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == kTcMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(2 * kTcAccCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -364,7 +373,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   const Plan* P = t.g.plan;
   const int total = P->item_start[t.sched][P->num_active];
 
-  if (warp == 0) {
+  if (warp == kTcTmaWarp) {
     // ---------------- TMA producer (lane 0 issues; the warp moves in step) ----------------
     uint32_t kc = 0;  // k-blocks issued so far
     bool ok = true;
@@ -416,7 +425,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == kTcMmaWarp) {
     // ---------------- MMA issuer (lane 0 issues; the warp moves in step) ----------------
     uint32_t kc = 0, ic = 0;
     bool ok = true;
@@ -462,14 +471,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       mbar_drain(drain_bar, 0, 100000000ull);
     }
     __syncwarp();
-  } else {
-    // ---------------- epilogue (warps 2..9) ----------------
+  } else if (warp >= kTcEpiWarp0) {
+    // ---------------- epilogue (warps 4..11) ----------------
     // Warp w reads TMEM lanes 32*(w%4)..+31 and every other 16-token chunk
-    // (half = (w-2)/4). Mode 0: lanes 0..63 hold gate rows, 64..127 the up
+    // (half = (w-4)/4). Mode 0: lanes 0..63 hold gate rows, 64..127 the up
     // rows of the same columns; the up warp of each pair hands u to the gate
     // warp through shared memory (named barrier per pair and half).
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - kTcEpiWarp0) >> 2;
     const int pair = quad & 1;
     const bool up_warp = MODE == 0 && quad >= 2;
     const int xpb = (pair * 2 + half) * 2;  // exchange barriers of this pair and half
@@ -479,7 +488,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       TcItem it;
       if (!tc_item<MODE, TT>(t, item, it)) break;
       if (!it.valid) {
-        if (threadIdx.x == 64) atomicOr(&t.plan_rw->error, 4);
+        if (threadIdx.x == kTcEpiWarp0 * 32) atomicOr(&t.plan_rw->error, 4);
         continue;
       }
       const int ab = ic & 1;
@@ -570,7 +579,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   __syncthreads();
   tc_fence_after();
   if (*abort_flag && threadIdx.x == 0) atomicOr(&t.plan_rw->error, 8);
-  if (warp == 1) {
+  if (warp == kTcMmaWarp) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kTcAccCols));
   }
 }

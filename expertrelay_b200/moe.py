@@ -151,6 +151,7 @@ class MoeBlock:
         return_routing: bool = False,
         stage_events: list | None = None,
         launch_counter: C.c_int | None = None,
+        workspace: torch.Tensor | None = None,
     ):
         """h [n, H] float32 or bfloat16 CUDA tensor -> y [n, H] float32. With
         `logits` ([n, E] float32) the routing uses those router logits. With
@@ -176,7 +177,12 @@ class MoeBlock:
             logits = logits.to(torch.float32).contiguous()
             if tuple(logits.shape) != (n, self.num_experts):
                 raise ValueError(f"logits: expected [{n}, {self.num_experts}], got {tuple(logits.shape)}")
-        ws = self._workspace(n, path)
+        if workspace is None:
+            ws = self._workspace(n, path)
+        else:
+            if workspace.numel() < self.workspace_bytes(n, path):
+                raise ValueError("workspace too small for this batch")
+            ws = workspace
         io = MoeIO(
             h=h.data_ptr(),
             h_dtype=_lib.DTYPE_BF16 if h.dtype == torch.bfloat16 else _lib.DTYPE_F32,
@@ -204,7 +210,52 @@ class MoeBlock:
 
     __call__ = forward
 
+    def capture(
+        self,
+        n: int,
+        *,
+        dtype: torch.dtype = torch.float32,
+        path: int = _lib.PATH_AUTO,
+        stage_events: list | None = None,
+    ) -> CapturedBlock:
+        """Record one forward over a fixed [n, H] input buffer into a CUDA graph.
+        The graph owns its workspace, input and output; replays re-read the
+        expert table, so remapped experts are picked up without re-capture."""
+        h = torch.zeros((n, self.hidden), dtype=dtype, device=self.device)
+        y = torch.empty((n, self.hidden), dtype=torch.float32, device=self.device)
+        ws = torch.empty(max(self.workspace_bytes(n, path), 256), dtype=torch.uint8, device=self.device)
+        self.forward(h, out=y, path=path, workspace=ws)  # first-use setup happens outside the capture
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.forward(h, out=y, path=path, workspace=ws, stage_events=stage_events)
+        return CapturedBlock(graph, h, y, ws)
+
     def moe_numpy(self, h: np.ndarray) -> np.ndarray:
         """The reference's calling convention: numpy float32 in, new numpy float32 out."""
         hd = torch.from_numpy(np.ascontiguousarray(h, dtype=np.float32)).to(self.device, non_blocking=False)
         return self.forward(hd).cpu().numpy()
+
+
+class CapturedBlock:
+    """A MoeBlock forward captured as a CUDA graph over fixed buffers `h` -> `y`."""
+
+    def __init__(self, graph, h: torch.Tensor, y: torch.Tensor, workspace: torch.Tensor):
+        self.graph, self.h, self.y, self._ws = graph, h, y, workspace
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.y
+
+    def __call__(self, h: torch.Tensor) -> torch.Tensor:
+        """Copy `h` (device or pinned host) into the graph's input and replay."""
+        self.h.copy_(h, non_blocking=True)
+        return self.replay()
+
+    def run_host(self, h_host: torch.Tensor, y_host: torch.Tensor) -> torch.Tensor:
+        """Host tokens in, host output back, all ordered on the current stream
+        (pinned buffers make both copies asynchronous)."""
+        self.h.copy_(h_host, non_blocking=True)
+        self.graph.replay()
+        y_host.copy_(self.y, non_blocking=True)
+        return y_host

@@ -137,6 +137,34 @@ def test_edge_routing_cases(decode8):
     assert tuple(empty.shape) == (0, 2048)
 
 
+@pytest.mark.parametrize("path", list(PATHS_INT8))
+def test_captured_graph_replays_and_follows_the_expert_table(decode8, path):
+    """A forward captured as a CUDA graph gives the eager result on replay,
+    and re-reads the expert table: remapping two experts' records after the
+    capture changes the replayed output exactly as it changes the eager one."""
+    blk, x, dev, _ = decode8
+    h = torch.from_numpy(x).to(dev.device)
+    cap = dev.capture(8, path=PATHS_INT8[path])
+    y_graph = cap(h).clone()
+    y_eager = dev.forward(h, path=PATHS_INT8[path])
+    torch.cuda.synchronize()
+    assert torch.equal(y_graph, y_eager)
+    table = dev.expert_table.clone()
+    swapped = table.clone()
+    swapped[[0, 1]] = table[[1, 0]]  # expert 0 now computes with expert 1's record and vice versa
+    try:
+        dev.set_expert_table(swapped)
+        y_swap_graph = cap.replay().clone()
+        y_swap_eager = dev.forward(h, path=PATHS_INT8[path])
+        torch.cuda.synchronize()
+        assert torch.equal(y_swap_graph, y_swap_eager)
+        _, _, idx, _ = dev.forward(h, path=PATHS_INT8[path], return_routing=True)
+        if bool(((idx == 0) | (idx == 1)).any()):
+            assert not torch.equal(y_swap_graph, y_graph)
+    finally:
+        dev.set_expert_table(table)
+
+
 @pytest.fixture(scope="module")
 def gptq_block(cuda):
     blk = synth.make_block(3, fmt="gptq_asym", group=128)
