@@ -122,11 +122,15 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   cudaStream_t st = (cudaStream_t)stream;
   char* ws = static_cast<char*>(workspace);
   int launches = 0;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (io->stage_events)
+    if (int rc = cuda_check(cudaStreamIsCapturing(st, &capture), "cudaStreamIsCapturing")) return rc;
   auto mark = [&](int i) -> int {
     if (!io->stage_events) return ER_OK;
-    // external record: also timestamps when the call is captured into a CUDA graph
-    return cuda_check(cudaEventRecordWithFlags((cudaEvent_t)io->stage_events[i], st, cudaEventRecordExternal),
-                      "cudaEventRecord");
+    // under stream capture the record becomes an external event node, so the
+    // graph's replays timestamp the stages too; outside capture a plain record
+    const unsigned flags = capture == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
+    return cuda_check(cudaEventRecordWithFlags((cudaEvent_t)io->stage_events[i], st, flags), "cudaEventRecord");
   };
   if (int rc = mark(0)) return rc;
   const int H = w->hidden, E = w->num_experts, k = w->top_k;

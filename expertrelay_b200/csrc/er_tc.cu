@@ -260,6 +260,21 @@ struct TcArgs {
   Plan* plan_rw;             // error bits
 };
 
+// The plan's schedule, copied into shared memory once per CTA so that the
+// per-item lookups of every role (a binary search over the item prefix,
+// then the group's rows and record) cost no global-memory round trips.
+// Entries are indexed by active position a, not by group id.
+struct TcPlanCache {
+  int total;       // work items of this schedule
+  int num_active;  // active groups (routed, then the shared expert)
+  int nk;
+  int item_start[kMaxExperts + 2];
+  int group[kMaxExperts + 1];   // group id (E = shared expert)
+  int rows[kMaxExperts + 1];    // tokens of the group
+  int offset[kMaxExperts + 1];  // first expert-sorted position (routed groups)
+  int slot[kMaxExperts + 1];    // arena slot of the group's record; -1 outside the arena
+};
+
 // TT = tokens per work item (128 for prefill, 16 for decode batches).
 // A tile: 128 weight rows x 128 bytes of K per stage (mode 0: 64 gate rows,
 // then the same 64 columns' up rows). B tile: slice 0 of TT token rows, then
@@ -275,7 +290,8 @@ struct TcGeom {
   static constexpr int kUnits = MODE == 0 ? 64 : 128;  // intermediate columns / hidden rows per item
   static constexpr size_t kRingBytes = (size_t)kStages * kStageBytes;
   static constexpr size_t kXchBytes = MODE == 0 ? 4 * 2 * 16 * 32 * 4 : 0;  // gate/up exchange
-  static constexpr size_t kSmem = kRingBytes + kXchBytes + 2048;
+  static constexpr int kChunks = (TT + 31) / 32;  // 16-token TMEM chunks per epilogue warp
+  static constexpr size_t kSmem = kRingBytes + kXchBytes + 2048 + sizeof(struct TcPlanCache);
 };
 
 struct TcItem {
@@ -289,13 +305,51 @@ struct TcItem {
   int units, nkb;
 };
 
-template <int MODE, int TT>
-__device__ __forceinline__ bool tc_item(const TcArgs& t, int item, TcItem& it) {
-  using Geo = TcGeom<MODE, TT>;
-  int local = 0;
-  const int g = find_item(t.g.plan, t.sched, item, &local);
-  if (g < 0) return false;
+// Copies the schedule `t.sched` of the plan into `pc` (all threads take part;
+// a __syncthreads must follow before any lookup).
+__device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) {
   const Plan* P = t.g.plan;
+  const int na = min(P->num_active, kMaxExperts + 1);
+  for (int a = threadIdx.x; a <= na; a += blockDim.x) {
+    pc->item_start[a] = P->item_start[t.sched][a];
+    if (a == na) continue;
+    const int g = P->active[a];
+    pc->group[a] = g;
+    pc->rows[a] = P->counts[g];
+    const bool shared = g == t.g.E;
+    pc->offset[a] = shared ? 0 : P->offsets[g];
+    int slot = 0;
+    if (!shared) {
+      const uint64_t addr = t.g.expert_records[g];
+      const uint64_t base = (uint64_t)t.arena;
+      slot = -1;  // record outside the arena: reported, never loaded
+      if (addr >= base && (addr - base) % t.record_bytes == 0 && (addr - base) / t.record_bytes < (uint64_t)t.arena_slots)
+        slot = (int)((addr - base) / t.record_bytes);
+    }
+    pc->slot[a] = slot;
+  }
+  if (threadIdx.x == 0) {
+    pc->num_active = na;
+    pc->total = P->item_start[t.sched][na];
+    pc->nk = P->nk;
+  }
+}
+
+template <int MODE, int TT>
+__device__ __forceinline__ bool tc_item(const TcArgs& t, const TcPlanCache* pc, int item, TcItem& it) {
+  using Geo = TcGeom<MODE, TT>;
+  const int na = pc->num_active;
+  if (item >= pc->total || na <= 0) return false;
+  int lo = 0, hi = na - 1;  // largest a with item_start[a] <= item
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pc->item_start[mid] <= item)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  const int local = item - pc->item_start[lo];
+  const int g = pc->group[lo];
   it.g = g;
   it.shared = (g == t.g.E);
   const int inter = it.shared ? t.g.Is : t.g.I;
@@ -303,26 +357,16 @@ __device__ __forceinline__ bool tc_item(const TcArgs& t, int item, TcItem& it) {
   const int K = MODE == 0 ? t.g.H : inter;
   it.nkb = (K + 127) / 128;
   const int ntiles = (it.units + Geo::kUnits - 1) / Geo::kUnits;
-  const int rows = P->counts[g];
   it.tok0 = (local / ntiles) * TT;
   it.unit0 = (local % ntiles) * Geo::kUnits;
-  it.nvalid = min(TT, rows - it.tok0);
+  it.nvalid = min(TT, pc->rows[lo] - it.tok0);
   it.npad = (it.nvalid + 15) & ~15;
   if (MODE == 0)
-    it.brow0 = (it.shared ? P->nk : P->offsets[g]) + it.tok0;
+    it.brow0 = (it.shared ? pc->nk : pc->offset[lo]) + it.tok0;
   else
-    it.brow0 = (it.shared ? 0 : P->offsets[g]) + it.tok0;
-  it.valid = 1;
-  it.slot = 0;
-  if (!it.shared) {
-    const uint64_t addr = t.g.expert_records[g];
-    const uint64_t base = (uint64_t)t.arena;
-    if (addr < base || (addr - base) % t.record_bytes != 0 || (addr - base) / t.record_bytes >= (uint64_t)t.arena_slots) {
-      it.valid = 0;  // record outside the arena: reported, never loaded
-    } else {
-      it.slot = (int)((addr - base) / t.record_bytes);
-    }
-  }
+    it.brow0 = pc->offset[lo] + it.tok0;
+  it.slot = it.shared ? 0 : pc->slot[lo];
+  it.valid = it.slot >= 0;
   return true;
 }
 
@@ -342,6 +386,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   uint64_t* xempty = xfull + 8;      // [pair*2 + half][buffer]: u values consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  TcPlanCache* pc = reinterpret_cast<TcPlanCache*>(smem + Geo::kRingBytes + Geo::kXchBytes + 2048);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -366,12 +411,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
                  "r"(2 * kTcAccCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  tc_cache_plan(t, pc);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const Plan* P = t.g.plan;
-  const int total = P->item_start[t.sched][P->num_active];
+  const int total = pc->total;
 
   if (warp == kTcTmaWarp) {
     // ---------------- TMA producer (lane 0 issues; the warp moves in step) ----------------
@@ -379,7 +424,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     bool ok = true;
     for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
       TcItem it;
-      if (!tc_item<MODE, TT>(t, item, it)) break;
+      if (!tc_item<MODE, TT>(t, pc, item, it)) break;
       if (!it.valid) continue;
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
@@ -431,7 +476,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     bool ok = true;
     for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
       TcItem it;
-      if (!tc_item<MODE, TT>(t, item, it)) break;
+      if (!tc_item<MODE, TT>(t, pc, item, it)) break;
       if (!it.valid) continue;
       const int ab = ic & 1;
       const uint32_t aph = (ic >> 1) & 1;
@@ -486,39 +531,52 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     bool alive = true;
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
       TcItem it;
-      if (!tc_item<MODE, TT>(t, item, it)) break;
+      if (!tc_item<MODE, TT>(t, pc, item, it)) break;
       if (!it.valid) {
         if (threadIdx.x == kTcEpiWarp0 * 32) atomicOr(&t.plan_rw->error, 4);
         continue;
+      }
+      // this thread's weight row: mode 0 -> intermediate column `col` of gate (or up);
+      // mode 1 -> hidden row
+      const int col = it.unit0 + (MODE == 0 ? pair * 32 + lane : quad * 32 + lane);
+      const bool row_ok = col < it.units;
+      const uint8_t* rec = it.shared ? t.g.shared_record : t.arena + (size_t)it.slot * t.record_bytes;
+      const RecordGeom geo{ER_FMT_INT8, t.g.H, it.shared ? t.g.Is : t.g.I, 1};
+      const int which = MODE == 0 ? (up_warp ? 1 : 0) : 2;
+      const float* xsc = (MODE == 1 && it.shared) ? t.xscale_s : t.xscale_r;
+      const float* tokw = it.shared ? t.g.gate_sig : t.g.perm_w;
+      // the row scale and the item's per-token scales (and, for down, routing
+      // weights) are fetched before the wait for the accumulator, so their
+      // latency hides behind the item's MMAs; lane l holds token 32 i + l
+      const float sw = row_ok ? __ldg(reinterpret_cast<const float*>(rec + geo.scale_offset(which)) + col) : 0.f;
+      float xs_r[Geo::kChunks], tw_r[Geo::kChunks];
+#pragma unroll
+      for (int i = 0; i < Geo::kChunks; ++i) {
+        const int tk = 32 * i + lane;
+        const bool ok = tk < it.nvalid;
+        xs_r[i] = ok ? __ldg(xsc + it.brow0 + tk) : 0.f;
+        tw_r[i] = (MODE == 1 && ok) ? __ldg(tokw + it.brow0 + tk) : 0.f;
       }
       const int ab = ic & 1;
       const uint32_t aph = (ic >> 1) & 1;
       if (!warp_wait(&acc_full[ab], aph, abort_flag, lane)) break;
       tc_fence_after();
-      // this thread's weight row: mode 0 -> intermediate column `col` of gate (or up);
-      // mode 1 -> hidden row
-      const int col = it.unit0 + (MODE == 0 ? pair * 32 + lane : quad * 32 + lane);
-      const bool row_ok = col < it.units;
-      const uint8_t* rec = it.shared ? t.g.shared_record : reinterpret_cast<const uint8_t*>(t.g.expert_records[it.g]);
-      const RecordGeom geo{ER_FMT_INT8, t.g.H, it.shared ? t.g.Is : t.g.I, 1};
-      const int which = MODE == 0 ? (up_warp ? 1 : 0) : 2;
-      const float sw = row_ok ? reinterpret_cast<const float*>(rec + geo.scale_offset(which))[col] : 0.f;
       const uint32_t tbase = tmem_base + ab * kTcAccCols + ((uint32_t)(quad * 32) << 16);
       const int ld_out = MODE == 0 ? (it.shared ? t.g.Is : t.g.I) : t.g.H;
       float* out_base = it.shared ? t.out_s : t.out_r;
       const int orow0 = (MODE == 0 && it.shared) ? it.tok0 : it.brow0;
-      const float* xsc = (MODE == 1 && it.shared) ? t.xscale_s : t.xscale_r;
-      const float* tokw = it.shared ? t.g.gate_sig : t.g.perm_w;
-      for (int c0 = half * 16; c0 < it.npad; c0 += 32, ++chunk) {
+#pragma unroll 1
+      for (int ci = 0; ci < Geo::kChunks; ++ci) {
+        const int c0 = half * 16 + 32 * ci;  // tokens c0 .. c0 + 15: lanes half*16 .. +15 of xs_r[ci]
+        if (c0 >= it.npad) break;
         uint32_t v0[16], v1[16];
         tmem_ld16(tbase + c0, v0);
         tmem_ld16(tbase + TT + c0, v1);
         float xs[16], tw[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int tk = c0 + j;
-          xs[j] = tk < it.nvalid ? __ldg(xsc + it.brow0 + tk) : 0.f;
-          if (MODE == 1) tw[j] = tk < it.nvalid ? __ldg(tokw + it.brow0 + tk) : 0.f;
+          xs[j] = __shfl_sync(0xffffffffu, xs_r[ci], half * 16 + j);
+          tw[j] = MODE == 1 ? __shfl_sync(0xffffffffu, tw_r[ci], half * 16 + j) : 0.f;
         }
         tmem_ld_wait();
         float val[16];
@@ -548,8 +606,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const float g = val[j], u = xb[j * 32 + lane];
-              // SiLU(g) * u = g / (1 + e^-g) * u, with the fast exponential and reciprocal
-              act[j] = row_ok ? g * __frcp_rn(1.f + __expf(-g)) * u : 0.f;
+              // SiLU(g) * u = g / (1 + e^-g) * u with the fast exponential and the
+              // fast divide (2 ulp; a correctly rounded reciprocal here costs a
+              // fifth of the kernel's time). g << 0 gives e^-g = inf and 0.
+              act[j] = row_ok ? __fdividef(g, 1.f + __expf(-g)) * u : 0.f;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&xempty[xpb + b]);
@@ -566,6 +626,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           for (int j = 0; j < 16; ++j)
             if (c0 + j < it.nvalid) dst[(size_t)j * ld_out] = val[j] * tw[j];
         }
+        ++chunk;
       }
       if (!alive) break;
       tc_fence_before();

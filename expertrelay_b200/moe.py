@@ -197,6 +197,9 @@ class MoeBlock:
         if stage_events is not None:
             if len(stage_events) != len(_lib.MOE_STAGES) + 1:
                 raise ValueError(f"stage_events: need {len(_lib.MOE_STAGES) + 1} events")
+            for ev in stage_events:
+                if not ev.cuda_event:  # torch creates the CUDA event on its first record
+                    ev.record()
             handles = (C.c_void_p * len(stage_events))(*[ev.cuda_event for ev in stage_events])
             io.stage_events = C.cast(handles, C.POINTER(C.c_void_p))
         if launch_counter is not None:

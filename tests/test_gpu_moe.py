@@ -165,6 +165,21 @@ def test_captured_graph_replays_and_follows_the_expert_table(decode8, path):
         dev.set_expert_table(table)
 
 
+@pytest.mark.parametrize("path", list(PATHS_INT8))
+def test_stage_events_time_an_eager_call(decode8, path):
+    """Stage events passed to an eager (uncaptured) call are recorded in
+    stage order, and the stages add up to the whole call."""
+    _, x, dev, _ = decode8
+    h = torch.from_numpy(x).to(dev.device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(_lib.MOE_STAGES) + 1)]
+    y = dev.forward(h, path=PATHS_INT8[path], stage_events=ev)
+    torch.cuda.synchronize()
+    stages = [ev[i].elapsed_time(ev[i + 1]) for i in range(len(_lib.MOE_STAGES))]
+    assert all(s >= 0.0 for s in stages)
+    assert abs(sum(stages) - ev[0].elapsed_time(ev[-1])) < 1e-2
+    assert torch.equal(y, dev.forward(h, path=PATHS_INT8[path]))
+
+
 @pytest.fixture(scope="module")
 def gptq_block(cuda):
     blk = synth.make_block(3, fmt="gptq_asym", group=128)
