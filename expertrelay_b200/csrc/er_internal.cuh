@@ -121,8 +121,13 @@ int launch_slice_rows(const void* src, int dtype, const int32_t* perm_token, int
                       int8_t* s0, int8_t* s1, float* scale, cudaStream_t st);
 // tokens per tcgen05 work item: 16 when every group fits (n <= 16), else 128
 inline int tc_tok_tile(int n) { return n <= 16 ? 16 : 128; }
-constexpr int kTcUnitsGU = 64;    // intermediate columns per gate/up item (64 gate + 64 up rows)
-constexpr int kTcUnitsDN = 128;   // hidden rows per down item
+// CTAs per work item: 128-token tiles run on an SM pair (tcgen05 cta_group::2,
+// M = 256), 16-token tiles on one SM.
+inline int tc_cta_group(int tok_tile) { return tok_tile >= 128 ? 2 : 1; }
+// intermediate columns per gate/up item (64 gate + 64 up rows per CTA)
+inline int tc_units_gu(int tok_tile) { return 64 * tc_cta_group(tok_tile); }
+// hidden rows per down item (128 per CTA)
+inline int tc_units_dn(int tok_tile) { return 128 * tc_cta_group(tok_tile); }
 
 // GEMV schedule geometry (er_gemv.cu): units per item
 constexpr int kGemvWarps = 8;

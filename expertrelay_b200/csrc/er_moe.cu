@@ -180,8 +180,8 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     specs[0] = SchedSpec{0, kGemvUnitsGU, 0};
     specs[1] = SchedSpec{0, kGemvUnitsDN, 1};
   } else if (path == ER_PATH_TC) {
-    specs[0] = SchedSpec{tc_tok_tile(n), kTcUnitsGU, 0};
-    specs[1] = SchedSpec{tc_tok_tile(n), kTcUnitsDN, 1};
+    specs[0] = SchedSpec{tc_tok_tile(n), tc_units_gu(tc_tok_tile(n)), 0};
+    specs[1] = SchedSpec{tc_tok_tile(n), tc_units_dn(tc_tok_tile(n)), 1};
   } else {
     specs[0] = SchedSpec{kSimtBM, kSimtBN, 0};
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};

@@ -18,12 +18,21 @@
 //  * D = weights x tokens: M = 128 weight rows per item, N = the group's
 //    tokens (rounded up to 16, at most kTokTile), so decode (a few tokens per
 //    expert) and prefill use the same kernel.
-//  * One persistent CTA per SM, warp-specialised: warp 0 issues TMA, warp 1
-//    allocates TMEM and issues MMAs, warps 2-5 run the epilogue out of TMEM.
-//    A 4-stage shared-memory ring and double-buffered accumulators overlap
-//    loads, MMAs and epilogue. Every mbarrier wait is bounded: after
-//    kWaitNs the kernel sets an abort flag and an error bit in the plan,
-//    drains what it has in flight and frees its TMEM.
+//  * One persistent CTA per SM, warp-specialised: one warp issues TMA, one
+//    allocates TMEM and issues MMAs, eight run the epilogue out of TMEM.
+//    A shared-memory ring and double-buffered accumulators overlap loads,
+//    MMAs and epilogue. Every mbarrier wait is bounded: after kWaitNs the
+//    kernel sets an abort flag and an error bit in the plan, drains what it
+//    has in flight and frees its TMEM.
+//  * 128-token tiles run on SM pairs (a cluster of 2, tcgen05 cta_group::2):
+//    one MMA is M = 256 weight rows (128 from each CTA's shared memory) by
+//    N = 256 (slice 0 of the 128 tokens from CTA 0, slice 1 from CTA 1), so
+//    each SM loads 32 KB per 128-deep K block instead of 48 KB for the same
+//    MMA work. CTA 0 issues the MMAs and commits to both CTAs' barriers;
+//    CTA 1's loads complete on CTA 0's full barriers and its epilogue frees
+//    the accumulator on CTA 0's barrier. No load uses cluster multicast.
+//    16-token tiles (decode) run on single SMs: there the weight bytes, not
+//    the activations, bound the kernel.
 //  mode 0: A = gate rows and up rows of 128 intermediate columns; four
 //          accumulators (gate/up x slice); epilogue writes act = silu(g)*u.
 //  mode 1: A = 128 rows of down; two accumulators; epilogue writes
@@ -127,6 +136,39 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// Pair forms: the tile lands in this CTA's shared memory and completes on the
+// barrier at shared::cluster address `bar` (CTA 0's full barrier). Plain
+// loads of this GPU's memory; no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+template <int CG>
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int x, int y) {
+  if constexpr (CG == 1)
+    tma_load_2d(dst, map, bar, x, y);
+  else
+    tma_load_2d_pair(dst, map, bar_c, x, y);
+}
+template <int CG>
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int x, int y,
+                                       int z) {
+  if constexpr (CG == 1)
+    tma_load_3d(dst, map, bar, x, y, z);
+  else
+    tma_load_3d_pair(dst, map, bar_c, x, y, z);
+}
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), LBO unused (1), descriptor version 1.
@@ -139,17 +181,81 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+template <int CG>
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+  if constexpr (CG == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+// Pair kernels arrive on the barrier at the same offset in both CTAs.
+template <int CG>
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+  if constexpr (CG == 1)
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+  else
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+template <int CG>
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+  if constexpr (CG == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  } else {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+}
+template <int CG>
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t cols) {
+  if constexpr (CG == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+  else
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+}
+
+// ---- clusters (SM pairs)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the variable at shared::cta address `a` in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -281,13 +387,20 @@ struct TcPlanCache {
 // slice 1 of the same rows, so ONE MMA with N = TT + npad covers both slices
 // and reads A once. The accumulator holds slice 0 in columns [0, TT) and
 // slice 1 in [TT, 2 TT).
-template <int MODE, int TT>
+//
+// CG = CTAs per item (1: one SM; 2: an SM pair, cta_group::2). Per stage a CTA
+// holds its 128 weight rows and, on one SM, both slices (N = TT + npad), on a
+// pair only its own slice (CTA r: slice r; the pair's MMA has N = 2 TT).
+template <int MODE, int TT, int CG>
 struct TcGeom {
   static constexpr int kABytes = 16384;
   static constexpr int kBSliceBytes = TT * 128;
-  static constexpr int kStageBytes = kABytes + 2 * kBSliceBytes;
-  static constexpr int kStages = TT >= 128 ? 4 : 9;
-  static constexpr int kUnits = MODE == 0 ? 64 : 128;  // intermediate columns / hidden rows per item
+  static constexpr int kBBytes = (3 - CG) * kBSliceBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTxBytes = CG * kStageBytes;  // bytes completing on the (CTA 0) full barrier per stage
+  static constexpr int kStages = CG == 2 ? 6 : (TT >= 128 ? 4 : 9);
+  static constexpr int kCtaUnits = MODE == 0 ? 64 : 128;  // this CTA's intermediate columns / hidden rows
+  static constexpr int kUnits = CG * kCtaUnits;           // per item
   static constexpr size_t kRingBytes = (size_t)kStages * kStageBytes;
   static constexpr size_t kXchBytes = MODE == 0 ? 4 * 2 * 16 * 32 * 4 : 0;  // gate/up exchange
   static constexpr int kChunks = (TT + 31) / 32;  // 16-token TMEM chunks per epilogue warp
@@ -335,9 +448,9 @@ __device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) 
   }
 }
 
-template <int MODE, int TT>
+template <int MODE, int TT, int CG>
 __device__ __forceinline__ bool tc_item(const TcArgs& t, const TcPlanCache* pc, int item, TcItem& it) {
-  using Geo = TcGeom<MODE, TT>;
+  using Geo = TcGeom<MODE, TT, CG>;
   const int na = pc->num_active;
   if (item >= pc->total || na <= 0) return false;
   int lo = 0, hi = na - 1;  // largest a with item_start[a] <= item
@@ -370,9 +483,9 @@ __device__ __forceinline__ bool tc_item(const TcArgs& t, const TcPlanCache* pc, 
   return true;
 }
 
-template <int MODE, int TT>
+template <int MODE, int TT, int CG>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __grid_constant__ TcMaps maps, TcArgs t) {
-  using Geo = TcGeom<MODE, TT>;
+  using Geo = TcGeom<MODE, TT, CG>;
   constexpr int S = Geo::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -389,6 +502,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   TcPlanCache* pc = reinterpret_cast<TcPlanCache*>(smem + Geo::kRingBytes + Geo::kXchBytes + 2048);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // pair kernels: CTA 0 of the cluster issues the MMAs; items go to pairs
+  const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  const int first_item = CG == 2 ? (int)cluster_id() : (int)blockIdx.x;
+  const int item_stride = CG == 2 ? (int)cluster_count() : (int)gridDim.x;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -396,7 +514,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kTcEpiWarps);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], CG * kTcEpiWarps);  // one arrival per epilogue warp of each CTA
     }
     mbar_init(drain_bar, 1);
     for (int i = 0; i < 8; ++i) {
@@ -406,12 +524,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kTcMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(2 * kTcAccCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
   tc_cache_plan(t, pc);
+  if constexpr (CG == 2) {
+    // the peer's loads and arrivals target CTA 0's barriers: both CTAs'
+    // barriers are initialised, and both CTAs running, before either goes on
+    __syncthreads();
+    cluster_sync();
+  }
+  // one warp of each CTA allocates TMEM (on a pair, the two warps collectively)
+  if (warp == kTcMmaWarp) tmem_alloc<CG>(tmem_slot, 2 * kTcAccCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -422,10 +543,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     // ---------------- TMA producer (lane 0 issues; the warp moves in step) ----------------
     uint32_t kc = 0;  // k-blocks issued so far
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
+    for (int item = first_item; ok && item < total; item += item_stride) {
       TcItem it;
-      if (!tc_item<MODE, TT>(t, pc, item, it)) break;
+      if (!tc_item<MODE, TT, CG>(t, pc, item, it)) break;
       if (!it.valid) continue;
+      const int arow = it.unit0 + (int)rank * Geo::kCtaUnits;  // this CTA's first weight row
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
@@ -437,46 +559,62 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         }
         if (lane == 0) {
           uint8_t* st = smem + s * Geo::kStageBytes;
-          mbar_expect_tx(&full[s], Geo::kStageBytes);
+          // CTA 0 expects the whole pair's bytes; the peer's copies may land
+          // before that (the barrier's transaction count goes negative until
+          // then, and the phase cannot complete without CTA 0's arrival)
+          if (leader) mbar_expect_tx(&full[s], Geo::kTxBytes);
+          const uint32_t fc = CG == 2 ? mapa_shared(smem_u32(&full[s]), 0) : 0u;
           const int x = kb * 128;
           if (MODE == 0) {
             if (it.shared) {
-              tma_load_2d(st, &maps.a_shared[0], &full[s], x, it.unit0);
-              tma_load_2d(st + 8192, &maps.a_shared[1], &full[s], x, it.unit0);
+              tma_2d<CG>(st, &maps.a_shared[0], &full[s], fc, x, arow);
+              tma_2d<CG>(st + 8192, &maps.a_shared[1], &full[s], fc, x, arow);
             } else {
-              tma_load_3d(st, &maps.a_routed[0], &full[s], x, it.unit0, it.slot);
-              tma_load_3d(st + 8192, &maps.a_routed[1], &full[s], x, it.unit0, it.slot);
+              tma_3d<CG>(st, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
+              tma_3d<CG>(st + 8192, &maps.a_routed[1], &full[s], fc, x, arow, it.slot);
             }
           } else {
             if (it.shared)
-              tma_load_2d(st, &maps.a_shared[0], &full[s], x, it.unit0);
+              tma_2d<CG>(st, &maps.a_shared[0], &full[s], fc, x, arow);
             else
-              tma_load_3d(st, &maps.a_routed[0], &full[s], x, it.unit0, it.slot);
+              tma_3d<CG>(st, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
           }
           const CUtensorMap* b = (MODE == 1 && it.shared) ? maps.b_shared : maps.b_routed;
-          tma_load_2d(st + Geo::kABytes, &b[0], &full[s], x, it.brow0);
-          tma_load_2d(st + Geo::kABytes + Geo::kBSliceBytes, &b[1], &full[s], x, it.brow0);
+          if (CG == 1) {
+            tma_2d<CG>(st + Geo::kABytes, &b[0], &full[s], fc, x, it.brow0);
+            tma_2d<CG>(st + Geo::kABytes + Geo::kBSliceBytes, &b[1], &full[s], fc, x, it.brow0);
+          } else {
+            tma_2d<CG>(st + Geo::kABytes, &b[rank], &full[s], fc, x, it.brow0);
+          }
         }
         __syncwarp();
       }
     }
     if (!ok && lane == 0) {
-      // aborted: let every stage this thread filled land before the CTA exits
-      for (int s = 0; s < S; ++s) {
-        if (kc > (uint32_t)s) {
-          const uint32_t last = kc - 1 - ((kc - 1 - s) % S);
-          mbar_drain(&full[s], (last / S) & 1, 100000000ull);
+      if (leader) {
+        // aborted: let every stage this CTA's barriers track land before the CTA exits
+        for (int s = 0; s < S; ++s) {
+          if (kc > (uint32_t)s) {
+            const uint32_t last = kc - 1 - ((kc - 1 - s) % S);
+            mbar_drain(&full[s], (last / S) & 1, 100000000ull);
+          }
+        }
+      } else {
+        // the peer's copies complete on CTA 0's barriers, which this CTA
+        // cannot wait on: give those in flight 1 ms to land
+        const unsigned long long t0 = globaltimer();
+        while (globaltimer() - t0 < 1000000ull) {
         }
       }
     }
     __syncwarp();
-  } else if (warp == kTcMmaWarp) {
+  } else if (warp == kTcMmaWarp && leader) {
     // ---------------- MMA issuer (lane 0 issues; the warp moves in step) ----------------
     uint32_t kc = 0, ic = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
+    for (int item = first_item; ok && item < total; item += item_stride) {
       TcItem it;
-      if (!tc_item<MODE, TT>(t, pc, item, it)) break;
+      if (!tc_item<MODE, TT, CG>(t, pc, item, it)) break;
       if (!it.valid) continue;
       const int ab = ic & 1;
       const uint32_t aph = (ic >> 1) & 1;
@@ -485,7 +623,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       if (!__shfl_sync(0xffffffffu, (int)w, 0)) break;
       tc_fence_after();
       const uint32_t d = tmem_base + ab * kTcAccCols;
-      const uint32_t idesc = idesc_i8(128, TT + it.npad);
+      const uint32_t idesc = CG == 1 ? idesc_i8(128, TT + it.npad) : idesc_i8(256, 2 * TT);
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
@@ -499,20 +637,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           const uint32_t st = smem_u32(smem + s * Geo::kStageBytes);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            mma_i8(d, umma_desc_sw128(st + ks * 32), umma_desc_sw128(st + Geo::kABytes + ks * 32), idesc,
-                   (kb > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+            mma_i8<CG>(d, umma_desc_sw128(st + ks * 32), umma_desc_sw128(st + Geo::kABytes + ks * 32), idesc,
+                       (kb > 0 || ks > 0) ? 1u : 0u);
+          umma_commit<CG>(&empty[s]);  // frees the stage (in both CTAs of a pair) once these MMAs have read it
         }
         __syncwarp();
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&acc_full[ab]);  // accumulator ready for the epilogue
+      if (lane == 0) umma_commit<CG>(&acc_full[ab]);  // accumulator ready for the epilogue(s)
       __syncwarp();
       ++ic;
     }
     if (lane == 0) {
       // every MMA issued by this thread has finished before TMEM is released
-      umma_commit(drain_bar);
+      umma_commit<CG>(drain_bar);
       mbar_drain(drain_bar, 0, 100000000ull);
     }
     __syncwarp();
@@ -529,16 +667,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     const int xpb = (pair * 2 + half) * 2;  // exchange barriers of this pair and half
     uint32_t ic = 0, chunk = 0;
     bool alive = true;
-    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+    for (int item = first_item; item < total; item += item_stride) {
       TcItem it;
-      if (!tc_item<MODE, TT>(t, pc, item, it)) break;
+      if (!tc_item<MODE, TT, CG>(t, pc, item, it)) break;
       if (!it.valid) {
         if (threadIdx.x == kTcEpiWarp0 * 32) atomicOr(&t.plan_rw->error, 4);
         continue;
       }
       // this thread's weight row: mode 0 -> intermediate column `col` of gate (or up);
       // mode 1 -> hidden row
-      const int col = it.unit0 + (MODE == 0 ? pair * 32 + lane : quad * 32 + lane);
+      const int col = it.unit0 + (int)rank * Geo::kCtaUnits + (MODE == 0 ? pair * 32 + lane : quad * 32 + lane);
       const bool row_ok = col < it.units;
       const uint8_t* rec = it.shared ? t.g.shared_record : t.arena + (size_t)it.slot * t.record_bytes;
       const RecordGeom geo{ER_FMT_INT8, t.g.H, it.shared ? t.g.Is : t.g.I, 1};
@@ -572,11 +710,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         uint32_t v0[16], v1[16];
         tmem_ld16(tbase + c0, v0);
         tmem_ld16(tbase + TT + c0, v1);
+        float xsc_ci = xs_r[0], tw_ci = tw_r[0];  // register select, no local-memory indexing
+#pragma unroll
+        for (int i = 1; i < Geo::kChunks; ++i)
+          if (ci == i) {
+            xsc_ci = xs_r[i];
+            tw_ci = tw_r[i];
+          }
         float xs[16], tw[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          xs[j] = __shfl_sync(0xffffffffu, xs_r[ci], half * 16 + j);
-          tw[j] = MODE == 1 ? __shfl_sync(0xffffffffu, tw_r[ci], half * 16 + j) : 0.f;
+          xs[j] = __shfl_sync(0xffffffffu, xsc_ci, half * 16 + j);
+          tw[j] = MODE == 1 ? __shfl_sync(0xffffffffu, tw_ci, half * 16 + j) : 0.f;
         }
         tmem_ld_wait();
         float val[16];
@@ -631,18 +776,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       if (!alive) break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(&acc_empty[ab]);
+        else
+          mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[ab]), 0));
+      }
       ++ic;
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves while the other may still arrive on its
+  // barriers or (CTA 0's MMAs) use its shared memory and TMEM
+  if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
   if (*abort_flag && threadIdx.x == 0) atomicOr(&t.plan_rw->error, 8);
-  if (warp == kTcMmaWarp) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kTcAccCols));
-  }
+  if (warp == kTcMmaWarp) tmem_dealloc<CG>(tmem_base, 2 * kTcAccCols);
 }
 
 // ---------------------------------------------------------------------------
@@ -683,25 +834,73 @@ static int make_map(CUtensorMap* m, const void* base, int rank, uint64_t k, uint
   return ER_OK;
 }
 
-template <int MODE, int TT>
-static int configure_tc() {
-  static int done_dev = -1;
+static void pair_launch_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, int pairs, size_t smem,
+                               cudaStream_t st) {
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = 2;
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
+  memset(cfg, 0, sizeof(*cfg));
+  cfg->gridDim = dim3(2 * pairs);
+  cfg->blockDim = dim3(kTcThreads);
+  cfg->dynamicSmemBytes = smem;
+  cfg->stream = st;
+  cfg->attrs = attr;
+  cfg->numAttrs = 1;
+}
+
+// Per device and kernel: the shared-memory attribute, and for pair kernels how
+// many SM pairs can be resident at once (the persistent grid's size).
+template <int MODE, int TT, int CG>
+static int configure_tc(int* resident_pairs) {
+  static int done_dev = -1, pairs = 0;
   int dev = 0;
   if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
-  if (done_dev == dev) return ER_OK;
-  if (int rc = cuda_check(cudaFuncSetAttribute(tc_expert_gemm_kernel<MODE, TT>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)TcGeom<MODE, TT>::kSmem),
-                          "tc smem attribute"))
-    return rc;
-  done_dev = dev;
+  if (done_dev != dev) {
+    using Geo = TcGeom<MODE, TT, CG>;
+    if (int rc = cuda_check(cudaFuncSetAttribute(tc_expert_gemm_kernel<MODE, TT, CG>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Geo::kSmem),
+                            "tc smem attribute"))
+      return rc;
+    pairs = 0;
+    if (CG == 2) {
+      int sms = 148;
+      if (int rc = er_device_sm_count(&sms)) return rc;
+      cudaLaunchConfig_t cfg;
+      cudaLaunchAttribute attr;
+      pair_launch_config(&cfg, &attr, sms / 2, Geo::kSmem, 0);
+      if (int rc = cuda_check(cudaOccupancyMaxActiveClusters(&pairs, tc_expert_gemm_kernel<MODE, TT, CG>, &cfg),
+                              "cudaOccupancyMaxActiveClusters"))
+        return rc;
+      if (pairs < 1)
+        return fail(ER_ECUDA, "no SM pair can hold the tensor-core kernel (%zu bytes of shared memory)", Geo::kSmem);
+    }
+    done_dev = dev;
+  }
+  if (resident_pairs) *resident_pairs = pairs;
   return ER_OK;
 }
 
-template <int MODE, int TT>
-static int launch_tc_mode(const TcMaps& maps, const TcArgs& t, int grid, cudaStream_t st) {
-  if (int rc = configure_tc<MODE, TT>()) return rc;
-  tc_expert_gemm_kernel<MODE, TT><<<grid, kTcThreads, TcGeom<MODE, TT>::kSmem, st>>>(maps, t);
+template <int MODE, int TT, int CG>
+static int launch_tc_mode(const TcMaps& maps, const TcArgs& t, long long items_bound, cudaStream_t st) {
+  int resident_pairs = 0;
+  if (int rc = configure_tc<MODE, TT, CG>(&resident_pairs)) return rc;
+  const long long items = items_bound > 0 ? items_bound : 1;
+  if constexpr (CG == 1) {
+    int sms = 148;
+    if (int rc = er_device_sm_count(&sms)) return rc;
+    const int grid = (int)(items < sms ? items : sms);
+    tc_expert_gemm_kernel<MODE, TT, CG><<<grid, kTcThreads, TcGeom<MODE, TT, CG>::kSmem, st>>>(maps, t);
+  } else {
+    // persistent: one cluster per resident SM pair, items strided over the pairs
+    const int pairs = (int)(items < resident_pairs ? items : resident_pairs);
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    pair_launch_config(&cfg, &attr, pairs, TcGeom<MODE, TT, CG>::kSmem, st);
+    if (int rc = cuda_check(cudaLaunchKernelEx(&cfg, tc_expert_gemm_kernel<MODE, TT, CG>, maps, t),
+                            "cudaLaunchKernelEx(tc pair)"))
+      return rc;
+  }
   return launch_check("tc_expert_gemm_kernel");
 }
 
@@ -767,11 +966,12 @@ int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
   t.out_r = L.out_r;
   t.out_s = L.out_s;
   t.plan_rw = const_cast<Plan*>(a.plan);
-  int sms = 148;
-  if (int rc = er_device_sm_count(&sms)) return rc;
-  const int grid = (int)(L.items_bound < sms ? (L.items_bound > 0 ? L.items_bound : 1) : sms);
-  if (L.mode == 0) return TT == 16 ? launch_tc_mode<0, 16>(maps, t, grid, st) : launch_tc_mode<0, 128>(maps, t, grid, st);
-  return TT == 16 ? launch_tc_mode<1, 16>(maps, t, grid, st) : launch_tc_mode<1, 128>(maps, t, grid, st);
+  // 16-token tiles on single SMs, 128-token tiles on SM pairs (tc_cta_group)
+  if (L.mode == 0)
+    return TT == 16 ? launch_tc_mode<0, 16, 1>(maps, t, L.items_bound, st)
+                    : launch_tc_mode<0, 128, 2>(maps, t, L.items_bound, st);
+  return TT == 16 ? launch_tc_mode<1, 16, 1>(maps, t, L.items_bound, st)
+                  : launch_tc_mode<1, 128, 2>(maps, t, L.items_bound, st);
 }
 
 }  // namespace er
