@@ -18,7 +18,9 @@ struct SchedSpec {
 
 constexpr int kNumSched = 2;
 
-// Routing plan, written by plan_kernel into the workspace.
+// Routing plan in the workspace. The router kernel clears `tally`, the top-k
+// kernel counts into it, plan_kernel turns it into groups and schedules, and
+// dispatch_kernel claims expert-sorted positions through `cursor`.
 struct Plan {
   int n, E, k, nk;
   int error;                           // nonzero: an expert id was out of range
@@ -28,6 +30,8 @@ struct Plan {
   int active[kMaxExperts + 1];         // active group ids, ascending, shared last
   int item_start[kNumSched][kMaxExperts + 2];  // prefix of items over active groups
   SchedSpec sched[kNumSched];
+  int tally[kMaxExperts];              // (token, slot) pairs routed to each expert
+  int cursor[kMaxExperts];             // next free expert-sorted position of each expert
 };
 
 // Everything a grouped expert kernel needs to find a group's tokens and weights.
@@ -76,20 +80,48 @@ __device__ __forceinline__ int find_item(const Plan* P, int s, int item, int* lo
   return P->active[lo];
 }
 
+// Two int8 slices of four values: with inv = 127 / max|x| of the row,
+// x ~= (x0 + x1 / 256) / inv, x0 = rint(x inv), x1 = rint((x inv - x0) 256)
+// clamped to +-127. Packs the low bytes, first value in the lowest byte.
+__device__ __forceinline__ void slice4(float4 v, float inv, uint32_t& w0, uint32_t& w1) {
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  int i0[4], i1[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float y = f[j] * inv;
+    const float q0 = rintf(y);
+    i0[j] = (int)q0;
+    i1[j] = max(-127, min(127, __float2int_rn((y - q0) * 256.f)));
+  }
+  w0 = __byte_perm(__byte_perm(i0[0], i0[1], 0x0040), __byte_perm(i0[2], i0[3], 0x0040), 0x5410);
+  w1 = __byte_perm(__byte_perm(i1[0], i1[1], 0x0040), __byte_perm(i1[2], i1[3], 0x0040), 0x5410);
+}
+
+__device__ __forceinline__ float abs_max4(float4 v) {
+  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
 // launchers (each returns an ER_* status)
 // Router logits; large batches write kRouterKSplit partial sums (K slices)
 // into logits / gate_logit (each n*E / n apart), *nparts says how many.
 constexpr int kRouterKSplit = 4;
+// `tally` (optional, `ntally` ints) is cleared for the top-k kernel's counts.
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
-                         float* logits, float* gate_logit, int* nparts, cudaStream_t st);
+                         float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st);
 // softmax + top-k over the sum of `nparts` partial logits (and `gparts` partial
-// shared-gate logits); logits_sum (optional) receives the summed logits
+// shared-gate logits); logits_sum (optional) receives the summed logits;
+// tally (optional) counts the selected (token, slot) pairs per expert
 int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
                        int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
-                       cudaStream_t st);
-int launch_plan(const int32_t* idx, const float* w, int n, int k, int E, int H, int I, int Is,
-                const SchedSpec* specs, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of,
-                cudaStream_t st);
+                       int* tally, cudaStream_t st);
+// groups, offsets and work-item schedules from plan->tally (one warp)
+int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, Plan* plan, cudaStream_t st);
+// Scatter of the (token, slot) pairs to expert-sorted positions (perm_token,
+// perm_w, pos_of). With s0 non-null also slices each token's h row once and
+// writes the slices to its k routed positions and to shared row nk + t.
+int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H,
+                    Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1,
+                    float* scale, cudaStream_t st);
 // Upper bound of the items a schedule can produce (host side, for grid sizing).
 long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int I, int Is);
 
@@ -117,8 +149,9 @@ struct TcLaunch {
   long long items_bound;
 };
 int launch_tc_grouped(const TcLaunch& L, cudaStream_t st);
-int launch_slice_rows(const void* src, int dtype, const int32_t* perm_token, int nk, int rows, int K, int src_mode,
-                      int8_t* s0, int8_t* s1, float* scale, cudaStream_t st);
+// two int8 slices and a scale per row of a [rows, K] fp32 / bf16 matrix
+int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, int8_t* s1, float* scale,
+                      cudaStream_t st);
 // tokens per tcgen05 work item: 16 when every group fits (n <= 16), else 128
 inline int tc_tok_tile(int n) { return n <= 16 ? 16 : 128; }
 // CTAs per work item: 128-token tiles run on an SM pair (tcgen05 cta_group::2,

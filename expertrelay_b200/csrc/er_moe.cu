@@ -1,8 +1,9 @@
 // er_moe.cu -- er_moe_block: the whole MoE block (runtime/qwen_moe.py:293-359)
 // as a fixed sequence of device launches with no host synchronisation, so
 // the call can be captured in a CUDA graph:
-//   K1 router logits (+ shared-gate logit) -> K1 softmax/top-k
-//   K2 plan: expert-sorted (token, slot) list and work-item schedules
+//   K1 router logits (+ shared-gate logit) -> K1 softmax/top-k (+ per-expert counts)
+//   K2 plan: expert ranges and work-item schedules -> dispatch: expert-sorted
+//      (token, slot) positions (and, for the tensor-core path, h's int8 slices)
 //   K3 gate/up + SwiGLU, K3 down (grouped GEMV for decode, GEMM otherwise)
 //   K4 combine in ascending expert order + gated shared expert
 #include "er_internal.cuh"
@@ -154,18 +155,18 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   float* logits_sum = io->logits_out;
   if (io->logits_in) {
     if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit,
-                                      &gparts, st))
+                                      &gparts, plan->tally, E, st))
       return rc;
     lg = io->logits_in;  // one whole set of logits
     if (logits_sum == io->logits_in) logits_sum = nullptr;
   } else {
     if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, w->router_w, w->shared_gate_w, E, logits, gate_logit,
-                                      &nparts, st))
+                                      &nparts, plan->tally, E, st))
       return rc;
     gparts = nparts;
   }
   if (int rc = launch_router_topk(lg, nparts, gparts, n, E, k, w->norm_topk_prob, io->topk_idx_out, idx32, topw,
-                                  gate_logit, gate_sig, logits_sum, st))
+                                  gate_logit, gate_sig, logits_sum, plan->tally, st))
     return rc;
   launches += 2;
   if (io->topk_w_out) {
@@ -187,10 +188,15 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
   }
   if (int rc = mark(1)) return rc;
-  if (int rc = launch_plan(idx32, topw, n, k, E, H, w->inter, w->shared_inter, specs, plan, perm_token, perm_w, pos_of,
-                           st))
+  if (int rc = launch_plan(n, k, E, H, w->inter, w->shared_inter, specs, plan, st)) return rc;
+  const size_t nk = (size_t)n * k;
+  int8_t* xs0 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs0) : nullptr;
+  int8_t* xs1 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs1) : nullptr;
+  float* xscale = path == ER_PATH_TC ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
+  if (int rc = launch_dispatch(io->h, io->h_dtype, idx32, topw, n, k, E, H, plan, perm_token, perm_w, pos_of, xs0, xs1,
+                               xscale, st))
     return rc;
-  launches += 1;
+  launches += 2;
   if (int rc = mark(2)) return rc;
 
   GroupArgs ga;
@@ -214,10 +220,6 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   // instance of the routed format when it is int4
   const int per_stage = (w->expert_fmt == ER_FMT_INT8 || path == ER_PATH_TC) ? 1 : 2;
   if (path == ER_PATH_TC) {
-    const size_t nk = (size_t)n * k;
-    int8_t* xs0 = reinterpret_cast<int8_t*>(ws + L.xs0);
-    int8_t* xs1 = reinterpret_cast<int8_t*>(ws + L.xs1);
-    float* xscale = reinterpret_cast<float*>(ws + L.xscale);
     int8_t* as0_r = reinterpret_cast<int8_t*>(ws + L.as0_r);
     int8_t* as1_r = reinterpret_cast<int8_t*>(ws + L.as1_r);
     float* ascale_r = reinterpret_cast<float*>(ws + L.ascale_r);
@@ -232,9 +234,6 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.nk = (int)nk;
     tl.n = n;
     tl.tok_tile = tc_tok_tile(n);
-    // slices of h (and the act row maxima cleared for the gate/up epilogue)
-    if (int rc = launch_slice_rows(io->h, io->h_dtype, perm_token, (int)nk, (int)nk + n, H, 0, xs0, xs1, xscale, st))
-      return rc;
     tl.mode = 0;
     tl.sched = 0;
     tl.b0_r = xs0;
@@ -245,10 +244,8 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.items_bound = b0;
     if (int rc = launch_tc_grouped(tl, st)) return rc;
     if (int rc = mark(3)) return rc;
-    if (int rc = launch_slice_rows(act_r, ER_DTYPE_F32, nullptr, 0, (int)nk, w->inter, 1, as0_r, as1_r, ascale_r, st))
-      return rc;
-    if (int rc = launch_slice_rows(act_s, ER_DTYPE_F32, nullptr, 0, n, w->shared_inter, 1, as0_s, as1_s, ascale_s, st))
-      return rc;
+    if (int rc = launch_slice_rows(act_r, ER_DTYPE_F32, (int)nk, w->inter, as0_r, as1_r, ascale_r, st)) return rc;
+    if (int rc = launch_slice_rows(act_s, ER_DTYPE_F32, n, w->shared_inter, as0_s, as1_s, ascale_s, st)) return rc;
     tl.mode = 1;
     tl.sched = 1;
     tl.b0_r = as0_r;
@@ -261,7 +258,7 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.out_s = y_s;
     tl.items_bound = b1;
     if (int rc = launch_tc_grouped(tl, st)) return rc;
-    launches += 3;  // the three slice launches; the two GEMMs are counted below
+    launches += 2;  // the two act slice launches; the two GEMMs are counted below
   } else if (path == ER_PATH_GEMV) {
     if (int rc = launch_gemv_grouped(ga, 0, 0, io->h, io->h_dtype, act_r, act_s, nullptr, nullptr, b0, st)) return rc;
     if (int rc = mark(3)) return rc;

@@ -2,185 +2,192 @@
 //
 // Reference: runtime/qwen_moe.py:341-344. The reference loops over
 // np.unique(selected) (ascending expert id) and, per expert, takes
-// np.nonzero(selected == e): the (token, slot) pairs in row-major order.
-// This kernel produces the same grouping as one expert-sorted array: the
-// pairs of expert 0 first, then expert 1, ..., each expert's pairs in
-// row-major (token, slot) order. It also lays out the work items of the
-// grouped expert kernels over the active experts (and the shared expert).
+// np.nonzero(selected == e): the (token, slot) pairs routed to it. Here the
+// pairs of each expert occupy one contiguous range of an expert-sorted array
+// (expert 0's range first), laid out in two launches:
+//   plan_kernel     per-expert counts (tallied by the top-k kernel) ->
+//                   ranges, the active groups, the work-item schedules;
+//   dispatch_kernel one warp per token claims a position in each of its k
+//                   experts' ranges (an atomic cursor per expert) and, for the
+//                   tensor-core path, slices the token's h row once into the
+//                   int8 operand rows of those positions and of the shared
+//                   expert's row nk + t.
+// The order of the pairs inside one expert's range follows the atomics, not
+// the token order; nothing downstream depends on it: every output element is
+// computed from its own token's row alone, and the combine sums each token's
+// slots in ascending expert id through pos_of.
 #include "er_internal.cuh"
 
 namespace er {
 
-constexpr int kPlanThreads = 1024;
-constexpr int kPlanWarps = kPlanThreads / 32;
-
-// One CTA. Warp w owns the contiguous entries [w * span, (w + 1) * span) of the
-// row-major (token, slot) list. (1) each warp counts its entries per expert;
-// (2) per expert, an exclusive prefix over the warps; per-expert offsets and
-// the work-item schedules; (3) each warp walks its entries again and places
-// entry i at offsets[e] + (entries of e in earlier warps) + (earlier entries
-// of e in this warp): the same stable order as np.nonzero per expert.
-__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __restrict__ idx,
-                                                            const float* __restrict__ w, int n, int k, int E,
-                                                            int H, int I, int Is, SchedSpec s0, SchedSpec s1,
-                                                            Plan* __restrict__ plan,
-                                                            int32_t* __restrict__ perm_token,
-                                                            float* __restrict__ perm_w,
-                                                            int32_t* __restrict__ pos_of) {
-  __shared__ int cnt[kPlanWarps][kMaxExperts];  // per-warp counts, then running bases
+// One warp. Lane l owns entries 9l .. 9l+8 of the per-expert lists (enough
+// for E + 2 <= 258) and the scans run over the lanes.
+__global__ void __launch_bounds__(32) plan_kernel(int n, int k, int E, int H, int I, int Is, SchedSpec s0,
+                                                  SchedSpec s1, Plan* __restrict__ plan) {
   __shared__ int hist[kMaxExperts];
-  __shared__ int base[kMaxExperts];
   __shared__ int act[kMaxExperts + 1];
-  __shared__ int bad;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kPer = 9;
+  const int lane = threadIdx.x;
   const int nk = n * k;
-  const int span = (nk + kPlanWarps * 32 - 1) / (kPlanWarps * 32) * 32;
-  const int beg = warp * span, end = min(nk, beg + span);
-  for (int i = tid; i < kPlanWarps * kMaxExperts; i += kPlanThreads) cnt[i / kMaxExperts][i % kMaxExperts] = 0;
-  if (tid == 0) bad = 0;
-  __syncthreads();
-  // the warp's entries are fetched kBatch rows of 32 at a time with independent
-  // loads, so a batch costs one memory round trip
-  constexpr int kBatch = 16;
-  for (int b0 = beg; b0 < end; b0 += 32 * kBatch) {
-    int ev[kBatch];
+  auto warp_excl_scan = [&](int v) {  // exclusive prefix of v over the lanes
+    int incl = v;
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int i = b0 + 32 * j + lane;
-      ev[j] = i < end ? __ldg(idx + i) : -1;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
     }
+    return incl - v;
+  };
+  for (int e = lane; e < E; e += 32) hist[e] = plan->tally[e];
+  __syncwarp();
+  int sum = 0, nact = 0;
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int i = b0 + 32 * j + lane;
-      int e = ev[j];
-      if (i < end && (e < 0 || e >= E)) {
-        bad = 1;
-        e = -1;
-      }
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
-      if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
-      __syncwarp();
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane * kPer + j;
+    if (e < E) {
+      sum += hist[e];
+      nact += hist[e] > 0;
     }
   }
-  __syncthreads();
-  for (int e = tid; e < E; e += kPlanThreads) {
-    int run = 0;
-    for (int w2 = 0; w2 < kPlanWarps; ++w2) {
-      const int c = cnt[w2][e];
-      cnt[w2][e] = run;
-      run += c;
+  int off = warp_excl_scan(sum), pos = warp_excl_scan(nact);
+  const int total = __shfl_sync(0xffffffffu, off + sum, 31);
+  const int na_routed = __shfl_sync(0xffffffffu, pos + nact, 31);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane * kPer + j;
+    if (e < E) {
+      plan->counts[e] = hist[e];
+      plan->offsets[e] = off;
+      plan->cursor[e] = off;  // dispatch_kernel claims positions from here
+      off += hist[e];
+      if (hist[e] > 0) act[pos++] = e;
     }
-    hist[e] = run;
   }
-  __syncthreads();
-  if (warp == 0) {
-    // Warp 0 builds the offsets, the active list and the schedules with
-    // warp scans (lane l owns entries 9l .. 9l+8, enough for E + 2 <= 258).
-    constexpr int kPer = 9;
-    auto warp_excl_scan = [&](int v) {  // exclusive prefix of v over the lanes; also returns the total
-      int incl = v;
+  // every pair lands in some expert's range: the counts must add up to n * k
+  const bool bad = total != nk;
+  const int na = na_routed + (n > 0 ? 1 : 0);
+  if (lane == 0) {
+    if (n > 0) act[na_routed] = E;
+    plan->counts[E] = n;
+    plan->offsets[E] = 0;
+  }
+  __syncwarp();
+  for (int a = lane; a < na; a += 32) plan->active[a] = act[a];
+  const SchedSpec specs[kNumSched] = {s0, s1};
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      return incl - v;
-    };
-    int sum = 0, nact = 0;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int e = lane * kPer + j;
-      if (e < E) {
-        sum += hist[e];
-        nact += hist[e] > 0;
-      }
-    }
-    int off = warp_excl_scan(sum), pos = warp_excl_scan(nact);
-    const int na_routed = __shfl_sync(0xffffffffu, pos + nact, 31);
+  for (int s = 0; s < kNumSched; ++s) {
+    const SchedSpec sp = specs[s];
+    int items[kPer], local = 0;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-      const int e = lane * kPer + j;
-      if (e < E) {
-        base[e] = off;
-        off += hist[e];
-        if (hist[e] > 0) act[pos++] = e;
+      const int a = lane * kPer + j;
+      items[j] = 0;
+      if (a < na) {
+        const int g = act[a];
+        const int rows = g == E ? n : hist[g];
+        const int units = sp.which == 0 ? (g == E ? Is : I) : H;
+        const int mt = sp.bm > 0 ? (rows + sp.bm - 1) / sp.bm : 1;
+        items[j] = mt * ((units + sp.bn - 1) / sp.bn);
       }
+      local += items[j];
     }
-    const int na = na_routed + (n > 0 ? 1 : 0);
-    if (lane == 0 && n > 0) act[na_routed] = E;
-    __syncwarp();
-    for (int a = lane; a < na; a += 32) plan->active[a] = act[a];
-    const SchedSpec specs[kNumSched] = {s0, s1};
+    int start_a = warp_excl_scan(local);
 #pragma unroll
-    for (int s = 0; s < kNumSched; ++s) {
-      const SchedSpec sp = specs[s];
-      int items[kPer], local = 0;
+    for (int j = 0; j < kPer; ++j) {
+      const int a = lane * kPer + j;
+      if (a <= na) plan->item_start[s][a] = bad ? 0 : start_a;
+      start_a += items[j];
+    }
+  }
+  if (lane == 0) {
+    plan->n = n;
+    plan->E = E;
+    plan->k = k;
+    plan->nk = nk;
+    plan->error = bad;
+    plan->sched[0] = s0;
+    plan->sched[1] = s1;
+    plan->num_active = bad ? 0 : na;  // no work items on an inconsistent tally
+  }
+}
+
+// One warp per token t. Lane r < k claims the position of slot r; with
+// SLICE, the warp then slices h[t] (K = H values) and writes the slices to
+// the k claimed rows and to row nk + t. Rows of up to 2048 values stay in
+// registers; longer rows are read twice.
+template <typename XT, bool SLICE>
+__global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
+                                                       const float* __restrict__ w, int n, int k, int E, int H,
+                                                       Plan* __restrict__ plan, int32_t* __restrict__ perm_token,
+                                                       float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
+                                                       int8_t* __restrict__ s0, int8_t* __restrict__ s1,
+                                                       float* __restrict__ scale) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const int nk = n * k;
+  int p = -1;
+  if (lane < k) {
+    const int e = idx[(size_t)t * k + lane];
+    if (e >= 0 && e < E) {
+      p = atomicAdd(&plan->cursor[e], 1);
+      if (p < 0 || p >= nk) {  // only an inconsistent tally gets here
+        atomicOr(&plan->error, 2);
+        p = -1;
+      } else {
+        perm_token[p] = t;
+        perm_w[p] = w[(size_t)t * k + lane];
+      }
+    } else {
+      atomicOr(&plan->error, 1);
+    }
+    pos_of[(size_t)t * k + lane] = p;
+  }
+  if constexpr (SLICE) {
+    int prow[kMaxTopK + 1];
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int a = lane * kPer + j;
-        items[j] = 0;
-        if (a < na) {
-          const int g = act[a];
-          const int rows = g == E ? n : hist[g];
-          const int units = sp.which == 0 ? (g == E ? Is : I) : H;
-          const int mt = sp.bm > 0 ? (rows + sp.bm - 1) / sp.bm : 1;
-          items[j] = mt * ((units + sp.bn - 1) / sp.bn);
+    for (int r = 0; r < kMaxTopK; ++r) prow[r] = __shfl_sync(0xffffffffu, p, r < k ? r : 31);
+    prow[kMaxTopK] = nk + t;  // the shared expert's row
+    const XT* x = h + (size_t)t * H;
+    auto put = [&](int c, float4 v, float inv) {
+      uint32_t w0, w1;
+      slice4(v, inv, w0, w1);
+#pragma unroll
+      for (int r = 0; r <= kMaxTopK; ++r) {
+        const int row = r < kMaxTopK ? (r < k ? prow[r] : -1) : prow[kMaxTopK];
+        if (row >= 0) {
+          *reinterpret_cast<uint32_t*>(s0 + (size_t)row * H + c) = w0;
+          *reinterpret_cast<uint32_t*>(s1 + (size_t)row * H + c) = w1;
         }
-        local += items[j];
       }
-      int start_a = warp_excl_scan(local);
+    };
+    float amax = 0.f;
+    constexpr int kRegVec = 16;  // float4 per lane held in registers: H <= 2048
+    if (H <= 128 * kRegVec) {
+      float4 v[kRegVec];
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int a = lane * kPer + j;
-        if (a <= na) plan->item_start[s][a] = bad ? 0 : start_a;
-        start_a += items[j];
+      for (int i = 0; i < kRegVec; ++i) {
+        const int c = lane * 4 + 128 * i;
+        v[i] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, abs_max4(v[i]));
       }
-    }
-    if (lane == 0) {
-      plan->n = n;
-      plan->E = E;
-      plan->k = k;
-      plan->nk = nk;
-      plan->error = bad;
-      plan->sched[0] = s0;
-      plan->sched[1] = s1;
-      // no work items at all when an expert id was out of range: nothing
-      // downstream may read the unfilled permutation
-      plan->num_active = bad ? 0 : na;
-    }
-  }
-  __syncthreads();
-  for (int e = tid; e <= E; e += kPlanThreads) {
-    plan->counts[e] = e < E ? hist[e] : n;
-    plan->offsets[e] = e < E ? base[e] : 0;
-  }
-  if (bad) return;
-  const unsigned lt_mask = (1u << lane) - 1u;
-  for (int b0 = beg; b0 < end; b0 += 32 * kBatch) {
-    int ev[kBatch];
-    float wv[kBatch];
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int i = b0 + 32 * j + lane;
-      ev[j] = i < end ? __ldg(idx + i) : -1;
-      wv[j] = i < end ? __ldg(w + i) : 0.f;
-    }
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float inv = amax > 0.f ? 127.f / amax : 0.f;
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int i = b0 + 32 * j + lane;
-      const int e = ev[j];
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
-      int p = 0;
-      if (e >= 0) p = base[e] + cnt[warp][e] + __popc(peers & lt_mask);
-      __syncwarp();
-      if (e >= 0 && (__ffs(peers) - 1) == lane) cnt[warp][e] += __popc(peers);
-      __syncwarp();
-      if (e >= 0) {
-        perm_token[p] = i / k;
-        perm_w[p] = wv[j];
-        pos_of[i] = p;
+      for (int i = 0; i < kRegVec; ++i) {
+        const int c = lane * 4 + 128 * i;
+        if (c < H) put(c, v[i], inv);
       }
+    } else {
+      for (int c = lane * 4; c < H; c += 128) amax = fmaxf(amax, abs_max4(load4(x + c)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float inv = amax > 0.f ? 127.f / amax : 0.f;
+      for (int c = lane * 4; c < H; c += 128) put(c, load4(x + c), inv);
     }
+    if (lane < k && p >= 0) scale[p] = amax / 127.f;
+    if (lane == 31) scale[nk + t] = amax / 127.f;
   }
 }
 
@@ -200,12 +207,26 @@ long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int 
   return routed_rows_tiles * nt_r + shared_tiles * nt_s;
 }
 
-int launch_plan(const int32_t* idx, const float* w, int n, int k, int E, int H, int I, int Is,
-                const SchedSpec* specs, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of,
-                cudaStream_t st) {
-  plan_kernel<<<1, kPlanThreads, 0, st>>>(idx, w, n, k, E, H, I, Is, specs[0], specs[1], plan, perm_token, perm_w,
-                                          pos_of);
+int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, Plan* plan, cudaStream_t st) {
+  plan_kernel<<<1, 32, 0, st>>>(n, k, E, H, I, Is, specs[0], specs[1], plan);
   return launch_check("plan_kernel");
+}
+
+int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H,
+                    Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1,
+                    float* scale, cudaStream_t st) {
+  if (n <= 0) return ER_OK;
+  const int blocks = (n + 7) / 8;
+  if (!s0)
+    dispatch_kernel<float, false><<<blocks, 256, 0, st>>>(nullptr, idx, w, n, k, E, H, plan, perm_token, perm_w,
+                                                          pos_of, nullptr, nullptr, nullptr);
+  else if (h_dtype == ER_DTYPE_BF16)
+    dispatch_kernel<__nv_bfloat16, true><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)h, idx, w, n, k, E, H, plan,
+                                                                 perm_token, perm_w, pos_of, s0, s1, scale);
+  else
+    dispatch_kernel<float, true><<<blocks, 256, 0, st>>>((const float*)h, idx, w, n, k, E, H, plan, perm_token,
+                                                         perm_w, pos_of, s0, s1, scale);
+  return launch_check("dispatch_kernel");
 }
 
 }  // namespace er

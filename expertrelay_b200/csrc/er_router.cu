@@ -15,8 +15,11 @@ template <typename XT>
 __global__ void __launch_bounds__(256) router_rows_kernel(const XT* __restrict__ h, int n, int H,
                                                           const float* __restrict__ wr, const float* __restrict__ wg,
                                                           int E, float* __restrict__ logits,
-                                                          float* __restrict__ gate_logit) {
+                                                          float* __restrict__ gate_logit, int* __restrict__ tally,
+                                                          int ntally) {
   constexpr int kTok = kRouterTok;
+  if (blockIdx.x == 0 && tally)  // cleared for the top-k kernel's per-expert counts
+    for (int i = threadIdx.x; i < ntally; i += blockDim.x) tally[i] = 0;
   __shared__ float red[8][kTok];
   const int r = blockIdx.x;
   const float* w = (r < E) ? wr + (size_t)r * H : wg;
@@ -69,8 +72,11 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__
                                                           const float* __restrict__ wr,
                                                           const float* __restrict__ wg, int E,
                                                           float* __restrict__ logits,
-                                                          float* __restrict__ gate_logit) {
+                                                          float* __restrict__ gate_logit, int* __restrict__ tally,
+                                                          int ntally) {
   constexpr int BM = 32, BN = 64, BK = 16, KG = 4;
+  if (blockIdx.x == 0 && blockIdx.y == 0 && tally)  // cleared for the top-k kernel's per-expert counts
+    for (int i = threadIdx.x; i < ntally; i += blockDim.x) tally[i] = 0;
   struct Tiles {
     float A[KG][BK][BM + 4];
     float B[KG][BK][BN + 4];
@@ -183,7 +189,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
                                                           float* __restrict__ wout,
                                                           const float* __restrict__ gate_logit,
                                                           float* __restrict__ gate_sig,
-                                                          float* __restrict__ logits_sum) {
+                                                          float* __restrict__ logits_sum, int* __restrict__ tally) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= n) return;
@@ -257,6 +263,9 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     pw[r] = p;
     wsum += p;
   }
+  if (tally)  // lane r counts slot r's expert
+    for (int r = 0; r < k; ++r)
+      if (lane == r) atomicAdd(&tally[sel[r]], 1);
   if (lane == 0) {
     for (int r = 0; r < k; ++r) {
       const float w = norm ? pw[r] / wsum : pw[r];
@@ -273,37 +282,39 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 }
 
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
-                         float* logits, float* gate_logit, int* nparts, cudaStream_t st) {
+                         float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st) {
   *nparts = 1;
   if (n <= 0) return ER_OK;
   // E == 0: only the shared-gate row (the caller supplies router logits)
   if (n <= 64 || E + 1 > 64) {
     if (h_dtype == ER_DTYPE_BF16)
       router_rows_kernel<__nv_bfloat16><<<E + 1, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
-                                                                gate_logit);
+                                                                gate_logit, tally, ntally);
     else
-      router_rows_kernel<float><<<E + 1, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit);
+      router_rows_kernel<float><<<E + 1, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit, tally,
+                                                       ntally);
     return launch_check("router_rows_kernel");
   }
   *nparts = kRouterKSplit;
   const dim3 grid((n + 31) / 32, kRouterKSplit);
   if (h_dtype == ER_DTYPE_BF16)
     router_gemm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
-                                                             gate_logit);
+                                                             gate_logit, tally, ntally);
   else
-    router_gemm_kernel<float><<<grid, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit);
+    router_gemm_kernel<float><<<grid, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit, tally,
+                                                    ntally);
   return launch_check("router_gemm_kernel");
 }
 
 int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
                        int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
-                       cudaStream_t st) {
+                       int* tally, cudaStream_t st) {
   if (n <= 0) return ER_OK;
   const int warps_per_block = 8;
   const int blocks = (n + warps_per_block - 1) / warps_per_block;
   router_topk_kernel<<<blocks, warps_per_block * 32, 0, st>>>(logits, nparts, gparts, n, E, k, norm, idx64, idx32,
                                                                wout,
-                                                               gate_logit, gate_sig, logits_sum);
+                                                               gate_logit, gate_sig, logits_sum, tally);
   return launch_check("router_topk_kernel");
 }
 
@@ -318,5 +329,5 @@ extern "C" int er_router_topk(const float* logits, int n, int num_experts, int k
   if (k < 1 || k > kMaxTopK || k > num_experts)
     return fail(ER_EINVAL, "er_router_topk: k %d outside 1..min(%d, num_experts)", k, kMaxTopK);
   return launch_router_topk(logits, 1, 1, n, num_experts, k, 0, idx64, idx32, probs_out, nullptr, nullptr, nullptr,
-                            (cudaStream_t)stream);
+                            nullptr, (cudaStream_t)stream);
 }

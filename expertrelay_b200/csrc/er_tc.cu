@@ -274,50 +274,34 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // activation slicing
 // ---------------------------------------------------------------------------
 
-// One warp per output row: s = max|x| / 127, x0 = rint(x/s), x1 = rint((x/s - x0) * 256)
-// clamped to +-127. src_mode 0: row p < nk is h[perm_token[p]], row nk + t is
-// h[t]; src_mode 1: row p is src[p] (width K). Rows of up to 2048 values are
-// held in registers and read once; longer rows are read twice (max, then slices).
+// One warp per row of a [rows, K] matrix: s = max|x| / 127 and the two int8
+// slices (slice4). Rows of up to 2048 values are held in registers and read
+// once; longer rows are read twice (max, then slices).
 template <typename XT>
-__global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ src, const int32_t* __restrict__ perm_token,
-                                                         int nk, int rows, int K, int src_mode,
+__global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ src, int rows, int K,
                                                          int8_t* __restrict__ s0, int8_t* __restrict__ s1,
                                                          float* __restrict__ scale) {
   constexpr int kRegVec = 16;  // float4 per lane held in registers: K <= 2048
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const XT* x;
-  if (src_mode == 0)
-    x = src + (size_t)(row < nk ? perm_token[row] : row - nk) * K;
-  else
-    x = src + (size_t)row * K;
+  const XT* x = src + (size_t)row * K;
   int8_t* d0 = s0 + (size_t)row * K;
   int8_t* d1 = s1 + (size_t)row * K;
   auto emit = [&](int k, float4 v, float inv) {
-    const float f[4] = {v.x, v.y, v.z, v.w};
-    int i0[4], i1[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float y = f[j] * inv;
-      const float q0 = rintf(y);
-      i0[j] = (int)q0;
-      i1[j] = max(-127, min(127, __float2int_rn((y - q0) * 256.f)));
-    }
-    // pack the low bytes of four ints (first in the lowest byte)
-    const uint32_t w0 = __byte_perm(__byte_perm(i0[0], i0[1], 0x0040), __byte_perm(i0[2], i0[3], 0x0040), 0x5410);
-    const uint32_t w1 = __byte_perm(__byte_perm(i1[0], i1[1], 0x0040), __byte_perm(i1[2], i1[3], 0x0040), 0x5410);
+    uint32_t w0, w1;
+    slice4(v, inv, w0, w1);
     *reinterpret_cast<uint32_t*>(d0 + k) = w0;
     *reinterpret_cast<uint32_t*>(d1 + k) = w1;
   };
+  float amax = 0.f;
   if (K <= 128 * kRegVec) {
     float4 v[kRegVec];
-    float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < kRegVec; ++i) {
       const int k = lane * 4 + 128 * i;
       v[i] = k < K ? load4(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+      amax = fmaxf(amax, abs_max4(v[i]));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -327,18 +311,13 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ 
       const int k = lane * 4 + 128 * i;
       if (k < K) emit(k, v[i], inv);
     }
-    if (lane == 0) scale[row] = amax / 127.f;
-    return;
-  }
-  float amax = 0.f;
-  for (int k = lane * 4; k < K; k += 128) {
-    const float4 v = load4(x + k);
-    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-  }
+  } else {
+    for (int k = lane * 4; k < K; k += 128) amax = fmaxf(amax, abs_max4(load4(x + k)));
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float inv = amax > 0.f ? 127.f / amax : 0.f;
-  for (int k = lane * 4; k < K; k += 128) emit(k, load4(x + k), inv);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+    for (int k = lane * 4; k < K; k += 128) emit(k, load4(x + k), inv);
+  }
   if (lane == 0) scale[row] = amax / 127.f;
 }
 
@@ -904,16 +883,14 @@ static int launch_tc_mode(const TcMaps& maps, const TcArgs& t, long long items_b
   return launch_check("tc_expert_gemm_kernel");
 }
 
-int launch_slice_rows(const void* src, int dtype, const int32_t* perm_token, int nk, int rows, int K, int src_mode,
-                      int8_t* s0, int8_t* s1, float* scale, cudaStream_t st) {
+int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, int8_t* s1, float* scale,
+                      cudaStream_t st) {
   if (rows <= 0) return ER_OK;
   const int blocks = (rows + 7) / 8;
   if (dtype == ER_DTYPE_BF16)
-    slice_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)src, perm_token, nk, rows, K,
-                                                             src_mode, s0, s1, scale);
+    slice_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)src, rows, K, s0, s1, scale);
   else
-    slice_rows_kernel<float><<<blocks, 256, 0, st>>>((const float*)src, perm_token, nk, rows, K, src_mode, s0, s1,
-                                                     scale);
+    slice_rows_kernel<float><<<blocks, 256, 0, st>>>((const float*)src, rows, K, s0, s1, scale);
   return launch_check("slice_rows_kernel");
 }
 

@@ -82,3 +82,18 @@ def test_moe_weights_validation_and_workspace_query():
     bad4 = _lib.MoeWeights.from_buffer_copy(w)
     bad4.expert_fmt, bad4.group = 1, 100
     assert L.er_moe_block(C.byref(bad4), C.byref(io), None, 0, None) == _lib.ER_EINVAL
+
+
+# fixed device scratch of er_moe_block_noalloc (csrc/er_moe_noalloc.cu)
+NOALLOC_SCRATCH_BYTES = 8 << 20
+
+
+def test_noalloc_token_limit_at_qwen_shapes():
+    """er_moe_block_noalloc serves a batch when its er_moe_workspace_bytes
+    fits the fixed 8 MiB scratch: at Qwen1.5-MoE-A2.7B shapes (60 experts,
+    top-4, default path) that is up to 96 tokens, the limit its header states."""
+    L = _lib.lib()
+    w = _lib.MoeWeights(hidden=2048, num_experts=60, top_k=4, inter=1408, shared_inter=5632, expert_fmt=0, group=0,
+                        norm_topk_prob=0, router_w=16, shared_gate_w=16, expert_records=16, shared_record=256)
+    assert L.er_moe_workspace_bytes(C.byref(w), 96, _lib.PATH_AUTO) <= NOALLOC_SCRATCH_BYTES
+    assert L.er_moe_workspace_bytes(C.byref(w), 97, _lib.PATH_AUTO) > NOALLOC_SCRATCH_BYTES

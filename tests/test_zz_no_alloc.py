@@ -48,17 +48,26 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cuda):
         assert err < TOL, f"rel-L2 {err:.2e} between the two entry points"
 
 
+# the fixed scratch of er_moe_block_noalloc (csrc/er_moe_noalloc.cu)
+SCRATCH_BYTES = 8 << 20
+
+
 def test_noalloc_refuses_batches_beyond_its_scratch(cuda):
     block = synth.make_block(2, num_experts=8)
     mb = MoeBlock.from_host_block(block, device=cuda)
-    h = torch.zeros((98, block.hidden), dtype=torch.float32, device=cuda)
-    y = torch.full((98, block.hidden), 7.0, device=cuda)
-    io = _lib.MoeIO(h=h.data_ptr(), h_dtype=_lib.DTYPE_F32, n=98, y=y.data_ptr(), path=_lib.PATH_AUTO)
+    # the largest batch whose workspace fits the scratch: it runs, one more is refused
+    fit = 1
+    while mb.workspace_bytes(fit + 1) <= SCRATCH_BYTES:
+        fit += 1
+    over = fit + 1
+    h = torch.zeros((over, block.hidden), dtype=torch.float32, device=cuda)
+    y = torch.full((over, block.hidden), 7.0, device=cuda)
+    io = _lib.MoeIO(h=h.data_ptr(), h_dtype=_lib.DTYPE_F32, n=over, y=y.data_ptr(), path=_lib.PATH_AUTO)
     rc = _lib.lib().er_moe_block_noalloc(C.byref(mb._w), C.byref(io), None)
     assert rc == _lib.ER_ENOSPACE and "fixed scratch" in _lib.last_error()
     torch.cuda.synchronize()
     assert bool((y == 7.0).all()), "nothing may be written when the batch is refused"
-    ok = torch.from_numpy(synth.make_tokens(3, 97, block.hidden)).to(cuda)
+    ok = torch.from_numpy(synth.make_tokens(3, fit, block.hidden)).to(cuda)
     ref = mb.forward(ok)
     got = _noalloc(mb, ok, _lib.PATH_AUTO)
     torch.cuda.synchronize()
