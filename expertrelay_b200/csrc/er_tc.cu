@@ -370,14 +370,20 @@ struct TcPlanCache {
 // CG = CTAs per item (1: one SM; 2: an SM pair, cta_group::2). Per stage a CTA
 // holds its 128 weight rows and, on one SM, both slices (N = TT + npad), on a
 // pair only its own slice (CTA r: slice r; the pair's MMA has N = 2 TT).
+//
+// A stage holds kKC 128-byte K chunks (each a 128-byte-swizzled tile of its
+// own): [A chunk 0][A chunk 1].. then [B chunk 0][B chunk 1]..
 template <int MODE, int TT, int CG>
 struct TcGeom {
-  static constexpr int kABytes = 16384;
-  static constexpr int kBSliceBytes = TT * 128;
-  static constexpr int kBBytes = (3 - CG) * kBSliceBytes;
+  static constexpr int kKC = 2;                  // 128-byte K chunks per stage
+  static constexpr int kAChunkBytes = 16384;     // 128 weight rows x 128 bytes
+  static constexpr int kABytes = kKC * kAChunkBytes;
+  static constexpr int kBSliceBytes = TT * 128;  // one slice, one chunk
+  static constexpr int kBChunkBytes = (3 - CG) * kBSliceBytes;
+  static constexpr int kBBytes = kKC * kBChunkBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTxBytes = CG * kStageBytes;  // bytes completing on the (CTA 0) full barrier per stage
-  static constexpr int kStages = CG == 2 ? 6 : (TT >= 128 ? 4 : 9);
+  static constexpr int kStages = (TT >= 128 ? 196608 : 184320) / kStageBytes;
   static constexpr int kCtaUnits = MODE == 0 ? 64 : 128;  // this CTA's intermediate columns / hidden rows
   static constexpr int kUnits = CG * kCtaUnits;           // per item
   static constexpr size_t kRingBytes = (size_t)kStages * kStageBytes;
@@ -447,7 +453,7 @@ __device__ __forceinline__ bool tc_item(const TcArgs& t, const TcPlanCache* pc, 
   const int inter = it.shared ? t.g.Is : t.g.I;
   it.units = MODE == 0 ? inter : t.g.H;
   const int K = MODE == 0 ? t.g.H : inter;
-  it.nkb = (K + 127) / 128;
+  it.nkb = (K + 128 * Geo::kKC - 1) / (128 * Geo::kKC);
   const int ntiles = (it.units + Geo::kUnits - 1) / Geo::kUnits;
   it.tok0 = (local / ntiles) * TT;
   it.unit0 = (local % ntiles) * Geo::kUnits;
@@ -543,27 +549,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           // then, and the phase cannot complete without CTA 0's arrival)
           if (leader) mbar_expect_tx(&full[s], Geo::kTxBytes);
           const uint32_t fc = CG == 2 ? mapa_shared(smem_u32(&full[s]), 0) : 0u;
-          const int x = kb * 128;
-          if (MODE == 0) {
-            if (it.shared) {
-              tma_2d<CG>(st, &maps.a_shared[0], &full[s], fc, x, arow);
-              tma_2d<CG>(st + 8192, &maps.a_shared[1], &full[s], fc, x, arow);
-            } else {
-              tma_3d<CG>(st, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
-              tma_3d<CG>(st + 8192, &maps.a_routed[1], &full[s], fc, x, arow, it.slot);
-            }
-          } else {
-            if (it.shared)
-              tma_2d<CG>(st, &maps.a_shared[0], &full[s], fc, x, arow);
-            else
-              tma_3d<CG>(st, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
-          }
           const CUtensorMap* b = (MODE == 1 && it.shared) ? maps.b_shared : maps.b_routed;
-          if (CG == 1) {
-            tma_2d<CG>(st + Geo::kABytes, &b[0], &full[s], fc, x, it.brow0);
-            tma_2d<CG>(st + Geo::kABytes + Geo::kBSliceBytes, &b[1], &full[s], fc, x, it.brow0);
-          } else {
-            tma_2d<CG>(st + Geo::kABytes, &b[rank], &full[s], fc, x, it.brow0);
+#pragma unroll
+          for (int c = 0; c < Geo::kKC; ++c) {
+            // chunks past K read as zeros (out-of-bounds fill) and add nothing
+            const int x = (kb * Geo::kKC + c) * 128;
+            uint8_t* sa = st + c * Geo::kAChunkBytes;
+            uint8_t* sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
+            if (MODE == 0) {
+              if (it.shared) {
+                tma_2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow);
+                tma_2d<CG>(sa + 8192, &maps.a_shared[1], &full[s], fc, x, arow);
+              } else {
+                tma_3d<CG>(sa, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
+                tma_3d<CG>(sa + 8192, &maps.a_routed[1], &full[s], fc, x, arow, it.slot);
+              }
+            } else {
+              if (it.shared)
+                tma_2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow);
+              else
+                tma_3d<CG>(sa, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
+            }
+            if (CG == 1) {
+              tma_2d<CG>(sb, &b[0], &full[s], fc, x, it.brow0);
+              tma_2d<CG>(sb + Geo::kBSliceBytes, &b[1], &full[s], fc, x, it.brow0);
+            } else {
+              tma_2d<CG>(sb, &b[rank], &full[s], fc, x, it.brow0);
+            }
           }
         }
         __syncwarp();
@@ -615,9 +627,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         if (lane == 0) {
           const uint32_t st = smem_u32(smem + s * Geo::kStageBytes);
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_i8<CG>(d, umma_desc_sw128(st + ks * 32), umma_desc_sw128(st + Geo::kABytes + ks * 32), idesc,
-                       (kb > 0 || ks > 0) ? 1u : 0u);
+          for (int c = 0; c < Geo::kKC; ++c) {
+            const uint32_t sa = st + c * Geo::kAChunkBytes, sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              mma_i8<CG>(d, umma_desc_sw128(sa + ks * 32), umma_desc_sw128(sb + ks * 32), idesc,
+                         (kb > 0 || c > 0 || ks > 0) ? 1u : 0u);
+          }
           umma_commit<CG>(&empty[s]);  // frees the stage (in both CTAs of a pair) once these MMAs have read it
         }
         __syncwarp();
