@@ -64,6 +64,32 @@ class MoeIO(C.Structure):
 
 MOE_STAGES = ("router", "plan", "gate_up", "down", "combine")
 
+CACHE_DRY = 1
+SLOT_FREE, SLOT_LOADING, SLOT_READY = 0, 1, 2
+
+
+class CacheStats(C.Structure):
+    """struct er_cache_stats (the counters of SourceStats, runtime/weights.py:170-193)."""
+
+    _fields_ = [
+        (name, C.c_longlong)
+        for name in (
+            "loads",
+            "bytes_read",
+            "demand_reads",
+            "cache_hits",
+            "prefetch_hits",
+            "prefetch_waits",
+            "prefetches_issued",
+            "prefetch_reads",
+            "prefetch_bytes",
+            "prefetches_wasted",
+            "prefetches_cancelled",
+            "prefetches_skipped_full",
+            "prefetches_skipped_budget",
+        )
+    ]
+
 
 # name -> (restype, argtypes); every function declared in include/expertrelay_b200.h
 SIGNATURES: dict[str, tuple] = {
@@ -82,6 +108,17 @@ SIGNATURES: dict[str, tuple] = {
     "er_moe_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_block": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp, C.c_size_t, _vp]),
     "er_moe_block_noalloc": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp]),
+    "er_cache_create": (_i, [_i, C.c_size_t, _i, _vp, _i, C.POINTER(_vp)]),
+    "er_cache_destroy": (_i, [_vp]),
+    "er_cache_info": (_i, [_vp, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_size_t), C.POINTER(_vp)]),
+    "er_cache_set_source": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
+    "er_cache_pin": (_i, [_vp, _i, _i]),
+    "er_cache_acquire": (_i, [_vp, _i, C.POINTER(_i), _i, _vp, C.POINTER(C.c_uint64)]),
+    "er_cache_prefetch": (_i, [_vp, _i, C.POINTER(_i), _i, C.POINTER(_i), _i, _i]),
+    "er_cache_end_layer": (_i, [_vp, _i, _vp]),
+    "er_cache_resize": (_i, [_vp, _i, _vp, C.POINTER(_i)]),
+    "er_cache_lookup": (_i, [_vp, _i, _i, C.POINTER(_i), C.POINTER(_i)]),
+    "er_cache_stats_get": (_i, [_vp, C.POINTER(CacheStats)]),
 }
 
 _lib: C.CDLL | None = None

@@ -126,6 +126,28 @@ class MoeBlock:
         self._w.record_arena = base
         self._w.arena_slots = int(slots or 0)
 
+    def use_arena(self, base: int, slots: int) -> None:
+        """Serve the routed records from an external arena of `slots` records
+        starting at device address `base` (an HbmExpertCache's); the expert
+        table must then point into it."""
+        self.records = None
+        self._set_arena(int(base), int(slots))
+
+    def router_logits(self, h: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """h @ router^T in fp32 ([n, E]); also what the next layer's router on
+        this layer's input gives for a Fate-style prefetch guess."""
+        _require_cuda(h, "h")
+        if h.dtype != torch.float32 or not h.is_contiguous():
+            h = h.float().contiguous()
+        n = h.shape[0]
+        if out is None:
+            out = torch.empty((n, self.num_experts), dtype=torch.float32, device=h.device)
+        stream = torch.cuda.current_stream(h.device).cuda_stream
+        rc = _lib.lib().er_linear_f32(h.data_ptr(), self.hidden, self.router.data_ptr(), None, out.data_ptr(), n,
+                                      self.num_experts, self.hidden, stream)
+        _lib.check(rc, "er_linear_f32")
+        return out
+
     def set_expert_table(self, addresses: torch.Tensor) -> None:
         """Device addresses of each expert's record (e.g. HBM cache slots)."""
         if addresses.numel() != self.num_experts:

@@ -1,0 +1,82 @@
+"""PagedMoeStack: MoE layers whose routed experts live in an HbmExpertCache.
+
+The runtime's cache hooks around the MoE block (runtime/qwen_moe.py:
+293-351), on the GPU: per layer, the router and top-k run on the device, the
+selected expert ids come back to the host, the cache makes those records
+resident (copies from pinned host memory on its copy stream, which the
+compute stream waits for) and the block runs on them through its expert
+table. With a prefetch policy, the next layer's router applied to this
+layer's input (the Fate guess, qwen_moe.py:314-320) picks experts whose
+copies start while this layer computes, keeping this layer's experts
+(qwen_moe.py:326-336).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib
+from .cache import HbmExpertCache
+from .moe import MoeBlock
+from .prefetch import PrefetchPolicy
+
+
+class PagedMoeStack:
+    """blocks: one HostBlock-like per layer (router, shared_gate, shared,
+    shared_inter, layout, top_k); their routed records are the cache's
+    source (HostRecords.from_blocks)."""
+
+    def __init__(
+        self,
+        blocks,
+        cache: HbmExpertCache,
+        *,
+        prefetcher: PrefetchPolicy | None = None,
+        norm_topk_prob: bool = False,
+    ):
+        self.cache = cache
+        self.prefetcher = prefetcher
+        self.prefetch_enabled = prefetcher is not None
+        self.layers = [
+            MoeBlock(router=b.router, shared_gate=b.shared_gate, shared=b.shared, layout=b.layout,
+                     shared_inter=b.shared_inter, records=None, top_k=b.top_k, norm_topk_prob=norm_topk_prob,
+                     device=cache.device)
+            for b in blocks
+        ]
+        self.num_experts = self.layers[0].num_experts
+        self.top_k = self.layers[0].top_k
+        self.prefetches_skipped_low_confidence = 0
+
+    def moe(self, layer: int, h: torch.Tensor, path: int = _lib.PATH_AUTO) -> torch.Tensor:
+        """One layer's MoE block output for h [n, H] (the layer's QwenMoe._moe)."""
+        blk = self.layers[layer]
+        cache = self.cache
+        n = h.shape[0]
+        logits = blk.router_logits(h)
+        idx = torch.empty((n, self.top_k), dtype=torch.int64, device=h.device)
+        stream = torch.cuda.current_stream(h.device).cuda_stream
+        rc = _lib.lib().er_router_topk(logits.data_ptr(), n, self.num_experts, self.top_k, idx.data_ptr(), None,
+                                       None, stream)
+        _lib.check(rc, "er_router_topk")
+        needed = np.unique(idx.cpu().numpy())  # the host decides which records to fetch
+        addrs = cache.acquire(layer, needed)
+        table = np.full(self.num_experts, int(addrs[0]), dtype=np.uint64)  # unrouted experts: never read
+        table[needed] = addrs
+        blk.use_arena(cache.arena_base, cache.num_slots)
+        blk.set_expert_table(torch.from_numpy(table.view(np.int64)))
+        if self.prefetch_enabled and layer + 1 < len(self.layers):
+            fate = self.layers[layer + 1].router_logits(h).cpu().numpy()
+            choice = self.prefetcher.choose(fate)
+            self.prefetches_skipped_low_confidence += choice.skipped_low_confidence
+            cache.prefetch(layer + 1, choice.experts, keep=[(layer, int(e)) for e in needed])
+        y = blk.forward(h, logits=logits, path=path)
+        cache.end_layer(layer)
+        return y
+
+    def forward(self, h: torch.Tensor, path: int = _lib.PATH_AUTO) -> torch.Tensor:
+        """All layers in order, each adding its MoE output to the residual
+        stream: h <- h + moe_l(h)."""
+        for layer in range(len(self.layers)):
+            h = h + self.moe(layer, h, path)
+        return h

@@ -23,6 +23,7 @@
  *   er_moe_block       runtime/qwen_moe.py:293-359        QwenMoe._moe
  *   er_record_*        store/layout.py:53-115, store/int4.py:165-244
  *                                                         expert record layouts
+ *   er_cache_*         cache/expert_cache.py:92-402       CachedExpertSource (HBM slots)
  */
 #ifndef EXPERTRELAY_B200_H
 #define EXPERTRELAY_B200_H
@@ -154,6 +155,89 @@ ER_API size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path);
 ER_API int er_moe_block_noalloc(const er_moe_weights* w, const er_moe_io* io, void* stream);
 ER_API int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
                  void* stream);
+
+/* ------------------------------------------------------------------------
+ * HBM expert cache: replaces CachedExpertSource (cache/expert_cache.py:92-402).
+ *
+ * A fixed number of slots, each one store record (record_bytes), in one
+ * device arena; keys are (layer, expert). Records come from pinned host
+ * memory (er_cache_set_source) by cudaMemcpyAsync on the cache's own copy
+ * stream, each fill followed by the slot's ready event; a stream that uses a
+ * slot waits on that event, so an expert whose copy is still in flight is
+ * waited for, never copied twice (expert_cache.py:271-279). Eviction takes the
+ * least recently used ready slot that the current layer does not hold and
+ * that is not pinned (expert_cache.py:172-191); a refill waits on the slot's
+ * last-use event, so kernels still reading the old record finish first.
+ * Not thread-safe per cache: one host thread drives it, like the reference's
+ * forward pass.
+ * ---------------------------------------------------------------------- */
+typedef struct er_cache er_cache;
+
+/* cumulative counters, the fields of SourceStats (runtime/weights.py:170-193) */
+typedef struct er_cache_stats {
+  long long loads;                     /* experts handed to the forward pass (er_cache_acquire) */
+  long long bytes_read;                /* bytes of demand fills */
+  long long demand_reads;              /* fills started by er_cache_acquire */
+  long long cache_hits;                /* resident, not from an unused prefetch */
+  long long prefetch_hits;             /* resident thanks to a finished prefetch */
+  long long prefetch_waits;            /* a prefetch's copy was still in flight: waited on it */
+  long long prefetches_issued;
+  long long prefetch_reads;            /* prefetch copies seen complete */
+  long long prefetch_bytes;
+  long long prefetches_wasted;         /* prefetched, evicted before any use */
+  long long prefetches_cancelled;      /* always 0: a copy in the stream is not withdrawn */
+  long long prefetches_skipped_full;   /* no evictable slot */
+  long long prefetches_skipped_budget; /* over max_new_reads */
+} er_cache_stats;
+
+#define ER_CACHE_DRY 1 /* bookkeeping only: no device memory, copies or events; fills complete at once */
+
+#define ER_SLOT_FREE 0
+#define ER_SLOT_LOADING 1
+#define ER_SLOT_READY 2
+
+/* slots >= min_free_slots (else ER_ENOSPACE, the reference's CacheTooSmall,
+ * expert_cache.py:104-113). arena: caller-owned device memory of
+ * slots * record_bytes, 256-byte aligned, or NULL to let the cache allocate it.
+ * record_bytes: a multiple of 256. */
+ER_API int er_cache_create(int slots, size_t record_bytes, int min_free_slots, void* arena, int flags,
+                           er_cache** out);
+ER_API int er_cache_destroy(er_cache* c);
+/* the arena's base address, slot count and record size; the copy stream (cudaStream_t) */
+ER_API int er_cache_info(const er_cache* c, void** arena, int* slots, size_t* record_bytes, void** copy_stream);
+/* host_records[layer * experts + expert]: pinned host address of that record */
+ER_API int er_cache_set_source(er_cache* c, int layers, int experts, const void* const* host_records);
+/* load now and never evict (the reference's `pinned`, expert_cache.py:150-158);
+ * ER_ENOSPACE when fewer than min_free_slots slots would stay unpinned */
+ER_API int er_cache_pin(er_cache* c, int layer, int expert);
+/* The forward pass's loads for one layer (expert_cache.py:203-262, batched):
+ * makes every listed expert resident (starting fills as needed), makes
+ * `stream` wait for their copies, and writes each record's device address to
+ * records_out[i]. The slots stay held until er_cache_end_layer(layer).
+ * ER_ENOSPACE when no slot can be freed (CacheTooSmall). */
+ER_API int er_cache_acquire(er_cache* c, int layer, const int* experts, int count, void* stream,
+                            uint64_t* records_out);
+/* Background loads (expert_cache.py:264-294): touches the (layer, expert)
+ * pairs in keep[2 * keep_count] and each listed expert already resident;
+ * starts at most max_new_reads fills (< 0: no limit) into free or evictable
+ * slots, counting skips like the reference. */
+ER_API int er_cache_prefetch(er_cache* c, int layer, const int* experts, int count, const int* keep, int keep_count,
+                             int max_new_reads);
+/* done with `layer` for this call (expert_cache.py:296-305): releases its held
+ * slots; their last use is recorded on `stream` for later refills */
+ER_API int er_cache_end_layer(er_cache* c, int layer, void* stream);
+/* Change the slot count between forward calls (expert_cache.py:307-354):
+ * waits for copies in flight and for kernels using the slots, keeps the pinned
+ * experts and then the most recently used ones, and moves them into a new
+ * arena of `slots` slots: `new_arena` (caller-owned from then on; the caller
+ * frees the old one after the call) or, when NULL, one the cache allocates
+ * (only if it allocated the old one). ER_ENOSPACE (nothing changed) when the
+ * pinned experts plus min_free_slots would not fit; ER_EINVAL while a layer
+ * holds slots. */
+ER_API int er_cache_resize(er_cache* c, int slots, void* new_arena, int* slots_out);
+/* slot and ER_SLOT_* state of a key (slot -1 when absent); polls its copy */
+ER_API int er_cache_lookup(er_cache* c, int layer, int expert, int* slot, int* state);
+ER_API int er_cache_stats_get(er_cache* c, er_cache_stats* out);
 
 #ifdef __cplusplus
 }
