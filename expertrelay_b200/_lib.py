@@ -62,6 +62,21 @@ class MoeIO(C.Structure):
     ]
 
 
+class MoeRowsIO(C.Structure):
+    """struct er_moe_rows_io."""
+
+    _fields_ = [
+        ("x", _vp),
+        ("x_dtype", _i),
+        ("m", _i),
+        ("expert", _vp),
+        ("weight", _vp),
+        ("y", _vp),
+        ("path", _i),
+        ("launch_count", C.POINTER(_i)),
+    ]
+
+
 MOE_STAGES = ("router", "plan", "gate_up", "down", "combine")
 
 CACHE_DRY = 1
@@ -108,6 +123,13 @@ SIGNATURES: dict[str, tuple] = {
     "er_moe_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_block": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp, C.c_size_t, _vp]),
     "er_moe_block_noalloc": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp]),
+    "er_moe_rows_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
+    "er_moe_rows": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeRowsIO), _vp, C.c_size_t, _vp]),
+    "er_moe_shared_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
+    "er_moe_shared": (_i, [C.POINTER(MoeWeights), _vp, _i, _i, _vp, _i, _vp, C.c_size_t, _vp]),
+    "er_moe_combine": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "er_ep_count": (_i, [_vp, _i, _i, _vp, _i, _i, _vp, _vp]),
+    "er_ep_pack": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "er_cache_create": (_i, [_i, C.c_size_t, _i, _vp, _i, C.POINTER(_vp)]),
     "er_cache_destroy": (_i, [_vp]),
     "er_cache_info": (_i, [_vp, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_size_t), C.POINTER(_vp)]),

@@ -176,12 +176,13 @@ int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void
 // out[t] = sum over the token's k routed outputs in ascending expert id (the
 // reference accumulates experts in that order, runtime/qwen_moe.py:341-349)
 // + the gated shared-expert output (:359).
+// y_s may be NULL (no shared term); error (optional): nonzero turns the rows into NaN.
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y_r, const float* __restrict__ y_s,
                                                       const int32_t* __restrict__ pos_of,
                                                       const int32_t* __restrict__ idx, int k, int H,
-                                                      const Plan* __restrict__ plan, float* __restrict__ out) {
+                                                      const int* __restrict__ error, float* __restrict__ out) {
   const int t = blockIdx.x;
-  if (plan->error) {
+  if (error && *error) {
     for (int c = threadIdx.x; c < H; c += blockDim.x) out[(size_t)t * H + c] = __int_as_float(0x7fc00000);
     return;
   }
@@ -210,19 +211,21 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
       acc.z += v.z;
       acc.w += v.w;
     }
-    const float4 sv = *reinterpret_cast<const float4*>(y_s + (size_t)t * H + c);
-    acc.x += sv.x;
-    acc.y += sv.y;
-    acc.z += sv.z;
-    acc.w += sv.w;
+    if (y_s) {
+      const float4 sv = *reinterpret_cast<const float4*>(y_s + (size_t)t * H + c);
+      acc.x += sv.x;
+      acc.y += sv.y;
+      acc.z += sv.z;
+      acc.w += sv.w;
+    }
     *reinterpret_cast<float4*>(out + (size_t)t * H + c) = acc;
   }
 }
 
-int launch_combine_plan(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k,
-                        int H, const Plan* plan, float* out, cudaStream_t st) {
+int launch_combine(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k, int H,
+                   const int* error, float* out, cudaStream_t st) {
   if (n <= 0) return ER_OK;
-  combine_kernel<<<n, 256, 0, st>>>(y_r, y_s, pos_of, idx, k, H, plan, out);
+  combine_kernel<<<n, 256, 0, st>>>(y_r, y_s, pos_of, idx, k, H, error, out);
   return launch_check("combine_kernel");
 }
 

@@ -114,14 +114,17 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
 int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
                        int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
                        int* tally, cudaStream_t st);
-// groups, offsets and work-item schedules from plan->tally (one warp)
-int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, Plan* plan, cudaStream_t st);
+// groups, offsets and work-item schedules from plan->tally (one warp); the
+// shared expert (all n tokens) is the last group when `shared` is nonzero
+int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, int shared, Plan* plan,
+                cudaStream_t st);
 // Scatter of the (token, slot) pairs to expert-sorted positions (perm_token,
 // perm_w, pos_of). With s0 non-null also slices each token's h row once and
-// writes the slices to its k routed positions and to shared row nk + t.
+// writes the slices to its k routed positions and, when `shared` is nonzero,
+// to shared row nk + t.
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H,
-                    Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1,
-                    float* scale, cudaStream_t st);
+                    int shared, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0,
+                    int8_t* s1, float* scale, cudaStream_t st);
 // Upper bound of the items a schedule can produce (host side, for grid sizing).
 long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int I, int Is);
 
@@ -130,8 +133,14 @@ int launch_gemv_grouped(const GroupArgs& a, int sched, int mode, const void* x, 
 int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void* x, int x_dtype,
                              float* act_r, float* act_s, float* out_r, float* out_s,
                              long long items_bound, cudaStream_t st);
-int launch_combine_plan(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k,
-                        int H, const Plan* plan, float* out, cudaStream_t st);
+// out[t] = sum over t's k slots, in ascending expert id (idx), of y_r[pos_of[t * k + j]]
+// (+ y_s[t] when y_s is not NULL); rows of NaN when *error is nonzero
+int launch_combine(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k, int H,
+                   const int* error, float* out, cudaStream_t st);
+// per-expert counts of ids[0..m) into tally[E] (cleared first); out-of-range ids are not counted
+int launch_tally(const int32_t* ids, int m, int E, int* tally, cudaStream_t st);
+// gate_sig[t] = sigmoid(sum of the nparts partial shared-gate logits of token t)
+int launch_gate_sigmoid(const float* gate_logit, int nparts, int n, float* gate_sig, cudaStream_t st);
 
 // tcgen05 grouped GEMM (er_tc.cu)
 struct TcLaunch {
@@ -144,6 +153,7 @@ struct TcLaunch {
   int tok_tile;                // tokens per work item: 16 (decode batches) or 128
   const int8_t *b0_r, *b1_r;   // B slices: mode 0 all nk + n rows of h; mode 1 routed act rows
   const int8_t *b0_s, *b1_s;   // mode 1: shared act rows
+  int has_shared;              // the shared expert is one of the groups (its maps are needed)
   const float *xscale_r, *xscale_s;
   float *out_r, *out_s;
   long long items_bound;

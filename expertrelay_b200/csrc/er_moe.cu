@@ -1,14 +1,41 @@
-// er_moe.cu -- er_moe_block: the whole MoE block (runtime/qwen_moe.py:293-359)
-// as a fixed sequence of device launches with no host synchronisation, so
-// the call can be captured in a CUDA graph:
+// er_moe.cu -- the MoE block (runtime/qwen_moe.py:293-359) as a fixed sequence
+// of device launches with no host synchronisation, so a call can be captured
+// in a CUDA graph:
 //   K1 router logits (+ shared-gate logit) -> K1 softmax/top-k (+ per-expert counts)
 //   K2 plan: expert ranges and work-item schedules -> dispatch: expert-sorted
 //      (token, slot) positions (and, for the tensor-core path, h's int8 slices)
-//   K3 gate/up + SwiGLU, K3 down (grouped GEMV for decode, GEMM otherwise)
+//   K3 gate/up + SwiGLU, K3 down (grouped GEMV, SIMT GEMM or tcgen05 GEMM)
 //   K4 combine in ascending expert order + gated shared expert
+// The same runner serves two parts of the block for expert parallelism:
+// er_moe_rows (routed experts on rows that already carry an expert id and a
+// weight: K2-K4 with one slot per row and no shared expert) and er_moe_shared
+// (the gated shared expert alone: K1's shared gate, K2-K4 with no routed slot).
 #include "er_internal.cuh"
 
 namespace er {
+
+enum RunMode { kBlock = 0, kRows = 1, kShared = 2 };
+
+struct Run {
+  int mode;
+  const void* h;  // tokens (kRows: the rows)
+  int h_dtype;
+  int n;
+  const float* logits_in;
+  float* y;
+  float* logits_out;
+  int64_t* topk_idx_out;
+  float* topk_w_out;
+  const int32_t* row_expert;  // kRows
+  const float* row_weight;    // kRows
+  int path;
+  void* const* stage_events;
+  int* launch_count;
+};
+
+// routed slots per token and whether the shared expert runs
+static int run_k(const er_moe_weights* w, int mode) { return mode == kBlock ? w->top_k : (mode == kRows ? 1 : 0); }
+static bool run_shared(int mode) { return mode != kRows; }
 
 struct WsLayout {
   size_t logits, gate_logit, gate_sig, idx32, topw, plan, perm_token, perm_w, pos_of, act_r, act_s, y_r, y_s;
@@ -17,7 +44,7 @@ struct WsLayout {
   size_t total;
 };
 
-static WsLayout ws_layout(const er_moe_weights* w, int n, int path) {
+static WsLayout ws_layout(const er_moe_weights* w, int n, int path, int mode) {
   WsLayout L{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -25,37 +52,39 @@ static WsLayout ws_layout(const er_moe_weights* w, int n, int path) {
     off = align_up(off + bytes, 256);
     return o;
   };
-  const size_t nk = (size_t)n * w->top_k;
-  L.logits = take((size_t)kRouterKSplit * n * w->num_experts * 4);  // partial sums of K slices
-  L.gate_logit = take((size_t)kRouterKSplit * n * 4);
-  L.gate_sig = take((size_t)n * 4);
-  L.idx32 = take(nk * 4);
-  L.topw = take(nk * 4);
+  const size_t nk = (size_t)n * run_k(w, mode);
+  const size_t ns = run_shared(mode) ? (size_t)n : 0;  // rows through the shared expert
+  const size_t nl = mode == kBlock ? (size_t)n : 0;    // rows with router logits
+  L.logits = take((size_t)kRouterKSplit * nl * w->num_experts * 4);  // partial sums of K slices
+  L.gate_logit = take((size_t)kRouterKSplit * ns * 4);
+  L.gate_sig = take(ns * 4);
+  L.idx32 = take(mode == kBlock ? nk * 4 : 0);
+  L.topw = take(mode == kBlock ? nk * 4 : 0);
   L.plan = take(sizeof(Plan));
   L.perm_token = take(nk * 4);
   L.perm_w = take(nk * 4);
   L.pos_of = take(nk * 4);
   L.act_r = take(nk * w->inter * 4);
-  L.act_s = take((size_t)n * w->shared_inter * 4);
+  L.act_s = take(ns * w->shared_inter * 4);
   L.y_r = take(nk * w->hidden * 4);
-  L.y_s = take((size_t)n * w->hidden * 4);
+  L.y_s = take(ns * w->hidden * 4);
   if (path == ER_PATH_TC) {
-    const size_t rows = nk + n;
+    const size_t rows = nk + ns;
     L.xs0 = take(rows * w->hidden);
     L.xs1 = take(rows * w->hidden);
     L.xscale = take(rows * 4);
     L.as0_r = take(nk * w->inter);
     L.as1_r = take(nk * w->inter);
     L.ascale_r = take(nk * 4);
-    L.as0_s = take((size_t)n * w->shared_inter);
-    L.as1_s = take((size_t)n * w->shared_inter);
-    L.ascale_s = take((size_t)n * 4);
+    L.as0_s = take(ns * w->shared_inter);
+    L.as1_s = take(ns * w->shared_inter);
+    L.ascale_s = take(ns * 4);
   }
   L.total = off;
   return L;
 }
 
-static int validate(const er_moe_weights* w) {
+static int validate(const er_moe_weights* w, int mode) {
   if (!w) return fail(ER_EINVAL, "er_moe: null weights");
   if (w->hidden <= 0 || w->hidden % 16)
     return fail(ER_EINVAL, "er_moe: hidden %d must be a positive multiple of 16", w->hidden);
@@ -64,7 +93,7 @@ static int validate(const er_moe_weights* w) {
                 w->shared_inter);
   if (w->num_experts < 1 || w->num_experts > kMaxExperts)
     return fail(ER_EINVAL, "er_moe: num_experts %d outside 1..%d", w->num_experts, kMaxExperts);
-  if (w->top_k < 1 || w->top_k > kMaxTopK || w->top_k > w->num_experts)
+  if (mode == kBlock && (w->top_k < 1 || w->top_k > kMaxTopK || w->top_k > w->num_experts))
     return fail(ER_EINVAL, "er_moe: top_k %d outside 1..min(%d, num_experts)", w->top_k, kMaxTopK);
   if (w->expert_fmt != ER_FMT_INT8 && w->expert_fmt != ER_FMT_INT4 && w->expert_fmt != ER_FMT_INT4_ZP)
     return fail(ER_EINVAL, "er_moe: unknown expert format %d", w->expert_fmt);
@@ -73,73 +102,70 @@ static int validate(const er_moe_weights* w) {
       return fail(ER_EINVAL, "er_moe: int4 group %d must be a multiple of 16 dividing hidden %d and inter %d",
                   w->group, w->hidden, w->inter);
   }
-  if (!w->router_w || !w->shared_gate_w || !w->expert_records || !w->shared_record)
-    return fail(ER_EINVAL, "er_moe: null weight pointer");
+  if (mode == kBlock && !w->router_w) return fail(ER_EINVAL, "er_moe: null router weights");
+  if (mode != kShared && !w->expert_records) return fail(ER_EINVAL, "er_moe: null expert record table");
+  if (mode != kRows && (!w->shared_gate_w || !w->shared_record))
+    return fail(ER_EINVAL, "er_moe: null shared-expert weights");
   if (((uintptr_t)w->router_w | (uintptr_t)w->shared_gate_w) & 15)
     return fail(ER_EINVAL, "er_moe: router / shared-gate weights must be 16-byte aligned");
   if ((uintptr_t)w->shared_record & 255) return fail(ER_EINVAL, "er_moe: shared record must be 256-byte aligned");
   return ER_OK;
 }
 
-static int pick_path(int path, int n) {
+// AUTO: the tensor-core path when it can run (int8 records in an arena),
+// else the weight-streaming GEMV for decode batches and the SIMT GEMM beyond.
+static int pick_path(const er_moe_weights* w, int path, int n) {
   if (path != ER_PATH_AUTO) return path;
+  if (w->expert_fmt == ER_FMT_INT8 && w->record_arena && w->arena_slots > 0) return ER_PATH_TC;
   return n <= kGemvMaxTok ? ER_PATH_GEMV : ER_PATH_GEMM;
 }
 
-}  // namespace er
-
-using namespace er;
-
-extern "C" size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path) {
-  if (validate(w) != ER_OK || n < 0) return 0;
-  return ws_layout(w, n, pick_path(path, n)).total;
-}
-
-extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
-                            void* stream) {
-  if (int rc = validate(w)) return rc;
-  if (!io) return fail(ER_EINVAL, "er_moe_block: null io");
-  const int n = io->n;
-  if (n < 0) return fail(ER_EINVAL, "er_moe_block: negative n");
+static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const int mode = r.mode;
+  if (int rc = validate(w, mode)) return rc;
+  const int n = r.n;
+  if (n < 0) return fail(ER_EINVAL, "er_moe: negative row count");
   if (n == 0) return ER_OK;
-  if (!io->h || !io->y) return fail(ER_EINVAL, "er_moe_block: null h or y");
-  if (io->h_dtype != ER_DTYPE_F32 && io->h_dtype != ER_DTYPE_BF16)
-    return fail(ER_EINVAL, "er_moe_block: unknown activation dtype %d", io->h_dtype);
-  if (((uintptr_t)io->h | (uintptr_t)io->y) & 15) return fail(ER_EINVAL, "er_moe_block: h and y must be 16-byte aligned");
-  const int path = pick_path(io->path, n);
+  if (!r.h || !r.y) return fail(ER_EINVAL, "er_moe: null input or output");
+  if (r.h_dtype != ER_DTYPE_F32 && r.h_dtype != ER_DTYPE_BF16)
+    return fail(ER_EINVAL, "er_moe: unknown activation dtype %d", r.h_dtype);
+  if (((uintptr_t)r.h | (uintptr_t)r.y) & 15)
+    return fail(ER_EINVAL, "er_moe: inputs and outputs must be 16-byte aligned");
+  if (mode == kRows && (!r.row_expert || !r.row_weight))
+    return fail(ER_EINVAL, "er_moe_rows: null expert ids or weights");
+  const int path = pick_path(w, r.path, n);
   if (path != ER_PATH_GEMV && path != ER_PATH_GEMM && path != ER_PATH_TC)
-    return fail(ER_EINVAL, "er_moe_block: unknown path %d", io->path);
+    return fail(ER_EINVAL, "er_moe: unknown path %d", r.path);
   if (path == ER_PATH_TC) {
     if (w->expert_fmt != ER_FMT_INT8)
-      return fail(ER_EINVAL, "er_moe_block: the tensor-core path takes int8 expert records");
-    if (!w->record_arena || w->arena_slots < 1 || ((uintptr_t)w->record_arena & 15))
-      return fail(ER_EINVAL, "er_moe_block: the tensor-core path needs the record arena (record_arena, arena_slots)");
+      return fail(ER_EINVAL, "er_moe: the tensor-core path takes int8 expert records");
+    if (mode != kShared && (!w->record_arena || w->arena_slots < 1 || ((uintptr_t)w->record_arena & 15)))
+      return fail(ER_EINVAL, "er_moe: the tensor-core path needs the record arena (record_arena, arena_slots)");
   }
-  const WsLayout L = ws_layout(w, n, path);
+  const WsLayout L = ws_layout(w, n, path, mode);
   if (!workspace || workspace_bytes < L.total)
-    return fail(ER_ENOSPACE, "er_moe_block: workspace %zu bytes, need %zu", workspace_bytes, L.total);
-  if ((uintptr_t)workspace & 255) return fail(ER_EINVAL, "er_moe_block: workspace must be 256-byte aligned");
+    return fail(ER_ENOSPACE, "er_moe: workspace %zu bytes, need %zu", workspace_bytes, L.total);
+  if ((uintptr_t)workspace & 255) return fail(ER_EINVAL, "er_moe: workspace must be 256-byte aligned");
 
-  cudaStream_t st = (cudaStream_t)stream;
   char* ws = static_cast<char*>(workspace);
   int launches = 0;
   cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
-  if (io->stage_events)
+  if (r.stage_events)
     if (int rc = cuda_check(cudaStreamIsCapturing(st, &capture), "cudaStreamIsCapturing")) return rc;
   auto mark = [&](int i) -> int {
-    if (!io->stage_events) return ER_OK;
+    if (!r.stage_events) return ER_OK;
     // under stream capture the record becomes an external event node, so the
     // graph's replays timestamp the stages too; outside capture a plain record
     const unsigned flags = capture == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
-    return cuda_check(cudaEventRecordWithFlags((cudaEvent_t)io->stage_events[i], st, flags), "cudaEventRecord");
+    return cuda_check(cudaEventRecordWithFlags((cudaEvent_t)r.stage_events[i], st, flags), "cudaEventRecord");
   };
   if (int rc = mark(0)) return rc;
-  const int H = w->hidden, E = w->num_experts, k = w->top_k;
+  const int H = w->hidden, E = w->num_experts, k = run_k(w, mode);
+  const bool shared = run_shared(mode);
+  const size_t nk = (size_t)n * k;
   float* logits = reinterpret_cast<float*>(ws + L.logits);
   float* gate_logit = reinterpret_cast<float*>(ws + L.gate_logit);
-  float* gate_sig = reinterpret_cast<float*>(ws + L.gate_sig);
-  int32_t* idx32 = reinterpret_cast<int32_t*>(ws + L.idx32);
-  float* topw = reinterpret_cast<float*>(ws + L.topw);
+  float* gate_sig = shared ? reinterpret_cast<float*>(ws + L.gate_sig) : nullptr;
   Plan* plan = reinterpret_cast<Plan*>(ws + L.plan);
   int32_t* perm_token = reinterpret_cast<int32_t*>(ws + L.perm_token);
   float* perm_w = reinterpret_cast<float*>(ws + L.perm_w);
@@ -147,35 +173,56 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   float* act_r = reinterpret_cast<float*>(ws + L.act_r);
   float* act_s = reinterpret_cast<float*>(ws + L.act_s);
   float* y_r = reinterpret_cast<float*>(ws + L.y_r);
-  float* y_s = reinterpret_cast<float*>(ws + L.y_s);
+  float* y_s = shared ? reinterpret_cast<float*>(ws + L.y_s) : nullptr;
+  const int32_t* idx32 = nullptr;  // expert id of each (token, slot)
+  const float* topw = nullptr;     // its routing weight
 
-  // K1: router (or only the shared-gate row when the caller supplies logits)
-  const float* lg = logits;
-  int nparts = 1, gparts = 1;
-  float* logits_sum = io->logits_out;
-  if (io->logits_in) {
-    if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit,
-                                      &gparts, plan->tally, E, st))
+  // K1: routing (the block), the shared gate alone, or the rows' expert counts
+  if (mode == kBlock) {
+    int32_t* idx = reinterpret_cast<int32_t*>(ws + L.idx32);
+    float* wts = reinterpret_cast<float*>(ws + L.topw);
+    const float* lg = logits;
+    int nparts = 1, gparts = 1;
+    float* logits_sum = r.logits_out;
+    if (r.logits_in) {
+      if (int rc = launch_router_logits(r.h, r.h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit,
+                                        &gparts, plan->tally, E, st))
+        return rc;
+      lg = r.logits_in;  // one whole set of logits
+      if (logits_sum == r.logits_in) logits_sum = nullptr;
+    } else {
+      if (int rc = launch_router_logits(r.h, r.h_dtype, n, H, w->router_w, w->shared_gate_w, E, logits, gate_logit,
+                                        &nparts, plan->tally, E, st))
+        return rc;
+      gparts = nparts;
+    }
+    if (int rc = launch_router_topk(lg, nparts, gparts, n, E, k, w->norm_topk_prob, r.topk_idx_out, idx, wts,
+                                    gate_logit, gate_sig, logits_sum, plan->tally, st))
       return rc;
-    lg = io->logits_in;  // one whole set of logits
-    if (logits_sum == io->logits_in) logits_sum = nullptr;
+    launches += 2;
+    if (r.topk_w_out) {
+      if (int rc = cuda_check(cudaMemcpyAsync(r.topk_w_out, wts, nk * 4, cudaMemcpyDeviceToDevice, st),
+                              "copy top-k weights"))
+        return rc;
+    }
+    idx32 = idx;
+    topw = wts;
+  } else if (mode == kShared) {
+    int gparts = 1;
+    if (int rc = launch_router_logits(r.h, r.h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit,
+                                      &gparts, nullptr, 0, st))
+      return rc;
+    if (int rc = launch_gate_sigmoid(gate_logit, gparts, n, gate_sig, st)) return rc;
+    if (int rc = cuda_check(cudaMemsetAsync(plan->tally, 0, (size_t)E * sizeof(int), st), "clear tally")) return rc;
+    launches += 2;
   } else {
-    if (int rc = launch_router_logits(io->h, io->h_dtype, n, H, w->router_w, w->shared_gate_w, E, logits, gate_logit,
-                                      &nparts, plan->tally, E, st))
-      return rc;
-    gparts = nparts;
-  }
-  if (int rc = launch_router_topk(lg, nparts, gparts, n, E, k, w->norm_topk_prob, io->topk_idx_out, idx32, topw,
-                                  gate_logit, gate_sig, logits_sum, plan->tally, st))
-    return rc;
-  launches += 2;
-  if (io->topk_w_out) {
-    if (int rc = cuda_check(cudaMemcpyAsync(io->topk_w_out, topw, (size_t)n * k * 4, cudaMemcpyDeviceToDevice, st),
-                            "copy top-k weights"))
-      return rc;
+    if (int rc = launch_tally(r.row_expert, n, E, plan->tally, st)) return rc;
+    launches += 1;
+    idx32 = r.row_expert;
+    topw = r.row_weight;
   }
 
-  // K2: plan
+  // K2: plan + dispatch
   SchedSpec specs[kNumSched];
   if (path == ER_PATH_GEMV) {
     specs[0] = SchedSpec{0, kGemvUnitsGU, 0};
@@ -188,13 +235,12 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
   }
   if (int rc = mark(1)) return rc;
-  if (int rc = launch_plan(n, k, E, H, w->inter, w->shared_inter, specs, plan, st)) return rc;
-  const size_t nk = (size_t)n * k;
+  if (int rc = launch_plan(n, k, E, H, w->inter, w->shared_inter, specs, shared, plan, st)) return rc;
   int8_t* xs0 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs0) : nullptr;
   int8_t* xs1 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs1) : nullptr;
   float* xscale = path == ER_PATH_TC ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
-  if (int rc = launch_dispatch(io->h, io->h_dtype, idx32, topw, n, k, E, H, plan, perm_token, perm_w, pos_of, xs0, xs1,
-                               xscale, st))
+  if (int rc = launch_dispatch(r.h, r.h_dtype, idx32, topw, n, k, E, H, shared, plan, perm_token, perm_w, pos_of,
+                               xs0, xs1, xscale, st))
     return rc;
   launches += 2;
   if (int rc = mark(2)) return rc;
@@ -232,7 +278,8 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.arena_slots = w->arena_slots;
     tl.record_bytes = er_record_bytes(ER_FMT_INT8, H, w->inter, 0);
     tl.nk = (int)nk;
-    tl.n = n;
+    tl.n = shared ? n : 0;
+    tl.has_shared = shared;
     tl.tok_tile = tc_tok_tile(n);
     tl.mode = 0;
     tl.sched = 0;
@@ -244,8 +291,14 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.items_bound = b0;
     if (int rc = launch_tc_grouped(tl, st)) return rc;
     if (int rc = mark(3)) return rc;
-    if (int rc = launch_slice_rows(act_r, ER_DTYPE_F32, (int)nk, w->inter, as0_r, as1_r, ascale_r, st)) return rc;
-    if (int rc = launch_slice_rows(act_s, ER_DTYPE_F32, n, w->shared_inter, as0_s, as1_s, ascale_s, st)) return rc;
+    if (nk > 0) {
+      if (int rc = launch_slice_rows(act_r, ER_DTYPE_F32, (int)nk, w->inter, as0_r, as1_r, ascale_r, st)) return rc;
+      launches += 1;
+    }
+    if (shared) {
+      if (int rc = launch_slice_rows(act_s, ER_DTYPE_F32, n, w->shared_inter, as0_s, as1_s, ascale_s, st)) return rc;
+      launches += 1;
+    }
     tl.mode = 1;
     tl.sched = 1;
     tl.b0_r = as0_r;
@@ -258,13 +311,12 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
     tl.out_s = y_s;
     tl.items_bound = b1;
     if (int rc = launch_tc_grouped(tl, st)) return rc;
-    launches += 2;  // the two act slice launches; the two GEMMs are counted below
   } else if (path == ER_PATH_GEMV) {
-    if (int rc = launch_gemv_grouped(ga, 0, 0, io->h, io->h_dtype, act_r, act_s, nullptr, nullptr, b0, st)) return rc;
+    if (int rc = launch_gemv_grouped(ga, 0, 0, r.h, r.h_dtype, act_r, act_s, nullptr, nullptr, b0, st)) return rc;
     if (int rc = mark(3)) return rc;
     if (int rc = launch_gemv_grouped(ga, 1, 1, nullptr, ER_DTYPE_F32, act_r, act_s, y_r, y_s, b1, st)) return rc;
   } else {
-    if (int rc = launch_gemm_simt_grouped(ga, 0, 0, io->h, io->h_dtype, act_r, act_s, nullptr, nullptr, b0, st))
+    if (int rc = launch_gemm_simt_grouped(ga, 0, 0, r.h, r.h_dtype, act_r, act_s, nullptr, nullptr, b0, st))
       return rc;
     if (int rc = mark(3)) return rc;
     if (int rc = launch_gemm_simt_grouped(ga, 1, 1, nullptr, ER_DTYPE_F32, act_r, act_s, y_r, y_s, b1, st))
@@ -273,8 +325,85 @@ extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* 
   launches += 2 * per_stage;
   if (int rc = mark(4)) return rc;
   // K4
-  if (int rc = launch_combine_plan(y_r, y_s, pos_of, idx32, n, k, H, plan, io->y, st)) return rc;
+  if (int rc = launch_combine(y_r, y_s, pos_of, idx32, n, k, H, &plan->error, r.y, st)) return rc;
   launches += 1;
-  if (io->launch_count) *io->launch_count += launches;
+  if (r.launch_count) *r.launch_count += launches;
   return mark(5);
+}
+
+}  // namespace er
+
+using namespace er;
+
+extern "C" size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path) {
+  if (validate(w, kBlock) != ER_OK || n < 0) return 0;
+  return ws_layout(w, n, pick_path(w, path, n), kBlock).total;
+}
+
+extern "C" int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (!io) return fail(ER_EINVAL, "er_moe_block: null io");
+  Run r{};
+  r.mode = kBlock;
+  r.h = io->h;
+  r.h_dtype = io->h_dtype;
+  r.n = io->n;
+  r.logits_in = io->logits_in;
+  r.y = io->y;
+  r.logits_out = io->logits_out;
+  r.topk_idx_out = io->topk_idx_out;
+  r.topk_w_out = io->topk_w_out;
+  r.path = io->path;
+  r.stage_events = io->stage_events;
+  r.launch_count = io->launch_count;
+  return run_moe(w, r, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" size_t er_moe_rows_workspace_bytes(const er_moe_weights* w, int m, int path) {
+  if (validate(w, kRows) != ER_OK || m < 0) return 0;
+  return ws_layout(w, m, pick_path(w, path, m), kRows).total;
+}
+
+extern "C" int er_moe_rows(const er_moe_weights* w, const er_moe_rows_io* io, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (!io) return fail(ER_EINVAL, "er_moe_rows: null io");
+  Run r{};
+  r.mode = kRows;
+  r.h = io->x;
+  r.h_dtype = io->x_dtype;
+  r.n = io->m;
+  r.y = io->y;
+  r.row_expert = io->expert;
+  r.row_weight = io->weight;
+  r.path = io->path;
+  r.launch_count = io->launch_count;
+  return run_moe(w, r, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" size_t er_moe_shared_workspace_bytes(const er_moe_weights* w, int n, int path) {
+  if (validate(w, kShared) != ER_OK || n < 0) return 0;
+  return ws_layout(w, n, pick_path(w, path, n), kShared).total;
+}
+
+extern "C" int er_moe_shared(const er_moe_weights* w, const void* h, int h_dtype, int n, float* y, int path,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  Run r{};
+  r.mode = kShared;
+  r.h = h;
+  r.h_dtype = h_dtype;
+  r.n = n;
+  r.y = y;
+  r.path = path;
+  return run_moe(w, r, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int er_moe_combine(const float* y_rows, const int32_t* pos_of, const int32_t* idx, const float* y_shared,
+                              int n, int k, int hidden, float* y, void* stream) {
+  if (n < 0 || k < 0 || k > kMaxTopK || hidden <= 0 || hidden % 4)
+    return fail(ER_EINVAL, "er_moe_combine: n %d, k %d (<= %d), hidden %d (a multiple of 4)", n, k, kMaxTopK, hidden);
+  if (n == 0) return ER_OK;
+  if (!y || (k > 0 && (!y_rows || !pos_of || !idx))) return fail(ER_EINVAL, "er_moe_combine: null argument");
+  if (((uintptr_t)y_rows | (uintptr_t)y_shared | (uintptr_t)y) & 15)
+    return fail(ER_EINVAL, "er_moe_combine: rows must be 16-byte aligned");
+  return launch_combine(y_rows, y_shared, pos_of, idx, n, k, hidden, nullptr, y, (cudaStream_t)stream);
 }

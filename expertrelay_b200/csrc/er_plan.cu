@@ -23,7 +23,7 @@ namespace er {
 // One warp. Lane l owns entries 9l .. 9l+8 of the per-expert lists (enough
 // for E + 2 <= 258) and the scans run over the lanes.
 __global__ void __launch_bounds__(32) plan_kernel(int n, int k, int E, int H, int I, int Is, SchedSpec s0,
-                                                  SchedSpec s1, Plan* __restrict__ plan) {
+                                                  SchedSpec s1, int shared, Plan* __restrict__ plan) {
   __shared__ int hist[kMaxExperts];
   __shared__ int act[kMaxExperts + 1];
   constexpr int kPer = 9;
@@ -65,9 +65,9 @@ __global__ void __launch_bounds__(32) plan_kernel(int n, int k, int E, int H, in
   }
   // every pair lands in some expert's range: the counts must add up to n * k
   const bool bad = total != nk;
-  const int na = na_routed + (n > 0 ? 1 : 0);
+  const int na = na_routed + (shared && n > 0 ? 1 : 0);
   if (lane == 0) {
-    if (n > 0) act[na_routed] = E;
+    if (shared && n > 0) act[na_routed] = E;
     plan->counts[E] = n;
     plan->offsets[E] = 0;
   }
@@ -118,7 +118,8 @@ __global__ void __launch_bounds__(32) plan_kernel(int n, int k, int E, int H, in
 template <typename XT, bool SLICE>
 __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
                                                        const float* __restrict__ w, int n, int k, int E, int H,
-                                                       Plan* __restrict__ plan, int32_t* __restrict__ perm_token,
+                                                       int shared, Plan* __restrict__ plan,
+                                                       int32_t* __restrict__ perm_token,
                                                        float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
                                                        int8_t* __restrict__ s0, int8_t* __restrict__ s1,
                                                        float* __restrict__ scale) {
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
     int prow[kMaxTopK + 1];
 #pragma unroll
     for (int r = 0; r < kMaxTopK; ++r) prow[r] = __shfl_sync(0xffffffffu, p, r < k ? r : 31);
-    prow[kMaxTopK] = nk + t;  // the shared expert's row
+    prow[kMaxTopK] = shared ? nk + t : -1;  // the shared expert's row
     const XT* x = h + (size_t)t * H;
     auto put = [&](int c, float4 v, float inv) {
       uint32_t w0, w1;
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
       for (int c = lane * 4; c < H; c += 128) put(c, load4(x + c), inv);
     }
     if (lane < k && p >= 0) scale[p] = amax / 127.f;
-    if (lane == 31) scale[nk + t] = amax / 127.f;
+    if (lane == 31 && shared) scale[nk + t] = amax / 127.f;
   }
 }
 
@@ -207,25 +208,42 @@ long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int 
   return routed_rows_tiles * nt_r + shared_tiles * nt_s;
 }
 
-int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, Plan* plan, cudaStream_t st) {
-  plan_kernel<<<1, 32, 0, st>>>(n, k, E, H, I, Is, specs[0], specs[1], plan);
+int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, int shared, Plan* plan,
+                cudaStream_t st) {
+  plan_kernel<<<1, 32, 0, st>>>(n, k, E, H, I, Is, specs[0], specs[1], shared, plan);
   return launch_check("plan_kernel");
 }
 
+__global__ void __launch_bounds__(256) tally_kernel(const int32_t* __restrict__ ids, int m, int E,
+                                                    int* __restrict__ tally) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= m) return;
+  const int e = ids[i];
+  if (e >= 0 && e < E) atomicAdd(&tally[e], 1);
+}
+
+int launch_tally(const int32_t* ids, int m, int E, int* tally, cudaStream_t st) {
+  if (int rc = cuda_check(cudaMemsetAsync(tally, 0, (size_t)E * sizeof(int), st), "clear tally")) return rc;
+  if (m <= 0) return ER_OK;
+  tally_kernel<<<(m + 255) / 256, 256, 0, st>>>(ids, m, E, tally);
+  return launch_check("tally_kernel");
+}
+
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H,
-                    Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1,
-                    float* scale, cudaStream_t st) {
+                    int shared, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0,
+                    int8_t* s1, float* scale, cudaStream_t st) {
   if (n <= 0) return ER_OK;
   const int blocks = (n + 7) / 8;
   if (!s0)
-    dispatch_kernel<float, false><<<blocks, 256, 0, st>>>(nullptr, idx, w, n, k, E, H, plan, perm_token, perm_w,
-                                                          pos_of, nullptr, nullptr, nullptr);
+    dispatch_kernel<float, false><<<blocks, 256, 0, st>>>(nullptr, idx, w, n, k, E, H, shared, plan, perm_token,
+                                                          perm_w, pos_of, nullptr, nullptr, nullptr);
   else if (h_dtype == ER_DTYPE_BF16)
-    dispatch_kernel<__nv_bfloat16, true><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)h, idx, w, n, k, E, H, plan,
-                                                                 perm_token, perm_w, pos_of, s0, s1, scale);
+    dispatch_kernel<__nv_bfloat16, true><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)h, idx, w, n, k, E, H,
+                                                                 shared, plan, perm_token, perm_w, pos_of, s0, s1,
+                                                                 scale);
   else
-    dispatch_kernel<float, true><<<blocks, 256, 0, st>>>((const float*)h, idx, w, n, k, E, H, plan, perm_token,
-                                                         perm_w, pos_of, s0, s1, scale);
+    dispatch_kernel<float, true><<<blocks, 256, 0, st>>>((const float*)h, idx, w, n, k, E, H, shared, plan,
+                                                         perm_token, perm_w, pos_of, s0, s1, scale);
   return launch_check("dispatch_kernel");
 }
 

@@ -281,6 +281,21 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   }
 }
 
+__global__ void __launch_bounds__(256) gate_sigmoid_kernel(const float* __restrict__ gate_logit, int nparts, int n,
+                                                           float* __restrict__ gate_sig) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  float gl = gate_logit[t];
+  for (int p = 1; p < nparts; ++p) gl += gate_logit[(size_t)p * n + t];  // slices in order, as the top-k kernel
+  gate_sig[t] = sigmoid_f(gl);
+}
+
+int launch_gate_sigmoid(const float* gate_logit, int nparts, int n, float* gate_sig, cudaStream_t st) {
+  if (n <= 0) return ER_OK;
+  gate_sigmoid_kernel<<<(n + 255) / 256, 256, 0, st>>>(gate_logit, nparts, n, gate_sig);
+  return launch_check("gate_sigmoid_kernel");
+}
+
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
                          float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st) {
   *nparts = 1;

@@ -919,34 +919,43 @@ int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
   const RecordGeom rg{ER_FMT_INT8, a.H, a.I, 1};
   const RecordGeom sg{ER_FMT_INT8, a.H, a.Is, 1};
   const uint8_t* arena = static_cast<const uint8_t*>(L.arena);
+  if (L.nk == 0 && !L.has_shared) return ER_OK;  // no rows at all
   const uint8_t* shr = a.shared_record;
   if (L.mode == 0) {
     // 64 gate rows + the same 64 up rows per item
-    if (int rc = make_map(&maps.a_routed[0], arena + rg.weight_offset(0), 3, a.H, a.I, L.arena_slots, a.H,
-                          L.record_bytes, 64, "gate"))
-      return rc;
-    if (int rc = make_map(&maps.a_routed[1], arena + rg.weight_offset(1), 3, a.H, a.I, L.arena_slots, a.H,
-                          L.record_bytes, 64, "up"))
-      return rc;
-    if (int rc = make_map(&maps.a_shared[0], shr + sg.weight_offset(0), 2, a.H, a.Is, 1, a.H, 0, 64, "shared gate"))
-      return rc;
-    if (int rc = make_map(&maps.a_shared[1], shr + sg.weight_offset(1), 2, a.H, a.Is, 1, a.H, 0, 64, "shared up"))
-      return rc;
+    if (L.nk > 0) {
+      if (int rc = make_map(&maps.a_routed[0], arena + rg.weight_offset(0), 3, a.H, a.I, L.arena_slots, a.H,
+                            L.record_bytes, 64, "gate"))
+        return rc;
+      if (int rc = make_map(&maps.a_routed[1], arena + rg.weight_offset(1), 3, a.H, a.I, L.arena_slots, a.H,
+                            L.record_bytes, 64, "up"))
+        return rc;
+    }
+    if (L.has_shared) {
+      if (int rc = make_map(&maps.a_shared[0], shr + sg.weight_offset(0), 2, a.H, a.Is, 1, a.H, 0, 64, "shared gate"))
+        return rc;
+      if (int rc = make_map(&maps.a_shared[1], shr + sg.weight_offset(1), 2, a.H, a.Is, 1, a.H, 0, 64, "shared up"))
+        return rc;
+    }
     const int rows_b = L.nk + L.n;
     if (int rc = make_map(&maps.b_routed[0], L.b0_r, 2, a.H, rows_b, 1, a.H, 0, TT, "x slice 0")) return rc;
     if (int rc = make_map(&maps.b_routed[1], L.b1_r, 2, a.H, rows_b, 1, a.H, 0, TT, "x slice 1")) return rc;
   } else {
-    if (int rc = make_map(&maps.a_routed[0], arena + rg.weight_offset(2), 3, a.I, a.H, L.arena_slots, a.I,
-                          L.record_bytes, 128, "down"))
-      return rc;
-    if (int rc = make_map(&maps.a_shared[0], shr + sg.weight_offset(2), 2, a.Is, a.H, 1, a.Is, 0, 128, "shared down"))
-      return rc;
+    if (L.nk > 0)
+      if (int rc = make_map(&maps.a_routed[0], arena + rg.weight_offset(2), 3, a.I, a.H, L.arena_slots, a.I,
+                            L.record_bytes, 128, "down"))
+        return rc;
+    if (L.has_shared)
+      if (int rc = make_map(&maps.a_shared[0], shr + sg.weight_offset(2), 2, a.Is, a.H, 1, a.Is, 0, 128, "shared down"))
+        return rc;
     if (L.nk > 0) {
       if (int rc = make_map(&maps.b_routed[0], L.b0_r, 2, a.I, L.nk, 1, a.I, 0, TT, "act slice 0")) return rc;
       if (int rc = make_map(&maps.b_routed[1], L.b1_r, 2, a.I, L.nk, 1, a.I, 0, TT, "act slice 1")) return rc;
     }
-    if (int rc = make_map(&maps.b_shared[0], L.b0_s, 2, a.Is, L.n, 1, a.Is, 0, TT, "shared act slice 0")) return rc;
-    if (int rc = make_map(&maps.b_shared[1], L.b1_s, 2, a.Is, L.n, 1, a.Is, 0, TT, "shared act slice 1")) return rc;
+    if (L.has_shared) {
+      if (int rc = make_map(&maps.b_shared[0], L.b0_s, 2, a.Is, L.n, 1, a.Is, 0, TT, "shared act slice 0")) return rc;
+      if (int rc = make_map(&maps.b_shared[1], L.b1_s, 2, a.Is, L.n, 1, a.Is, 0, TT, "shared act slice 1")) return rc;
+    }
   }
   TcArgs t;
   t.g = a;

@@ -1,0 +1,218 @@
+"""Expert parallelism for the MoE block: one process per GPU, the routed
+experts of a layer spread over the ranks, tokens staying on their rank.
+
+The reference computes every expert in one process (runtime/qwen_moe.py:
+340-359). Here rank r holds experts [lo_r, hi_r) (contiguous, sizes differing
+by at most one: 30/30 at 2 GPUs, 15 x 4 at 4, 8,8,8,8,7,7,7,7 at 8) and the
+replicated router, shared gate and shared expert. Per layer, on each rank:
+
+  1. route its tokens (router + softmax/top-k, same kernels as the block);
+  2. count the (token, slot) pairs bound for each rank and exchange the
+     counts (all-to-all of ints);
+  3. pack the pairs' token rows by destination and send them with their
+     local expert id and routing weight (all-to-all);
+  4. compute the received rows with its own experts (er_moe_rows);
+  5. send the results back (all-to-all), the reverse of 3;
+  6. add each token's slots in ascending expert id, plus the gated shared
+     expert computed locally (er_moe_shared, er_moe_combine).
+
+Every routed row's result depends only on that row, and the combine adds in
+the reference's order, so the output equals the single-GPU block's on the
+same router logits bit for bit.
+
+The collectives are torch.distributed's (NCCL over NVLink on GPUs); the
+steps on each rank are an `ops` object: EpCudaOps runs them through the
+library; tests may pass host implementations to exercise the exchange.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import MoeRowsIO, MoeWeights
+from .moe import MoeBlock
+from .store import FMT_INT8
+
+
+def expert_partition(num_experts: int, ranks: int) -> list[tuple[int, int]]:
+    """Contiguous [lo, hi) expert ranges per rank, the larger ones first."""
+    if ranks < 1 or num_experts < ranks:
+        raise ValueError(f"cannot spread {num_experts} experts over {ranks} ranks")
+    base, extra = divmod(num_experts, ranks)
+    out, lo = [], 0
+    for r in range(ranks):
+        hi = lo + base + (1 if r < extra else 0)
+        out.append((lo, hi))
+        lo = hi
+    return out
+
+
+def owner_tables(num_experts: int, ranks: int) -> tuple[np.ndarray, np.ndarray]:
+    """owner[e] = rank holding expert e; local[e] = its index on that rank."""
+    owner = np.empty(num_experts, dtype=np.int32)
+    local = np.empty(num_experts, dtype=np.int32)
+    for r, (lo, hi) in enumerate(expert_partition(num_experts, ranks)):
+        owner[lo:hi] = r
+        local[lo:hi] = np.arange(hi - lo, dtype=np.int32)
+    return owner, local
+
+
+class EpCudaOps:
+    """The per-rank steps on this rank's GPU, through the library. `block`: the
+    layer's HostBlock (router, shared expert, all routed records; only the
+    records of experts [lo, hi) are uploaded)."""
+
+    def __init__(self, block, rank: int, ranks: int, device, path: int = _lib.PATH_AUTO):
+        self.device = torch.device(device)
+        # AUTO resolved as the single-GPU block resolves it for int8 records in
+        # an arena (the tensor-core path), the same for the routed rows and the
+        # shared expert; for int4 records the library picks by row count
+        self.path = _lib.PATH_TC if path == _lib.PATH_AUTO and block.layout.fmt == FMT_INT8 else path
+        self.ranks = ranks
+        self.lo, self.hi = expert_partition(block.num_experts, ranks)[rank]
+        self.top_k, self.hidden, self.num_experts = block.top_k, block.hidden, block.num_experts
+        # router, shared gate and shared expert (replicated); no routed records here
+        self.full = MoeBlock(router=block.router, shared_gate=block.shared_gate, shared=block.shared,
+                             layout=block.layout, shared_inter=block.shared_inter, records=None, top_k=block.top_k,
+                             device=self.device)
+        owner, local = owner_tables(block.num_experts, ranks)
+        self.owner = torch.from_numpy(owner).to(self.device)
+        self.local = torch.from_numpy(local).to(self.device)
+        rs = block.layout.record_size
+        recs = block.records()[self.lo : self.hi]
+        self.records = torch.from_numpy(np.ascontiguousarray(recs)).to(self.device)
+        n_local = self.hi - self.lo
+        self.table = torch.arange(n_local, dtype=torch.int64, device=self.device) * rs + self.records.data_ptr()
+        fw = self.full._w
+        # this rank's experts as a block of n_local experts
+        self.w_rows = MoeWeights(
+            hidden=fw.hidden, num_experts=n_local, top_k=1, inter=fw.inter, shared_inter=fw.shared_inter,
+            expert_fmt=fw.expert_fmt, group=fw.group, norm_topk_prob=0, router_w=None, shared_gate_w=None,
+            expert_records=self.table.data_ptr(), shared_record=None,
+            record_arena=self.records.data_ptr() if block.layout.fmt == FMT_INT8 else None,
+            arena_slots=n_local if block.layout.fmt == FMT_INT8 else 0,
+        )
+        self.cursor = torch.zeros(ranks, dtype=torch.int32, device=self.device)
+        self._ws: torch.Tensor | None = None
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _workspace(self, nbytes: int) -> torch.Tensor:
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def route(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(router logits [n, E], expert ids int32 [n, k], weights [n, k])."""
+        n = h.shape[0]
+        logits = self.full.router_logits(h)
+        idx = torch.empty((n, self.top_k), dtype=torch.int32, device=self.device)
+        w = torch.empty((n, self.top_k), dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().er_router_topk(logits.data_ptr(), n, self.num_experts, self.top_k, None,
+                                             idx.data_ptr(), w.data_ptr(), self._stream()), "er_router_topk")
+        return logits, idx, w
+
+    def count(self, idx: torch.Tensor) -> torch.Tensor:
+        counts = torch.empty(self.ranks, dtype=torch.int32, device=self.device)
+        n = idx.shape[0]
+        _lib.check(_lib.lib().er_ep_count(idx.data_ptr(), n, self.top_k, self.owner.data_ptr(), self.num_experts,
+                                          self.ranks, counts.data_ptr(), self._stream()), "er_ep_count")
+        return counts
+
+    def pack(self, h: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor, total: int):
+        n = h.shape[0]
+        dtype = _lib.DTYPE_BF16 if h.dtype == torch.bfloat16 else _lib.DTYPE_F32
+        x_send = torch.empty((total, self.hidden), dtype=h.dtype, device=self.device)
+        e_send = torch.empty(total, dtype=torch.int32, device=self.device)
+        w_send = torch.empty(total, dtype=torch.float32, device=self.device)
+        pos_of = torch.empty((n, self.top_k), dtype=torch.int32, device=self.device)
+        _lib.check(_lib.lib().er_ep_pack(
+            h.data_ptr(), dtype, self.hidden, idx.data_ptr(), w.data_ptr(), n, self.top_k, self.owner.data_ptr(),
+            self.local.data_ptr(), self.num_experts, self.ranks, offsets.data_ptr(), self.cursor.data_ptr(),
+            x_send.data_ptr(), e_send.data_ptr(), w_send.data_ptr(), pos_of.data_ptr(), self._stream()),
+            "er_ep_pack")
+        return x_send, e_send, w_send, pos_of
+
+    def rows(self, x: torch.Tensor, expert: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        m = x.shape[0]
+        y = torch.empty((m, self.hidden), dtype=torch.float32, device=self.device)
+        if m == 0:
+            return y
+        ws = self._workspace(_lib.lib().er_moe_rows_workspace_bytes(C.byref(self.w_rows), m, self.path))
+        io = MoeRowsIO(x=x.data_ptr(), x_dtype=_lib.DTYPE_BF16 if x.dtype == torch.bfloat16 else _lib.DTYPE_F32,
+                       m=m, expert=expert.data_ptr(), weight=weight.data_ptr(), y=y.data_ptr(), path=self.path)
+        _lib.check(_lib.lib().er_moe_rows(C.byref(self.w_rows), C.byref(io), ws.data_ptr(), ws.numel(),
+                                          self._stream()), "er_moe_rows")
+        return y
+
+    def shared(self, h: torch.Tensor) -> torch.Tensor:
+        n = h.shape[0]
+        y = torch.empty((n, self.hidden), dtype=torch.float32, device=self.device)
+        if n == 0:
+            return y
+        w = self.full._w
+        ws = self._workspace(_lib.lib().er_moe_shared_workspace_bytes(C.byref(w), n, self.path))
+        dtype = _lib.DTYPE_BF16 if h.dtype == torch.bfloat16 else _lib.DTYPE_F32
+        _lib.check(_lib.lib().er_moe_shared(C.byref(w), h.data_ptr(), dtype, n, y.data_ptr(), self.path,
+                                            ws.data_ptr(), ws.numel(), self._stream()), "er_moe_shared")
+        return y
+
+    def combine(self, y_ret, pos_of, idx, y_s) -> torch.Tensor:
+        n = idx.shape[0]
+        y = torch.empty((n, self.hidden), dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().er_moe_combine(y_ret.data_ptr() if y_ret.numel() else None, pos_of.data_ptr(),
+                                             idx.data_ptr(), y_s.data_ptr(), n, self.top_k, self.hidden,
+                                             y.data_ptr(), self._stream()), "er_moe_combine")
+        return y
+
+
+class ExpertParallelMoe:
+    """One rank's part of an expert-parallel MoE layer (see the module
+    docstring). `ops` provides route/count/pack/rows/shared/combine on this
+    rank's tensors; `group` is the torch.distributed group (default: world)."""
+
+    def __init__(self, ops, *, group=None):
+        self.ops = ops
+        self.group = group
+        self.ranks = dist.get_world_size(group) if dist.is_initialized() else 1
+        if self.ranks != ops.ranks:
+            raise ValueError(f"ops are laid out for {ops.ranks} ranks, the group has {self.ranks}")
+        self.last_counts: tuple[list[int], list[int]] | None = None
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        if self.ranks == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, h):
+        ops = self.ops
+        _, idx, w = ops.route(h)
+        counts = ops.count(idx)
+        recv_counts = torch.empty_like(counts)
+        self._a2a(recv_counts, counts, None, None)
+        send = [int(c) for c in counts.cpu().tolist()]
+        recv = [int(c) for c in recv_counts.cpu().tolist()]
+        self.last_counts = (send, recv)
+        offsets = torch.tensor(np.concatenate([[0], np.cumsum(send)[:-1]]).astype(np.int32), device=counts.device)
+        x_send, e_send, w_send, pos_of = ops.pack(h, idx, w, offsets, sum(send))
+        hidden = x_send.shape[1]
+        x_recv = torch.empty((sum(recv), hidden), dtype=x_send.dtype, device=x_send.device)
+        e_recv = torch.empty(sum(recv), dtype=e_send.dtype, device=e_send.device)
+        w_recv = torch.empty(sum(recv), dtype=w_send.dtype, device=w_send.device)
+        self._a2a(x_recv, x_send, recv, send)
+        self._a2a(e_recv, e_send, recv, send)
+        self._a2a(w_recv, w_send, recv, send)
+        y_recv = ops.rows(x_recv, e_recv, w_recv)
+        y_ret = torch.empty((sum(send), hidden), dtype=y_recv.dtype, device=y_recv.device)
+        self._a2a(y_ret, y_recv, send, recv)
+        y_s = ops.shared(h)
+        return ops.combine(y_ret, pos_of, idx, y_s)
+
+    __call__ = forward

@@ -156,6 +156,52 @@ ER_API int er_moe_block_noalloc(const er_moe_weights* w, const er_moe_io* io, vo
 ER_API int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* ---- the block in parts, for expert parallelism ---------------------------
+ * One rank holds experts [lo, hi) of every layer; tokens stay on their rank.
+ * The reference runs on one process (runtime/qwen_moe.py:340-359); these
+ * split its routed sum and shared expert so that routed rows can travel to
+ * the rank holding their expert (one collective each way) and back. */
+typedef struct er_moe_rows_io {
+  const void* x;               /* [m, H] rows, dtype x_dtype */
+  int x_dtype;
+  int m;
+  const int32_t* expert;       /* [m] expert of each row: 0 .. num_experts-1 of `w` (this rank's experts) */
+  const float* weight;         /* [m] routing weight of each row */
+  float* y;                    /* [m, H] = weight * down(silu(gate x) * up x) (qwen_moe.py:345-349) */
+  int path;                    /* ER_PATH_* */
+  int* launch_count;           /* optional */
+} er_moe_rows_io;
+/* routed experts on pre-routed rows (w->router_w and the shared weights unused) */
+ER_API size_t er_moe_rows_workspace_bytes(const er_moe_weights* w, int m, int path);
+ER_API int er_moe_rows(const er_moe_weights* w, const er_moe_rows_io* io, void* workspace, size_t workspace_bytes,
+                       void* stream);
+/* y [n, H] = sigmoid(h . w_g) * shared(h) (qwen_moe.py:353-359; w->router_w and
+ * the routed records unused) */
+ER_API size_t er_moe_shared_workspace_bytes(const er_moe_weights* w, int n, int path);
+ER_API int er_moe_shared(const er_moe_weights* w, const void* h, int h_dtype, int n, float* y, int path,
+                         void* workspace, size_t workspace_bytes, void* stream);
+/* y[t] = sum over t's k slots in ascending expert id (idx [n, k]) of
+ * y_rows[pos_of[t * k + j]] (+ y_shared[t] when not NULL): the reference's
+ * np.add.at order (qwen_moe.py:340-349) and its final sum (:359) */
+ER_API int er_moe_combine(const float* y_rows, const int32_t* pos_of, const int32_t* idx, const float* y_shared,
+                          int n, int k, int hidden, float* y, void* stream);
+
+/* ---- expert-parallel exchange buffers -------------------------------------
+ * owner[e] = rank holding global expert e, local[e] = its index there. */
+/* counts[r] = (token, slot) pairs of idx [n, k] whose expert lives on rank r */
+ER_API int er_ep_count(const int32_t* idx, int n, int k, const int32_t* owner, int num_experts, int ranks,
+                       int32_t* counts, void* stream);
+/* Packs the send buffers, destination rank by destination rank: rank r's
+ * rows occupy [offsets[r], offsets[r] + counts[r]) (offsets: device, the
+ * exclusive prefix of er_ep_count's counts). For pair (t, j) at position p:
+ * x_send[p] = h[t] (dtype h_dtype), expert_send[p] = local[idx[t, j]],
+ * weight_send[p] = w[t, j], pos_of[t * k + j] = p. cursor: device scratch of
+ * `ranks` ints. Rows of one destination are in no particular order. */
+ER_API int er_ep_pack(const void* h, int h_dtype, int hidden, const int32_t* idx, const float* w, int n, int k,
+                      const int32_t* owner, const int32_t* local, int num_experts, int ranks, const int32_t* offsets,
+                      int32_t* cursor, void* x_send, int32_t* expert_send, float* weight_send, int32_t* pos_of,
+                      void* stream);
+
 /* ------------------------------------------------------------------------
  * HBM expert cache: replaces CachedExpertSource (cache/expert_cache.py:92-402).
  *

@@ -1,0 +1,75 @@
+"""GPU: expert parallelism through the library (EpCudaOps) over NCCL.
+
+Each rank's output must equal, bit for bit, the single-GPU block on the same
+tokens routed from the same logits: every routed row is computed from that
+row alone and the combine adds in the block's order. One rank runs without
+collectives; two ranks need two GPUs (skipped otherwise).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from expertrelay_b200 import _lib, synth
+from expertrelay_b200.ep import EpCudaOps, ExpertParallelMoe
+from expertrelay_b200.moe import MoeBlock
+
+pytestmark = pytest.mark.gpu
+
+PATHS = {"auto": _lib.PATH_AUTO, "gemv": _lib.PATH_GEMV, "gemm": _lib.PATH_GEMM, "tc": _lib.PATH_TC}
+
+
+def _expected(block, h, path, device):
+    mb = MoeBlock.from_host_block(block, device=device)
+    return mb.forward(h, logits=mb.router_logits(h), path=path)
+
+
+@pytest.mark.parametrize("path", list(PATHS))
+def test_one_rank_equals_the_block(cuda, path):
+    block = synth.make_block(4, num_experts=16)
+    ep = ExpertParallelMoe(EpCudaOps(block, 0, 1, cuda, PATHS[path]))
+    for n in (3, 40, 300):
+        h = torch.from_numpy(synth.make_tokens(60 + n, n)).to(cuda)
+        y = ep(h)
+        ref = _expected(block, h, PATHS[path], cuda)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref), f"n={n}"
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    try:
+        block = synth.make_block(4)  # Qwen shapes: 60 experts, 30 per rank
+        for path in (_lib.PATH_TC, _lib.PATH_GEMV):
+            ep = ExpertParallelMoe(EpCudaOps(block, rank, world, dev, path))
+            for n in (8, 96 + 32 * rank):  # ragged across ranks
+                h = torch.from_numpy(synth.make_tokens(70 + 10 * rank + n, n)).to(dev)
+                y = ep(h)
+                ref = _expected(block, h, path, dev)
+                torch.cuda.synchronize()
+                if not torch.equal(y, ref):
+                    raise AssertionError(f"rank {rank} path {path} n={n}: max diff {(y - ref).abs().max().item()}")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_over_nccl_equal_the_block():
+    mp.start_processes(_rank_main, args=(2, _free_port()), nprocs=2, start_method="spawn")
