@@ -43,7 +43,7 @@ FLUSH_BYTES = 256 << 20
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="prefill4096_int8_zipf")
@@ -88,7 +88,7 @@ def traffic_from_profiles(workload: str, stage: str) -> float | None:
 
 class ClockSampler:
     """SM clock, power and clock-event reasons sampled through NVML every
-    20 ms while the timed region runs (the data nvidia-smi's clocks query
+    5 ms while the timed region runs (the data nvidia-smi's clocks query
     reports), for the GPU behind `device`."""
 
     REASONS = {
@@ -139,7 +139,7 @@ class ClockSampler:
                 except Exception as e:
                     self.error = f"{type(e).__name__}: {e}"
                     return
-                self._stop.wait(0.02)
+                self._stop.wait(0.005)
 
         self._thread = threading.Thread(target=run, daemon=True)
         self._thread.start()
@@ -164,7 +164,7 @@ class ClockSampler:
             "power_w_max": max(p for _, p, _ in self.samples),
             "reasons": reasons,
             "samples": len(self.samples),
-            "source": "NVML, 20 ms period, during the timed steps",
+            "source": "NVML, 5 ms period, during the timed steps",
         }
 
 
@@ -537,7 +537,8 @@ def decode_side(args, dev, mb, block, peaks, peak_src) -> dict:
             "block_weight_GBps": acct["block_weight_bytes"] / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "gate_up", "achieved": gu_gbs, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": gu_gbs / peaks["hbm_gbs"], "peak_source": f"of {peak_src}",
-                         "algorithmic_bytes_per_launch": acct["gate_up_bytes"]},
+                         "algorithmic_bytes_per_launch": acct["gate_up_bytes"],
+                         "traffic": traffic_from_profiles("decode8_int8", "gate_up") if name == "tc" else None},
             "stages_ms": stage,
         }
     if base_router is not None:
