@@ -8,7 +8,7 @@
 // applied to the accumulated output; int4 weights are dequantized exactly to
 // fp32 before the product.
 //
-// Work item = one BM x BN output tile of one group (see plan_kernel).
+// Work item = one BM x BN output tile of one group (see the plan in er_plan.cu).
 // mode 0: A = h rows gathered through the expert-sorted token list,
 //         B = gate and up rows; epilogue act = silu(g * s_g) * (u * s_u).
 // mode 1: A = act rows, B = down rows; epilogue y = acc * s_d * routing weight.

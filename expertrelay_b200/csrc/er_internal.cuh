@@ -18,9 +18,10 @@ struct SchedSpec {
 
 constexpr int kNumSched = 2;
 
-// Routing plan in the workspace. The router kernel clears `tally`, the top-k
-// kernel counts into it, plan_kernel turns it into groups and schedules, and
-// dispatch_kernel claims expert-sorted positions through `cursor`.
+// Routing plan in the workspace. `tally` and `cursor` are cleared (kPlanClear
+// ints from `tally`) before the top-k kernel counts into `tally`; the dispatch
+// kernel turns the counts into groups and schedules and claims expert-sorted
+// positions through `cursor`.
 struct Plan {
   int n, E, k, nk;
   int error;                           // nonzero: an expert id was out of range
@@ -31,8 +32,9 @@ struct Plan {
   int item_start[kNumSched][kMaxExperts + 2];  // prefix of items over active groups
   SchedSpec sched[kNumSched];
   int tally[kMaxExperts];              // (token, slot) pairs routed to each expert
-  int cursor[kMaxExperts];             // next free expert-sorted position of each expert
+  int cursor[kMaxExperts];             // positions of each expert's range claimed so far
 };
+constexpr int kPlanClear = 2 * kMaxExperts;  // tally and cursor, contiguous
 
 // Everything a grouped expert kernel needs to find a group's tokens and weights.
 struct GroupArgs {
@@ -114,17 +116,15 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
 int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
                        int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
                        int* tally, cudaStream_t st);
-// groups, offsets and work-item schedules from plan->tally (one warp); the
-// shared expert (all n tokens) is the last group when `shared` is nonzero
-int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, int shared, Plan* plan,
-                cudaStream_t st);
-// Scatter of the (token, slot) pairs to expert-sorted positions (perm_token,
-// perm_w, pos_of). With s0 non-null also slices each token's h row once and
-// writes the slices to its k routed positions and, when `shared` is nonzero,
-// to shared row nk + t.
-int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H,
-                    int shared, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0,
-                    int8_t* s1, float* scale, cudaStream_t st);
+// The plan (groups, ranges, work-item schedules; the shared expert, all n
+// tokens, is the last group when `shared` is nonzero) from plan->tally, and
+// the scatter of the (token, slot) pairs to expert-sorted positions
+// (perm_token, perm_w, pos_of). With s0 non-null also slices each token's h
+// row once and writes the slices to its k routed positions and, when
+// `shared` is nonzero, to shared row nk + t.
+int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
+                    int Is, const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
+                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, cudaStream_t st);
 // Upper bound of the items a schedule can produce (host side, for grid sizing).
 long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int I, int Is);
 
@@ -137,8 +137,9 @@ int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void
 // (+ y_s[t] when y_s is not NULL); rows of NaN when *error is nonzero
 int launch_combine(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k, int H,
                    const int* error, float* out, cudaStream_t st);
-// per-expert counts of ids[0..m) into tally[E] (cleared first); out-of-range ids are not counted
-int launch_tally(const int32_t* ids, int m, int E, int* tally, cudaStream_t st);
+// per-expert counts of ids[0..m) into tally[E] (nclear ints from tally cleared
+// first); out-of-range ids are not counted
+int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaStream_t st);
 // gate_sig[t] = sigmoid(sum of the nparts partial shared-gate logits of token t)
 int launch_gate_sigmoid(const float* gate_logit, int nparts, int n, float* gate_sig, cudaStream_t st);
 

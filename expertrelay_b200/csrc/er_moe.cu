@@ -186,13 +186,13 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     float* logits_sum = r.logits_out;
     if (r.logits_in) {
       if (int rc = launch_router_logits(r.h, r.h_dtype, n, H, nullptr, w->shared_gate_w, 0, nullptr, gate_logit,
-                                        &gparts, plan->tally, E, st))
+                                        &gparts, plan->tally, kPlanClear, st))
         return rc;
       lg = r.logits_in;  // one whole set of logits
       if (logits_sum == r.logits_in) logits_sum = nullptr;
     } else {
       if (int rc = launch_router_logits(r.h, r.h_dtype, n, H, w->router_w, w->shared_gate_w, E, logits, gate_logit,
-                                        &nparts, plan->tally, E, st))
+                                        &nparts, plan->tally, kPlanClear, st))
         return rc;
       gparts = nparts;
     }
@@ -213,10 +213,11 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
                                       &gparts, nullptr, 0, st))
       return rc;
     if (int rc = launch_gate_sigmoid(gate_logit, gparts, n, gate_sig, st)) return rc;
-    if (int rc = cuda_check(cudaMemsetAsync(plan->tally, 0, (size_t)E * sizeof(int), st), "clear tally")) return rc;
+    if (int rc = cuda_check(cudaMemsetAsync(plan->tally, 0, (size_t)kPlanClear * sizeof(int), st), "clear tally"))
+      return rc;
     launches += 2;
   } else {
-    if (int rc = launch_tally(r.row_expert, n, E, plan->tally, st)) return rc;
+    if (int rc = launch_tally(r.row_expert, n, E, plan->tally, kPlanClear, st)) return rc;
     launches += 1;
     idx32 = r.row_expert;
     topw = r.row_weight;
@@ -235,14 +236,13 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
   }
   if (int rc = mark(1)) return rc;
-  if (int rc = launch_plan(n, k, E, H, w->inter, w->shared_inter, specs, shared, plan, st)) return rc;
   int8_t* xs0 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs0) : nullptr;
   int8_t* xs1 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs1) : nullptr;
   float* xscale = path == ER_PATH_TC ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
-  if (int rc = launch_dispatch(r.h, r.h_dtype, idx32, topw, n, k, E, H, shared, plan, perm_token, perm_w, pos_of,
-                               xs0, xs1, xscale, st))
+  if (int rc = launch_dispatch(r.h, r.h_dtype, idx32, topw, n, k, E, H, w->inter, w->shared_inter, specs, shared,
+                               plan, perm_token, perm_w, pos_of, xs0, xs1, xscale, st))
     return rc;
-  launches += 2;
+  launches += 1;
   if (int rc = mark(2)) return rc;
 
   GroupArgs ga;

@@ -5,13 +5,14 @@
 // np.nonzero(selected == e): the (token, slot) pairs routed to it. Here the
 // pairs of each expert occupy one contiguous range of an expert-sorted array
 // (expert 0's range first), laid out in two launches:
-//   plan_kernel     per-expert counts (tallied by the top-k kernel) ->
-//                   ranges, the active groups, the work-item schedules;
-//   dispatch_kernel one warp per token claims a position in each of its k
-//                   experts' ranges (an atomic cursor per expert) and, for the
-//                   tensor-core path, slices the token's h row once into the
-//                   int8 operand rows of those positions and of the shared
-//                   expert's row nk + t.
+//   per-expert counts, tallied by the top-k kernel (or tally_kernel) ->
+//   dispatch_kernel: each CTA derives the experts' ranges from the counts
+//                   (CTA 0 also writes the active groups and the work-item
+//                   schedules); one warp per token claims a position in each
+//                   of its k experts' ranges (an atomic count per expert) and,
+//                   for the tensor-core path, slices the token's h row once
+//                   into the int8 operand rows of those positions and of the
+//                   shared expert's row nk + t.
 // The order of the pairs inside one expert's range follows the atomics, not
 // the token order; nothing downstream depends on it: every output element is
 // computed from its own token's row alone, and the combine sums each token's
@@ -20,14 +21,16 @@
 
 namespace er {
 
-// One warp. Lane l owns entries 9l .. 9l+8 of the per-expert lists (enough
-// for E + 2 <= 258) and the scans run over the lanes.
-__global__ void __launch_bounds__(32) plan_kernel(int n, int k, int E, int H, int I, int Is, SchedSpec s0,
-                                                  SchedSpec s1, int shared, Plan* __restrict__ plan) {
-  __shared__ int hist[kMaxExperts];
-  __shared__ int act[kMaxExperts + 1];
+// The plan from the per-expert tallies, by one warp: lane l owns entries
+// 9l .. 9l+8 of the per-expert lists (enough for E + 2 <= 258) and the scans
+// run over the lanes. Every caller gets the expert ranges' first positions in
+// `offs` (shared memory) and whether the tallies are consistent; with
+// write_plan it also writes the plan's groups, ranges and work-item schedules
+// for the expert kernels.
+__device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, int I, int Is, SchedSpec s0,
+                          SchedSpec s1, int shared, bool write_plan, int* hist, int* offs, int* act, int* bad_out) {
   constexpr int kPer = 9;
-  const int lane = threadIdx.x;
+  const int lane = threadIdx.x & 31;
   const int nk = n * k;
   auto warp_excl_scan = [&](int v) {  // exclusive prefix of v over the lanes
     int incl = v;
@@ -56,15 +59,22 @@ __global__ void __launch_bounds__(32) plan_kernel(int n, int k, int E, int H, in
   for (int j = 0; j < kPer; ++j) {
     const int e = lane * kPer + j;
     if (e < E) {
-      plan->counts[e] = hist[e];
-      plan->offsets[e] = off;
-      plan->cursor[e] = off;  // dispatch_kernel claims positions from here
+      offs[e] = off;
+      if (write_plan) {
+        plan->counts[e] = hist[e];
+        plan->offsets[e] = off;
+      }
       off += hist[e];
       if (hist[e] > 0) act[pos++] = e;
     }
   }
   // every pair lands in some expert's range: the counts must add up to n * k
   const bool bad = total != nk;
+  if (lane == 0) *bad_out = bad;
+  if (!write_plan) {
+    __syncwarp();
+    return;
+  }
   const int na = na_routed + (shared && n > 0 ? 1 : 0);
   if (lane == 0) {
     if (shared && n > 0) act[na_routed] = E;
@@ -109,33 +119,43 @@ __global__ void __launch_bounds__(32) plan_kernel(int n, int k, int E, int H, in
     plan->sched[1] = s1;
     plan->num_active = bad ? 0 : na;  // no work items on an inconsistent tally
   }
+  __syncwarp();
 }
 
-// One warp per token t. Lane r < k claims the position of slot r; with
-// SLICE, the warp then slices h[t] (K = H values) and writes the slices to
-// the k claimed rows and to row nk + t. Rows of up to 2048 values stay in
-// registers; longer rows are read twice.
+// Eight tokens per CTA, one warp each. Warp 0 first derives the expert
+// ranges from the tallies (CTA 0 also writes the plan). Then lane r < k of a
+// token's warp claims the position of slot r (its expert's range start plus
+// an atomic count, from 0); with SLICE the warp slices h[t] (K = H values)
+// and writes the slices to the k claimed rows and, for the shared expert, to
+// row nk + t. Rows of up to 2048 values stay in registers; longer rows are
+// read twice.
 template <typename XT, bool SLICE>
 __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
-                                                       const float* __restrict__ w, int n, int k, int E, int H,
-                                                       int shared, Plan* __restrict__ plan,
-                                                       int32_t* __restrict__ perm_token,
+                                                       const float* __restrict__ w, int n, int k, int E, int H, int I,
+                                                       int Is, SchedSpec spec0, SchedSpec spec1, int shared,
+                                                       Plan* __restrict__ plan, int32_t* __restrict__ perm_token,
                                                        float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
                                                        int8_t* __restrict__ s0, int8_t* __restrict__ s1,
                                                        float* __restrict__ scale) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= n) return;
+  __shared__ int hist[kMaxExperts];
+  __shared__ int offs[kMaxExperts];
+  __shared__ int act[kMaxExperts + 1];
+  __shared__ int bad;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp == 0) plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad);
+  __syncthreads();
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= n || bad) return;  // nothing downstream reads positions of an inconsistent tally
   const int nk = n * k;
   int p = -1;
   if (lane < k) {
     const int e = idx[(size_t)t * k + lane];
     if (e >= 0 && e < E) {
-      p = atomicAdd(&plan->cursor[e], 1);
-      if (p < 0 || p >= nk) {  // only an inconsistent tally gets here
+      const int c = atomicAdd(&plan->cursor[e], 1);
+      if (c >= hist[e]) {  // only an inconsistent tally gets here
         atomicOr(&plan->error, 2);
-        p = -1;
       } else {
+        p = offs[e] + c;
         perm_token[p] = t;
         perm_w[p] = w[(size_t)t * k + lane];
       }
@@ -208,12 +228,6 @@ long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int 
   return routed_rows_tiles * nt_r + shared_tiles * nt_s;
 }
 
-int launch_plan(int n, int k, int E, int H, int I, int Is, const SchedSpec* specs, int shared, Plan* plan,
-                cudaStream_t st) {
-  plan_kernel<<<1, 32, 0, st>>>(n, k, E, H, I, Is, specs[0], specs[1], shared, plan);
-  return launch_check("plan_kernel");
-}
-
 __global__ void __launch_bounds__(256) tally_kernel(const int32_t* __restrict__ ids, int m, int E,
                                                     int* __restrict__ tally) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -222,28 +236,29 @@ __global__ void __launch_bounds__(256) tally_kernel(const int32_t* __restrict__ 
   if (e >= 0 && e < E) atomicAdd(&tally[e], 1);
 }
 
-int launch_tally(const int32_t* ids, int m, int E, int* tally, cudaStream_t st) {
-  if (int rc = cuda_check(cudaMemsetAsync(tally, 0, (size_t)E * sizeof(int), st), "clear tally")) return rc;
+int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaStream_t st) {
+  if (int rc = cuda_check(cudaMemsetAsync(tally, 0, (size_t)nclear * sizeof(int), st), "clear tally")) return rc;
   if (m <= 0) return ER_OK;
   tally_kernel<<<(m + 255) / 256, 256, 0, st>>>(ids, m, E, tally);
   return launch_check("tally_kernel");
 }
 
-int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H,
-                    int shared, Plan* plan, int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0,
-                    int8_t* s1, float* scale, cudaStream_t st) {
-  if (n <= 0) return ER_OK;
-  const int blocks = (n + 7) / 8;
+int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
+                    int Is, const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
+                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, cudaStream_t st) {
+  const int blocks = n > 0 ? (n + 7) / 8 : 1;  // CTA 0 writes the plan even for no tokens
   if (!s0)
-    dispatch_kernel<float, false><<<blocks, 256, 0, st>>>(nullptr, idx, w, n, k, E, H, shared, plan, perm_token,
-                                                          perm_w, pos_of, nullptr, nullptr, nullptr);
+    dispatch_kernel<float, false><<<blocks, 256, 0, st>>>(nullptr, idx, w, n, k, E, H, I, Is, specs[0], specs[1],
+                                                          shared, plan, perm_token, perm_w, pos_of, nullptr, nullptr,
+                                                          nullptr);
   else if (h_dtype == ER_DTYPE_BF16)
-    dispatch_kernel<__nv_bfloat16, true><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)h, idx, w, n, k, E, H,
-                                                                 shared, plan, perm_token, perm_w, pos_of, s0, s1,
-                                                                 scale);
+    dispatch_kernel<__nv_bfloat16, true><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)h, idx, w, n, k, E, H, I, Is,
+                                                                 specs[0], specs[1], shared, plan, perm_token, perm_w,
+                                                                 pos_of, s0, s1, scale);
   else
-    dispatch_kernel<float, true><<<blocks, 256, 0, st>>>((const float*)h, idx, w, n, k, E, H, shared, plan,
-                                                         perm_token, perm_w, pos_of, s0, s1, scale);
+    dispatch_kernel<float, true><<<blocks, 256, 0, st>>>((const float*)h, idx, w, n, k, E, H, I, Is, specs[0],
+                                                         specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1,
+                                                         scale);
   return launch_check("dispatch_kernel");
 }
 

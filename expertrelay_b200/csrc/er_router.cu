@@ -178,40 +178,22 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__
   }
 }
 
-// One warp per token: softmax over the E logits (max subtracted, expf, sum,
-// divide) and top-k by logit value, largest first, exact ties to the lower
-// expert id. Ranking by the logits equals ranking by the probabilities
-// because every step of the softmax is monotone; NaN logits rank as -inf.
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int nparts, int gparts,
-                                                          int n, int E,
-                                                          int k, int norm, int64_t* __restrict__ idx64,
-                                                          int32_t* __restrict__ idx32,
-                                                          float* __restrict__ wout,
-                                                          const float* __restrict__ gate_logit,
-                                                          float* __restrict__ gate_sig,
-                                                          float* __restrict__ logits_sum, int* __restrict__ tally) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= n) return;
-  const float* l = logits + (size_t)t * E;
-  constexpr int kPer = kMaxExperts / 32;
-  float v[kPer], ex[kPer];
+// Softmax over the E logits of one token held by a warp (lane l holds
+// experts l + 32 j in v[j]; max subtracted, expf, sum, divide) and top-k by
+// logit value, largest first, exact ties to the lower expert id. Ranking by
+// the logits equals ranking by the probabilities because every step of the
+// softmax is monotone; NaN logits rank as -inf. Writes token t's ids and
+// weights; tally (optional) counts the selected experts.
+template <int kPer>
+__device__ __forceinline__ void warp_select(const float (&v)[kPer], int E, int k, int norm, int t, int lane,
+                                            int64_t* __restrict__ idx64, int32_t* __restrict__ idx32,
+                                            float* __restrict__ wout, int* __restrict__ tally) {
   float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = lane + 32 * j;
-    v[j] = -INFINITY;
-    if (e < E) {  // partial logits of K slices, added in slice order
-      float a = l[e];
-      for (int p = 1; p < nparts; ++p) a += l[(size_t)p * n * E + e];
-      v[j] = a;
-      if (logits_sum) logits_sum[(size_t)t * E + e] = a;
-    }
-    mx = fmaxf(mx, v[j]);
-  }
+  for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, v[j]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float s = 0.f;
+  float ex[kPer], s = 0.f;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int e = lane + 32 * j;
@@ -273,11 +255,40 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       if (idx32) idx32[(size_t)t * k + r] = sel[r];
       if (wout) wout[(size_t)t * k + r] = w;
     }
-    if (gate_sig && gate_logit) {
-      float gl = gate_logit[t];
-      for (int p = 1; p < gparts; ++p) gl += gate_logit[(size_t)p * n + t];
-      gate_sig[t] = sigmoid_f(gl);
+  }
+}
+
+// One warp per token over logits summed from `nparts` K-slice partials.
+template <int kPer>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int nparts, int gparts,
+                                                          int n, int E,
+                                                          int k, int norm, int64_t* __restrict__ idx64,
+                                                          int32_t* __restrict__ idx32,
+                                                          float* __restrict__ wout,
+                                                          const float* __restrict__ gate_logit,
+                                                          float* __restrict__ gate_sig,
+                                                          float* __restrict__ logits_sum, int* __restrict__ tally) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const float* l = logits + (size_t)t * E;
+  float v[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = -INFINITY;
+    if (e < E) {  // partial logits of K slices, added in slice order
+      float a = l[e];
+      for (int p = 1; p < nparts; ++p) a += l[(size_t)p * n * E + e];
+      v[j] = a;
+      if (logits_sum) logits_sum[(size_t)t * E + e] = a;
     }
+  }
+  warp_select<kPer>(v, E, k, norm, t, lane, idx64, idx32, wout, tally);
+  if (lane == 0 && gate_sig && gate_logit) {
+    float gl = gate_logit[t];
+    for (int p = 1; p < gparts; ++p) gl += gate_logit[(size_t)p * n + t];
+    gate_sig[t] = sigmoid_f(gl);
   }
 }
 
@@ -327,11 +338,16 @@ int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E
   if (n <= 0) return ER_OK;
   const int warps_per_block = 8;
   const int blocks = (n + warps_per_block - 1) / warps_per_block;
-  router_topk_kernel<<<blocks, warps_per_block * 32, 0, st>>>(logits, nparts, gparts, n, E, k, norm, idx64, idx32,
-                                                               wout,
-                                                               gate_logit, gate_sig, logits_sum, tally);
+  if (E <= 64)
+    router_topk_kernel<2><<<blocks, warps_per_block * 32, 0, st>>>(logits, nparts, gparts, n, E, k, norm, idx64,
+                                                                    idx32, wout, gate_logit, gate_sig, logits_sum,
+                                                                    tally);
+  else
+    router_topk_kernel<kMaxExperts / 32><<<blocks, warps_per_block * 32, 0, st>>>(
+        logits, nparts, gparts, n, E, k, norm, idx64, idx32, wout, gate_logit, gate_sig, logits_sum, tally);
   return launch_check("router_topk_kernel");
 }
+
 
 }  // namespace er
 

@@ -899,9 +899,58 @@ static int launch_tc_mode(const TcMaps& maps, const TcArgs& t, long long items_b
   return launch_check("tc_expert_gemm_kernel");
 }
 
+// Rows longer than a warp holds (K > 2048): one CTA of 256 threads per row,
+// each thread holding kVec float4 of it, so the row is read once; the CTA
+// reduces the row maximum through shared memory.
+template <typename XT, int kVec>
+__global__ void __launch_bounds__(256) slice_long_rows_kernel(const XT* __restrict__ src, int K,
+                                                              int8_t* __restrict__ s0, int8_t* __restrict__ s1,
+                                                              float* __restrict__ scale) {
+  __shared__ float red[8];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const XT* x = src + (size_t)row * K;
+  float4 v[kVec];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int k = (tid + 256 * i) * 4;
+    v[i] = k < K ? load4(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    amax = fmaxf(amax, abs_max4(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (lane == 0) red[warp] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
+  const float inv = amax > 0.f ? 127.f / amax : 0.f;
+  int8_t* d0 = s0 + (size_t)row * K;
+  int8_t* d1 = s1 + (size_t)row * K;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int k = (tid + 256 * i) * 4;
+    if (k < K) {
+      uint32_t w0, w1;
+      slice4(v[i], inv, w0, w1);
+      *reinterpret_cast<uint32_t*>(d0 + k) = w0;
+      *reinterpret_cast<uint32_t*>(d1 + k) = w1;
+    }
+  }
+  if (tid == 0) scale[row] = amax / 127.f;
+}
+
 int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, int8_t* s1, float* scale,
                       cudaStream_t st) {
   if (rows <= 0) return ER_OK;
+  if (K > 2048 && K <= 8192) {  // 256 threads x 8 float4 cover 8192 values
+    if (dtype == ER_DTYPE_BF16)
+      slice_long_rows_kernel<__nv_bfloat16, 8><<<rows, 256, 0, st>>>((const __nv_bfloat16*)src, K, s0, s1, scale);
+    else
+      slice_long_rows_kernel<float, 8><<<rows, 256, 0, st>>>((const float*)src, K, s0, s1, scale);
+    return launch_check("slice_long_rows_kernel");
+  }
   const int blocks = (rows + 7) / 8;
   if (dtype == ER_DTYPE_BF16)
     slice_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)src, rows, K, s0, s1, scale);
