@@ -347,12 +347,17 @@ def main() -> None:
         mb.forward(h_dev, path=path)
     torch.cuda.synchronize()
 
-    # the forward captured once as a CUDA graph (no host work per step), with
-    # the stage events inside it so the dominant kernel is timed on replay
-    cap = mb.capture(n, dtype=act_dtype, path=path, stage_events=stage_ev)
+    # the forward captured once as a CUDA graph (no host work per step); a
+    # second capture carries CUDA events between the stages, for the live
+    # per-stage times (event nodes between kernels would break the kernels'
+    # chained launches, so the step time comes from the first)
+    cap = mb.capture(n, dtype=act_dtype, path=path)
+    cap_st = mb.capture(n, dtype=act_dtype, path=path, stage_events=stage_ev)
     cap.h.copy_(h_dev)
+    cap_st.h.copy_(h_dev)
     for _ in range(max(args.warmup, 3)):
         cap.replay()
+        cap_st.replay()
     torch.cuda.synchronize()
 
     # timed region: K steps, each after an L2 flush, bracketed by barrier + sync
@@ -372,12 +377,17 @@ def main() -> None:
             cap.replay()
             ends[i].record()
             launches.value += launches_per_forward.value
-            stage_ev[-1].synchronize()
-            for j, s in enumerate(_lib.MOE_STAGES):
-                stage_ms[s] += stage_ev[j].elapsed_time(stage_ev[j + 1])
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
+    # the stage pass: the same steps through the capture with stage events
+    for i in range(args.steps):
+        flush.zero_()
+        cap_st.replay()
+        stage_ev[-1].synchronize()
+        for j, s in enumerate(_lib.MOE_STAGES):
+            stage_ms[s] += stage_ev[j].elapsed_time(stage_ev[j + 1])
+    torch.cuda.synchronize()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
@@ -513,19 +523,30 @@ def decode_side(args, dev, mb, block, peaks, peak_src) -> dict:
         e.record()
     steps = max(args.steps, 20)
     results = {}
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for name, path in (("gemv", _lib.PATH_GEMV), ("tc", _lib.PATH_TC)):
-        cap = mb.capture(8, path=path, stage_events=ev)
+        # block time from a capture without events between the stages; stage
+        # times from a second capture with them
+        cap = mb.capture(8, path=path)
+        cap_st = mb.capture(8, path=path, stage_events=ev)
         cap.h.copy_(h)
+        cap_st.h.copy_(h)
         for _ in range(5):
             cap.replay()
+            cap_st.replay()
         torch.cuda.synchronize()
         tot = 0.0
         stage = {s: 0.0 for s in _lib.MOE_STAGES}
         for _ in range(steps):
             flush.zero_()
+            t0.record()
             cap.replay()
+            t1.record()
+            t1.synchronize()
+            tot += t0.elapsed_time(t1)
+            flush.zero_()
+            cap_st.replay()
             ev[-1].synchronize()
-            tot += ev[0].elapsed_time(ev[-1])
             for j, s in enumerate(_lib.MOE_STAGES):
                 stage[s] += ev[j].elapsed_time(ev[j + 1])
         ms = tot / steps

@@ -1,6 +1,8 @@
 // er_common.cuh -- shared helpers for libexpertrelay_b200 (sm_100a).
 #pragma once
 
+#include <utility>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -14,6 +16,32 @@ namespace er {
 int fail(int code, const char* fmt, ...);                 // records the message, returns code
 int cuda_check(cudaError_t e, const char* what);          // ER_OK or ER_ECUDA with the CUDA message
 inline int launch_check(const char* what) { return cuda_check(cudaGetLastError(), what); }
+
+// The block's kernels run as one chain on a stream. Each is launched with
+// programmatic stream serialization, so its launch (and any prologue that
+// touches only its own shared memory, TMEM and registers) overlaps the tail
+// of the kernel before it; chain_wait() returns once that kernel has
+// completed and its writes are visible. Every chained kernel calls
+// chain_wait() before it reads or writes global memory another kernel of
+// the stream uses. In a kernel launched without the attribute it returns at
+// once.
+__device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline int launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
 
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;

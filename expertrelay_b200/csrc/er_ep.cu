@@ -14,6 +14,7 @@ namespace er {
 __global__ void __launch_bounds__(256) ep_count_kernel(const int32_t* __restrict__ idx, int nk,
                                                        const int32_t* __restrict__ owner, int E, int ranks,
                                                        int32_t* __restrict__ counts) {
+  chain_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nk) return;
   const int e = idx[i];
@@ -33,6 +34,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const XT* __restrict__ h, 
                                                       int32_t* __restrict__ cursor, XT* __restrict__ x_send,
                                                       int32_t* __restrict__ expert_send,
                                                       float* __restrict__ weight_send, int32_t* __restrict__ pos_of) {
+  chain_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= n) return;
@@ -71,8 +73,8 @@ extern "C" int er_ep_count(const int32_t* idx, int n, int k, const int32_t* owne
     return rc;
   const int nk = n * k;
   if (nk == 0) return ER_OK;
-  ep_count_kernel<<<(nk + 255) / 256, 256, 0, st>>>(idx, nk, owner, num_experts, ranks, counts);
-  return launch_check("ep_count_kernel");
+  return launch_chained(ep_count_kernel, dim3((nk + 255) / 256), dim3(256), 0, st, "ep_count_kernel", idx, nk, owner,
+                        num_experts, ranks, counts);
 }
 
 extern "C" int er_ep_pack(const void* h, int h_dtype, int hidden, const int32_t* idx, const float* w, int n, int k,
@@ -94,12 +96,10 @@ extern "C" int er_ep_pack(const void* h, int h_dtype, int hidden, const int32_t*
     return rc;
   const int blocks = (n + 7) / 8;
   if (h_dtype == ER_DTYPE_BF16)
-    ep_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-        (const __nv_bfloat16*)h, hidden, idx, w, n, k, owner, local, num_experts, ranks, offsets, cursor,
-        (__nv_bfloat16*)x_send, expert_send, weight_send, pos_of);
-  else
-    ep_pack_kernel<float><<<blocks, 256, 0, st>>>((const float*)h, hidden, idx, w, n, k, owner, local, num_experts,
-                                                  ranks, offsets, cursor, (float*)x_send, expert_send, weight_send,
-                                                  pos_of);
-  return launch_check("ep_pack_kernel");
+    return launch_chained(ep_pack_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, "ep_pack_kernel",
+                          (const __nv_bfloat16*)h, hidden, idx, w, n, k, owner, local, num_experts, ranks, offsets,
+                          cursor, (__nv_bfloat16*)x_send, expert_send, weight_send, pos_of);
+  return launch_chained(ep_pack_kernel<float>, dim3(blocks), dim3(256), 0, st, "ep_pack_kernel", (const float*)h,
+                        hidden, idx, w, n, k, owner, local, num_experts, ranks, offsets, cursor, (float*)x_send,
+                        expert_send, weight_send, pos_of);
 }

@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GroupArgs a, int sched, 
   constexpr bool kInt8 = (FMT == ER_FMT_INT8);
   __shared__ __align__(16) float As[BK][BM + 4];
   __shared__ __align__(16) float Bs[NB][BK][BN + 4];
+  chain_wait();
   const Plan* P = a.plan;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int lrow = tid >> 2, lk = (tid & 3) * 4;  // load mapping: row 0..63, k 0,4,8,12
@@ -146,16 +147,15 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GroupArgs a, int sched, 
 template <int MODE, typename XT>
 static int launch_simt_fmt(const GroupArgs& a, int sched, const XT* x, float* act_r, float* act_s,
                            float* out_r, float* out_s, int grid, cudaStream_t st) {
-  gemm_simt_kernel<ER_FMT_INT8, MODE, XT><<<grid, 256, 0, st>>>(a, sched, x, act_r, act_s, out_r, out_s);
-  if (int rc = launch_check("gemm_simt_kernel<int8>")) return rc;
-  if (a.fmt == ER_FMT_INT4) {
-    gemm_simt_kernel<ER_FMT_INT4, MODE, XT><<<grid, 256, 0, st>>>(a, sched, x, act_r, act_s, out_r, out_s);
-    return launch_check("gemm_simt_kernel<int4>");
-  }
-  if (a.fmt == ER_FMT_INT4_ZP) {
-    gemm_simt_kernel<ER_FMT_INT4_ZP, MODE, XT><<<grid, 256, 0, st>>>(a, sched, x, act_r, act_s, out_r, out_s);
-    return launch_check("gemm_simt_kernel<int4zp>");
-  }
+  if (int rc = launch_chained(gemm_simt_kernel<ER_FMT_INT8, MODE, XT>, dim3(grid), dim3(256), 0, st,
+                              "gemm_simt_kernel<int8>", a, sched, x, act_r, act_s, out_r, out_s))
+    return rc;
+  if (a.fmt == ER_FMT_INT4)
+    return launch_chained(gemm_simt_kernel<ER_FMT_INT4, MODE, XT>, dim3(grid), dim3(256), 0, st,
+                          "gemm_simt_kernel<int4>", a, sched, x, act_r, act_s, out_r, out_s);
+  if (a.fmt == ER_FMT_INT4_ZP)
+    return launch_chained(gemm_simt_kernel<ER_FMT_INT4_ZP, MODE, XT>, dim3(grid), dim3(256), 0, st,
+                          "gemm_simt_kernel<int4zp>", a, sched, x, act_r, act_s, out_r, out_s);
   return ER_OK;
 }
 
@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
                                                       const int32_t* __restrict__ pos_of,
                                                       const int32_t* __restrict__ idx, int k, int H,
                                                       const int* __restrict__ error, float* __restrict__ out) {
+  chain_wait();
   const int t = blockIdx.x;
   if (error && *error) {
     for (int c = threadIdx.x; c < H; c += blockDim.x) out[(size_t)t * H + c] = __int_as_float(0x7fc00000);
@@ -225,8 +226,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
 int launch_combine(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k, int H,
                    const int* error, float* out, cudaStream_t st) {
   if (n <= 0) return ER_OK;
-  combine_kernel<<<n, 256, 0, st>>>(y_r, y_s, pos_of, idx, k, H, error, out);
-  return launch_check("combine_kernel");
+  return launch_chained(combine_kernel, dim3(n), dim3(256), 0, st, "combine_kernel", y_r, y_s, pos_of, idx, k, H,
+                        error, out);
 }
 
 }  // namespace er

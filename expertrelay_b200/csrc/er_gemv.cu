@@ -32,6 +32,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_grouped_kernel(GroupArgs
   constexpr int MT = kGemvMaxTok;
   constexpr bool kInt8 = (FMT == ER_FMT_INT8);
   __shared__ __align__(16) float xs[MT * kGemvSlab];
+  chain_wait();
   const Plan* P = a.plan;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = P->item_start[sched][P->num_active];
@@ -210,19 +211,15 @@ static int launch_fmt(const GroupArgs& a, int sched, const XT* x, float* act_r, 
                       float* out_r, float* out_s, int grid, cudaStream_t st) {
   // the shared expert (int8) is processed by the int8 instance; routed groups by
   // the instance of their format (each instance skips groups of another format)
-  gemv_grouped_kernel<ER_FMT_INT8, MODE, XT>
-      <<<grid, kGemvWarps * 32, 0, st>>>(a, sched, x, act_r, act_s, out_r, out_s);
-  if (int rc = launch_check("gemv_grouped_kernel<int8>")) return rc;
-  if (a.fmt == ER_FMT_INT4) {
-    gemv_grouped_kernel<ER_FMT_INT4, MODE, XT>
-        <<<grid, kGemvWarps * 32, 0, st>>>(a, sched, x, act_r, act_s, out_r, out_s);
-    return launch_check("gemv_grouped_kernel<int4>");
-  }
-  if (a.fmt == ER_FMT_INT4_ZP) {
-    gemv_grouped_kernel<ER_FMT_INT4_ZP, MODE, XT>
-        <<<grid, kGemvWarps * 32, 0, st>>>(a, sched, x, act_r, act_s, out_r, out_s);
-    return launch_check("gemv_grouped_kernel<int4zp>");
-  }
+  if (int rc = launch_chained(gemv_grouped_kernel<ER_FMT_INT8, MODE, XT>, dim3(grid), dim3(kGemvWarps * 32), 0, st,
+                              "gemv_grouped_kernel<int8>", a, sched, x, act_r, act_s, out_r, out_s))
+    return rc;
+  if (a.fmt == ER_FMT_INT4)
+    return launch_chained(gemv_grouped_kernel<ER_FMT_INT4, MODE, XT>, dim3(grid), dim3(kGemvWarps * 32), 0, st,
+                          "gemv_grouped_kernel<int4>", a, sched, x, act_r, act_s, out_r, out_s);
+  if (a.fmt == ER_FMT_INT4_ZP)
+    return launch_chained(gemv_grouped_kernel<ER_FMT_INT4_ZP, MODE, XT>, dim3(grid), dim3(kGemvWarps * 32), 0, st,
+                          "gemv_grouped_kernel<int4zp>", a, sched, x, act_r, act_s, out_r, out_s);
   return ER_OK;
 }
 

@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
   __shared__ int offs[kMaxExperts];
   __shared__ int act[kMaxExperts + 1];
   __shared__ int bad;
+  chain_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp == 0) plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad);
   __syncthreads();
@@ -230,6 +231,7 @@ long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int 
 
 __global__ void __launch_bounds__(256) tally_kernel(const int32_t* __restrict__ ids, int m, int E,
                                                     int* __restrict__ tally) {
+  chain_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= m) return;
   const int e = ids[i];
@@ -239,8 +241,7 @@ __global__ void __launch_bounds__(256) tally_kernel(const int32_t* __restrict__ 
 int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaStream_t st) {
   if (int rc = cuda_check(cudaMemsetAsync(tally, 0, (size_t)nclear * sizeof(int), st), "clear tally")) return rc;
   if (m <= 0) return ER_OK;
-  tally_kernel<<<(m + 255) / 256, 256, 0, st>>>(ids, m, E, tally);
-  return launch_check("tally_kernel");
+  return launch_chained(tally_kernel, dim3((m + 255) / 256), dim3(256), 0, st, "tally_kernel", ids, m, E, tally);
 }
 
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
@@ -248,18 +249,16 @@ int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float*
                     int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, cudaStream_t st) {
   const int blocks = n > 0 ? (n + 7) / 8 : 1;  // CTA 0 writes the plan even for no tokens
   if (!s0)
-    dispatch_kernel<float, false><<<blocks, 256, 0, st>>>(nullptr, idx, w, n, k, E, H, I, Is, specs[0], specs[1],
-                                                          shared, plan, perm_token, perm_w, pos_of, nullptr, nullptr,
-                                                          nullptr);
-  else if (h_dtype == ER_DTYPE_BF16)
-    dispatch_kernel<__nv_bfloat16, true><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)h, idx, w, n, k, E, H, I, Is,
-                                                                 specs[0], specs[1], shared, plan, perm_token, perm_w,
-                                                                 pos_of, s0, s1, scale);
-  else
-    dispatch_kernel<float, true><<<blocks, 256, 0, st>>>((const float*)h, idx, w, n, k, E, H, I, Is, specs[0],
-                                                         specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1,
-                                                         scale);
-  return launch_check("dispatch_kernel");
+    return launch_chained(dispatch_kernel<float, false>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel",
+                          (const float*)nullptr, idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan,
+                          perm_token, perm_w, pos_of, (int8_t*)nullptr, (int8_t*)nullptr, (float*)nullptr);
+  if (h_dtype == ER_DTYPE_BF16)
+    return launch_chained(dispatch_kernel<__nv_bfloat16, true>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel",
+                          (const __nv_bfloat16*)h, idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan,
+                          perm_token, perm_w, pos_of, s0, s1, scale);
+  return launch_chained(dispatch_kernel<float, true>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel",
+                        (const float*)h, idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token,
+                        perm_w, pos_of, s0, s1, scale);
 }
 
 }  // namespace er

@@ -17,6 +17,7 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const XT* __restrict__
                                                           int E, float* __restrict__ logits,
                                                           float* __restrict__ gate_logit, int* __restrict__ tally,
                                                           int ntally) {
+  chain_wait();
   constexpr int kTok = kRouterTok;
   if (blockIdx.x == 0 && tally)  // cleared for the top-k kernel's per-expert counts
     for (int i = threadIdx.x; i < ntally; i += blockDim.x) tally[i] = 0;
@@ -74,6 +75,7 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__
                                                           float* __restrict__ logits,
                                                           float* __restrict__ gate_logit, int* __restrict__ tally,
                                                           int ntally) {
+  chain_wait();
   constexpr int BM = 32, BN = 64, BK = 16, KG = 4;
   if (blockIdx.x == 0 && blockIdx.y == 0 && tally)  // cleared for the top-k kernel's per-expert counts
     for (int i = threadIdx.x; i < ntally; i += blockDim.x) tally[i] = 0;
@@ -268,6 +270,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
                                                           const float* __restrict__ gate_logit,
                                                           float* __restrict__ gate_sig,
                                                           float* __restrict__ logits_sum, int* __restrict__ tally) {
+  chain_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= n) return;
@@ -294,6 +297,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 
 __global__ void __launch_bounds__(256) gate_sigmoid_kernel(const float* __restrict__ gate_logit, int nparts, int n,
                                                            float* __restrict__ gate_sig) {
+  chain_wait();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= n) return;
   float gl = gate_logit[t];
@@ -303,8 +307,8 @@ __global__ void __launch_bounds__(256) gate_sigmoid_kernel(const float* __restri
 
 int launch_gate_sigmoid(const float* gate_logit, int nparts, int n, float* gate_sig, cudaStream_t st) {
   if (n <= 0) return ER_OK;
-  gate_sigmoid_kernel<<<(n + 255) / 256, 256, 0, st>>>(gate_logit, nparts, n, gate_sig);
-  return launch_check("gate_sigmoid_kernel");
+  return launch_chained(gate_sigmoid_kernel, dim3((n + 255) / 256), dim3(256), 0, st, "gate_sigmoid_kernel",
+                        gate_logit, nparts, n, gate_sig);
 }
 
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
@@ -314,22 +318,18 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
   // E == 0: only the shared-gate row (the caller supplies router logits)
   if (n <= 64 || E + 1 > 64) {
     if (h_dtype == ER_DTYPE_BF16)
-      router_rows_kernel<__nv_bfloat16><<<E + 1, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
-                                                                gate_logit, tally, ntally);
-    else
-      router_rows_kernel<float><<<E + 1, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit, tally,
-                                                       ntally);
-    return launch_check("router_rows_kernel");
+      return launch_chained(router_rows_kernel<__nv_bfloat16>, dim3(E + 1), dim3(256), 0, st, "router_rows_kernel",
+                            (const __nv_bfloat16*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally);
+    return launch_chained(router_rows_kernel<float>, dim3(E + 1), dim3(256), 0, st, "router_rows_kernel",
+                          (const float*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally);
   }
   *nparts = kRouterKSplit;
   const dim3 grid((n + 31) / 32, kRouterKSplit);
   if (h_dtype == ER_DTYPE_BF16)
-    router_gemm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)h, n, H, wr, wg, E, logits,
-                                                             gate_logit, tally, ntally);
-  else
-    router_gemm_kernel<float><<<grid, 256, 0, st>>>((const float*)h, n, H, wr, wg, E, logits, gate_logit, tally,
-                                                    ntally);
-  return launch_check("router_gemm_kernel");
+    return launch_chained(router_gemm_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, "router_gemm_kernel",
+                          (const __nv_bfloat16*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally);
+  return launch_chained(router_gemm_kernel<float>, grid, dim3(256), 0, st, "router_gemm_kernel", (const float*)h, n, H,
+                        wr, wg, E, logits, gate_logit, tally, ntally);
 }
 
 int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
@@ -339,13 +339,12 @@ int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E
   const int warps_per_block = 8;
   const int blocks = (n + warps_per_block - 1) / warps_per_block;
   if (E <= 64)
-    router_topk_kernel<2><<<blocks, warps_per_block * 32, 0, st>>>(logits, nparts, gparts, n, E, k, norm, idx64,
-                                                                    idx32, wout, gate_logit, gate_sig, logits_sum,
-                                                                    tally);
-  else
-    router_topk_kernel<kMaxExperts / 32><<<blocks, warps_per_block * 32, 0, st>>>(
-        logits, nparts, gparts, n, E, k, norm, idx64, idx32, wout, gate_logit, gate_sig, logits_sum, tally);
-  return launch_check("router_topk_kernel");
+    return launch_chained(router_topk_kernel<2>, dim3(blocks), dim3(warps_per_block * 32), 0, st,
+                          "router_topk_kernel", logits, nparts, gparts, n, E, k, norm, idx64, idx32, wout, gate_logit,
+                          gate_sig, logits_sum, tally);
+  return launch_chained(router_topk_kernel<kMaxExperts / 32>, dim3(blocks), dim3(warps_per_block * 32), 0, st,
+                        "router_topk_kernel", logits, nparts, gparts, n, E, k, norm, idx64, idx32, wout, gate_logit,
+                        gate_sig, logits_sum, tally);
 }
 
 

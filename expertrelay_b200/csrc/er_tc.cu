@@ -282,6 +282,7 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ 
                                                          int8_t* __restrict__ s0, int8_t* __restrict__ s1,
                                                          float* __restrict__ scale) {
   constexpr int kRegVec = 16;  // float4 per lane held in registers: K <= 2048
+  chain_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -509,6 +510,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // everything above touched only this CTA's shared memory; the plan and the
+  // operands come from the kernels before this one
+  chain_wait();
   tc_cache_plan(t, pc);
   if constexpr (CG == 2) {
     // the peer's loads and arrivals target CTA 0's barriers: both CTAs'
@@ -829,19 +833,22 @@ static int make_map(CUtensorMap* m, const void* base, int rank, uint64_t k, uint
   return ER_OK;
 }
 
+// clusters of 2 CTAs; chained to the kernel before (chain_wait) when `chained`
 static void pair_launch_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, int pairs, size_t smem,
-                               cudaStream_t st) {
-  attr->id = cudaLaunchAttributeClusterDimension;
-  attr->val.clusterDim.x = 2;
-  attr->val.clusterDim.y = 1;
-  attr->val.clusterDim.z = 1;
+                               cudaStream_t st, bool chained) {
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   memset(cfg, 0, sizeof(*cfg));
   cfg->gridDim = dim3(2 * pairs);
   cfg->blockDim = dim3(kTcThreads);
   cfg->dynamicSmemBytes = smem;
   cfg->stream = st;
   cfg->attrs = attr;
-  cfg->numAttrs = 1;
+  cfg->numAttrs = chained ? 2 : 1;
 }
 
 // Per device and kernel: the shared-memory attribute, and for pair kernels how
@@ -862,8 +869,8 @@ static int configure_tc(int* resident_pairs) {
       int sms = 148;
       if (int rc = er_device_sm_count(&sms)) return rc;
       cudaLaunchConfig_t cfg;
-      cudaLaunchAttribute attr;
-      pair_launch_config(&cfg, &attr, sms / 2, Geo::kSmem, 0);
+      cudaLaunchAttribute attr[2];
+      pair_launch_config(&cfg, attr, sms / 2, Geo::kSmem, 0, false);
       if (int rc = cuda_check(cudaOccupancyMaxActiveClusters(&pairs, tc_expert_gemm_kernel<MODE, TT, CG>, &cfg),
                               "cudaOccupancyMaxActiveClusters"))
         return rc;
@@ -885,13 +892,15 @@ static int launch_tc_mode(const TcMaps& maps, const TcArgs& t, long long items_b
     int sms = 148;
     if (int rc = er_device_sm_count(&sms)) return rc;
     const int grid = (int)(items < sms ? items : sms);
-    tc_expert_gemm_kernel<MODE, TT, CG><<<grid, kTcThreads, TcGeom<MODE, TT, CG>::kSmem, st>>>(maps, t);
+    if (int rc = launch_chained(tc_expert_gemm_kernel<MODE, TT, CG>, dim3(grid), dim3(kTcThreads),
+                                TcGeom<MODE, TT, CG>::kSmem, st, "tc_expert_gemm_kernel", maps, t))
+      return rc;
   } else {
     // persistent: one cluster per resident SM pair, items strided over the pairs
     const int pairs = (int)(items < resident_pairs ? items : resident_pairs);
     cudaLaunchConfig_t cfg;
-    cudaLaunchAttribute attr;
-    pair_launch_config(&cfg, &attr, pairs, TcGeom<MODE, TT, CG>::kSmem, st);
+    cudaLaunchAttribute attr[2];
+    pair_launch_config(&cfg, attr, pairs, TcGeom<MODE, TT, CG>::kSmem, st, true);
     if (int rc = cuda_check(cudaLaunchKernelEx(&cfg, tc_expert_gemm_kernel<MODE, TT, CG>, maps, t),
                             "cudaLaunchKernelEx(tc pair)"))
       return rc;
@@ -907,6 +916,7 @@ __global__ void __launch_bounds__(256) slice_long_rows_kernel(const XT* __restri
                                                               int8_t* __restrict__ s0, int8_t* __restrict__ s1,
                                                               float* __restrict__ scale) {
   __shared__ float red[8];
+  chain_wait();
   const int row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const XT* x = src + (size_t)row * K;
@@ -946,17 +956,17 @@ int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, i
   if (rows <= 0) return ER_OK;
   if (K > 2048 && K <= 8192) {  // 256 threads x 8 float4 cover 8192 values
     if (dtype == ER_DTYPE_BF16)
-      slice_long_rows_kernel<__nv_bfloat16, 8><<<rows, 256, 0, st>>>((const __nv_bfloat16*)src, K, s0, s1, scale);
-    else
-      slice_long_rows_kernel<float, 8><<<rows, 256, 0, st>>>((const float*)src, K, s0, s1, scale);
-    return launch_check("slice_long_rows_kernel");
+      return launch_chained(slice_long_rows_kernel<__nv_bfloat16, 8>, dim3(rows), dim3(256), 0, st,
+                            "slice_long_rows_kernel", (const __nv_bfloat16*)src, K, s0, s1, scale);
+    return launch_chained(slice_long_rows_kernel<float, 8>, dim3(rows), dim3(256), 0, st, "slice_long_rows_kernel",
+                          (const float*)src, K, s0, s1, scale);
   }
   const int blocks = (rows + 7) / 8;
   if (dtype == ER_DTYPE_BF16)
-    slice_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)src, rows, K, s0, s1, scale);
-  else
-    slice_rows_kernel<float><<<blocks, 256, 0, st>>>((const float*)src, rows, K, s0, s1, scale);
-  return launch_check("slice_rows_kernel");
+    return launch_chained(slice_rows_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, "slice_rows_kernel",
+                          (const __nv_bfloat16*)src, rows, K, s0, s1, scale);
+  return launch_chained(slice_rows_kernel<float>, dim3(blocks), dim3(256), 0, st, "slice_rows_kernel",
+                        (const float*)src, rows, K, s0, s1, scale);
 }
 
 int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
