@@ -175,59 +175,115 @@ int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void
 
 // out[t] = sum over the token's k routed outputs in ascending expert id (the
 // reference accumulates experts in that order, runtime/qwen_moe.py:341-349)
-// + the gated shared-expert output (:359).
-// y_s may be NULL (no shared term); error (optional): nonzero turns the rows into NaN.
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y_r, const float* __restrict__ y_s,
-                                                      const int32_t* __restrict__ pos_of,
-                                                      const int32_t* __restrict__ idx, int k, int H,
-                                                      const int* __restrict__ error, float* __restrict__ out) {
+// + the gated shared-expert output (:359), itself the sum of `parts` partial
+// rows in order. y_s may be NULL (no shared term); error (optional): nonzero
+// turns the rows into NaN, and so does a slot without a position.
+// CTA (t, y): 128 threads of token t, one float4 column each per step over
+// columns y*512 + j*gridDim.y*512. The slots' order is ranked once per CTA;
+// every thread issues all of a column's loads before adding them, so a step
+// costs one round of memory latency. KMAX / PMAX bound k and parts.
+constexpr int kCombineThreads = 128;
+constexpr int kCombineMaxParts = 8;
+
+template <int KMAX, int PMAX>
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ y_r,
+                                                                  const float* __restrict__ y_s, int parts,
+                                                                  const int32_t* __restrict__ pos_of,
+                                                                  const int32_t* __restrict__ idx, int n, int k,
+                                                                  int H, const int* __restrict__ error,
+                                                                  float* __restrict__ out) {
+  __shared__ int pos_sorted[KMAX];
   chain_wait();
   const int t = blockIdx.x;
-  if (error && *error) {
-    for (int c = threadIdx.x; c < H; c += blockDim.x) out[(size_t)t * H + c] = __int_as_float(0x7fc00000);
-    return;
-  }
-  int e_ord[kMaxTopK], p_ord[kMaxTopK];
-  for (int s = 0; s < k; ++s) {
-    e_ord[s] = idx[(size_t)t * k + s];
-    p_ord[s] = pos_of[(size_t)t * k + s];
-  }
-  for (int s = 1; s < k; ++s) {  // insertion sort by expert id
-    const int e = e_ord[s], p = p_ord[s];
-    int j = s - 1;
-    while (j >= 0 && e_ord[j] > e) {
-      e_ord[j + 1] = e_ord[j];
-      p_ord[j + 1] = p_ord[j];
-      --j;
+  if (threadIdx.x < k) {
+    // rank of slot s: slots with a smaller expert id, or the same id and a smaller slot, come first
+    const int s = threadIdx.x;
+    const int e = idx[(size_t)t * k + s];
+    int rank = 0;
+    for (int j = 0; j < k; ++j) {
+      const int ej = idx[(size_t)t * k + j];
+      rank += (ej < e) || (ej == e && j < s);
     }
-    e_ord[j + 1] = e;
-    p_ord[j + 1] = p;
+    pos_sorted[rank] = pos_of[(size_t)t * k + s];
   }
-  for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
+  __syncthreads();
+  const float nan = __int_as_float(0x7fc00000);
+  const bool failed = error && *error;
+  int pos[KMAX];
+  bool missing = false;
+#pragma unroll
+  for (int s = 0; s < KMAX; ++s) {
+    pos[s] = s < k ? pos_sorted[s] : 0;
+    missing |= s < k && pos[s] < 0;
+  }
+  const int step = gridDim.y * kCombineThreads * 4;
+  for (int c = (blockIdx.y * kCombineThreads + threadIdx.x) * 4; c < H; c += step) {
+    float4* dst = reinterpret_cast<float4*>(out + (size_t)t * H + c);
+    if (failed || missing) {
+      *dst = make_float4(nan, nan, nan, nan);
+      continue;
+    }
+    float4 v[KMAX], sv[PMAX];
+#pragma unroll
+    for (int s = 0; s < KMAX; ++s)
+      if (s < k) v[s] = *reinterpret_cast<const float4*>(y_r + (size_t)pos[s] * H + c);
+    if (y_s) {
+#pragma unroll
+      for (int q = 0; q < PMAX; ++q)
+        if (q < parts) sv[q] = *reinterpret_cast<const float4*>(y_s + ((size_t)q * n + t) * H + c);
+    }
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < k; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(y_r + (size_t)p_ord[s] * H + c);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+#pragma unroll
+    for (int s = 0; s < KMAX; ++s) {
+      if (s < k) {
+        acc.x += v[s].x;
+        acc.y += v[s].y;
+        acc.z += v[s].z;
+        acc.w += v[s].w;
+      }
     }
     if (y_s) {
-      const float4 sv = *reinterpret_cast<const float4*>(y_s + (size_t)t * H + c);
-      acc.x += sv.x;
-      acc.y += sv.y;
-      acc.z += sv.z;
-      acc.w += sv.w;
+      float4 sh = sv[0];
+#pragma unroll
+      for (int q = 1; q < PMAX; ++q) {
+        if (q < parts) {
+          sh.x += sv[q].x;
+          sh.y += sv[q].y;
+          sh.z += sv[q].z;
+          sh.w += sv[q].w;
+        }
+      }
+      acc.x += sh.x;
+      acc.y += sh.y;
+      acc.z += sh.z;
+      acc.w += sh.w;
     }
-    *reinterpret_cast<float4*>(out + (size_t)t * H + c) = acc;
+    *dst = acc;
   }
 }
 
-int launch_combine(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k, int H,
-                   const int* error, float* out, cudaStream_t st) {
+template <int KMAX>
+static int launch_combine_k(const float* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx,
+                            int n, int k, int H, const int* error, float* out, dim3 grid, cudaStream_t st) {
+  if (parts <= 1)
+    return launch_chained(combine_kernel<KMAX, 1>, grid, dim3(kCombineThreads), 0, st, "combine_kernel", y_r, y_s,
+                          parts, pos_of, idx, n, k, H, error, out);
+  if (parts <= 4)
+    return launch_chained(combine_kernel<KMAX, 4>, grid, dim3(kCombineThreads), 0, st, "combine_kernel", y_r, y_s,
+                          parts, pos_of, idx, n, k, H, error, out);
+  return launch_chained(combine_kernel<KMAX, kCombineMaxParts>, grid, dim3(kCombineThreads), 0, st, "combine_kernel",
+                        y_r, y_s, parts, pos_of, idx, n, k, H, error, out);
+}
+
+int launch_combine(const float* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx, int n,
+                   int k, int H, const int* error, float* out, cudaStream_t st) {
   if (n <= 0) return ER_OK;
-  return launch_chained(combine_kernel, dim3(n), dim3(256), 0, st, "combine_kernel", y_r, y_s, pos_of, idx, k, H,
-                        error, out);
+  if (parts < 1 || parts > kCombineMaxParts) return fail(ER_EINVAL, "combine: %d shared parts", parts);
+  // a few tokens: their columns spread over CTAs; many: one CTA per token row
+  const int col_blocks = (H / 4 + kCombineThreads - 1) / kCombineThreads;
+  const dim3 grid(n, n >= 2 * 148 ? 1 : col_blocks);
+  if (k <= 4) return launch_combine_k<4>(y_r, y_s, parts, pos_of, idx, n, k, H, error, out, grid, st);
+  return launch_combine_k<kMaxTopK>(y_r, y_s, parts, pos_of, idx, n, k, H, error, out, grid, st);
 }
 
 }  // namespace er

@@ -11,9 +11,10 @@ constexpr int kRouterTok = 8;  // tokens per router CTA
 // routed expert g (its tokens in expert-sorted order), group E is the shared
 // expert (all n tokens). Item count of group g = mtiles(g) * ntiles(g).
 struct SchedSpec {
-  int bm;     // tokens per item (0: all tokens of the group in one item)
-  int bn;     // output units per item
-  int which;  // 0: gate/up (units = intermediate columns), 1: down (units = hidden rows)
+  int bm;      // tokens per item (0: all tokens of the group in one item)
+  int bn;      // output units per item
+  int which;   // 0: gate/up (units = intermediate columns), 1: down (units = hidden rows)
+  int ks = 1;  // down only: parts the shared expert's K is split into (partial outputs)
 };
 
 constexpr int kNumSched = 2;
@@ -110,21 +111,35 @@ constexpr int kRouterKSplit = 4;
 // `tally` (optional, `ntally` ints) is cleared for the top-k kernel's counts.
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
                          float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st);
-// softmax + top-k over the sum of `nparts` partial logits (and `gparts` partial
-// shared-gate logits); logits_sum (optional) receives the summed logits;
-// tally (optional) counts the selected (token, slot) pairs per expert
-int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
-                       int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
-                       int* tally, cudaStream_t st);
+// The top-k step's inputs and outputs: softmax + top-k over the sum of
+// `nparts` partial logits (and the sigmoid of `gparts` partial shared-gate
+// logits).
+struct TopkArgs {
+  const float* logits;      // [nparts][n][E] partial logits, added in order
+  int nparts, gparts;       // logit / shared-gate partials
+  int norm;                 // renormalise the k weights to sum 1
+  int64_t* idx64;           // optional [n, k] ids
+  int32_t* idx32;           // optional [n, k] ids
+  float* wout;              // optional [n, k] weights
+  const float* gate_logit;  // optional [gparts][n] shared-gate partial logits
+  float* gate_sig;          // optional [n] sigmoid of their sum
+  float* logits_sum;        // optional [n, E] summed logits
+  int* tally;               // optional [E] counts of the selected (token, slot) pairs per expert
+};
+int launch_router_topk(const TopkArgs& a, int n, int E, int k, cudaStream_t st);
+// Batches of at most this many tokens run the top-k inside the dispatch kernel.
+constexpr int kFusedTopkMaxTok = 16;
 // The plan (groups, ranges, work-item schedules; the shared expert, all n
 // tokens, is the last group when `shared` is nonzero) from plan->tally, and
 // the scatter of the (token, slot) pairs to expert-sorted positions
 // (perm_token, perm_w, pos_of). With s0 non-null also slices each token's h
 // row once and writes the slices to its k routed positions and, when
-// `shared` is nonzero, to shared row nk + t.
+// `shared` is nonzero, to shared row nk + t. With `topk` non-null (n <=
+// kFusedTopkMaxTok) the kernel first runs that top-k step itself, whose
+// idx32 / wout / tally must be idx / w / plan->tally.
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
                     int Is, const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
-                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, cudaStream_t st);
+                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk, cudaStream_t st);
 // Upper bound of the items a schedule can produce (host side, for grid sizing).
 long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int I, int Is);
 
@@ -134,9 +149,10 @@ int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void
                              float* act_r, float* act_s, float* out_r, float* out_s,
                              long long items_bound, cudaStream_t st);
 // out[t] = sum over t's k slots, in ascending expert id (idx), of y_r[pos_of[t * k + j]]
-// (+ y_s[t] when y_s is not NULL); rows of NaN when *error is nonzero
-int launch_combine(const float* y_r, const float* y_s, const int32_t* pos_of, const int32_t* idx, int n, int k, int H,
-                   const int* error, float* out, cudaStream_t st);
+// (+ the `parts` partial shared rows y_s[p * n + t], in order, when y_s is not
+// NULL); rows of NaN when *error is nonzero
+int launch_combine(const float* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx, int n,
+                   int k, int H, const int* error, float* out, cudaStream_t st);
 // per-expert counts of ids[0..m) into tally[E] (nclear ints from tally cleared
 // first); out-of-range ids are not counted
 int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaStream_t st);
@@ -156,15 +172,37 @@ struct TcLaunch {
   const int8_t *b0_s, *b1_s;   // mode 1: shared act rows
   int has_shared;              // the shared expert is one of the groups (its maps are needed)
   const float *xscale_r, *xscale_s;
-  float *out_r, *out_s;
+  float *out_r, *out_s;        // mode 1: out_s holds shared_parts partial [n, H] outputs
+  int shared_parts;            // mode 1: K parts of the shared expert's down items (the schedule's ks)
   long long items_bound;
 };
 int launch_tc_grouped(const TcLaunch& L, cudaStream_t st);
 // two int8 slices and a scale per row of a [rows, K] fp32 / bf16 matrix
 int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, int8_t* s1, float* scale,
                       cudaStream_t st);
+// rows [0, rows) of a [rows, K] fp32 matrix to slice (the same outputs as launch_slice_rows)
+struct SliceSet {
+  const float* src;
+  int rows, K;
+  int8_t *s0, *s1;
+  float* scale;
+};
+// two such sets in one launch (K up to 8192 each)
+int launch_slice_sets(const SliceSet& a, const SliceSet& b, cudaStream_t st);
 // tokens per tcgen05 work item: 16 when every group fits (n <= 16), else 128
 inline int tc_tok_tile(int n) { return n <= 16 ? 16 : 128; }
+constexpr int kTcKBlock = 256;  // K elements per tcgen05 pipeline stage
+// Decode tiles split the shared expert's down product (K = Is, Is / I times a
+// routed expert's) into parts of about a routed expert's K, so its items take
+// no longer than the others; the parts' outputs are added by the combine.
+// Every part is non-empty: ks = ceil(blocks / ceil(blocks / wanted)).
+inline int tc_shared_parts(int tok_tile, int I, int Is) {
+  if (tok_tile > 16) return 1;
+  const int blocks = (Is + kTcKBlock - 1) / kTcKBlock;
+  const int want = Is / I > 1 ? Is / I : 1;
+  const int span = (blocks + want - 1) / want;
+  return (blocks + span - 1) / span;
+}
 // CTAs per work item: 128-token tiles run on an SM pair (tcgen05 cta_group::2,
 // M = 256), 16-token tiles on one SM.
 inline int tc_cta_group(int tok_tile) { return tok_tile >= 128 ? 2 : 1; }

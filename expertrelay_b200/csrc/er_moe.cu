@@ -37,6 +37,11 @@ struct Run {
 static int run_k(const er_moe_weights* w, int mode) { return mode == kBlock ? w->top_k : (mode == kRows ? 1 : 0); }
 static bool run_shared(int mode) { return mode != kRows; }
 
+// partial outputs of the shared expert's down product (K parts of its tiles)
+static int shared_parts(const er_moe_weights* w, int n, int path) {
+  return path == ER_PATH_TC ? tc_shared_parts(tc_tok_tile(n), w->inter, w->shared_inter) : 1;
+}
+
 struct WsLayout {
   size_t logits, gate_logit, gate_sig, idx32, topw, plan, perm_token, perm_w, pos_of, act_r, act_s, y_r, y_s;
   // tensor-core path: int8 activation slices and their row scales
@@ -67,7 +72,7 @@ static WsLayout ws_layout(const er_moe_weights* w, int n, int path, int mode) {
   L.act_r = take(nk * w->inter * 4);
   L.act_s = take(ns * w->shared_inter * 4);
   L.y_r = take(nk * w->hidden * 4);
-  L.y_s = take(ns * w->hidden * 4);
+  L.y_s = take(shared_parts(w, n, path) * ns * w->hidden * 4);
   if (path == ER_PATH_TC) {
     const size_t rows = nk + ns;
     L.xs0 = take(rows * w->hidden);
@@ -176,6 +181,8 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
   float* y_s = shared ? reinterpret_cast<float*>(ws + L.y_s) : nullptr;
   const int32_t* idx32 = nullptr;  // expert id of each (token, slot)
   const float* topw = nullptr;     // its routing weight
+  TopkArgs topk{};                 // the block's top-k step
+  bool fused_topk = false;         // run by the dispatch kernel (small batches)
 
   // K1: routing (the block), the shared gate alone, or the rows' expert counts
   if (mode == kBlock) {
@@ -196,15 +203,23 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
         return rc;
       gparts = nparts;
     }
-    if (int rc = launch_router_topk(lg, nparts, gparts, n, E, k, w->norm_topk_prob, r.topk_idx_out, idx, wts,
-                                    gate_logit, gate_sig, logits_sum, plan->tally, st))
-      return rc;
-    launches += 2;
-    if (r.topk_w_out) {
-      if (int rc = cuda_check(cudaMemcpyAsync(r.topk_w_out, wts, nk * 4, cudaMemcpyDeviceToDevice, st),
-                              "copy top-k weights"))
-        return rc;
+    topk.logits = lg;
+    topk.nparts = nparts;
+    topk.gparts = gparts;
+    topk.norm = w->norm_topk_prob;
+    topk.idx64 = r.topk_idx_out;
+    topk.idx32 = idx;
+    topk.wout = wts;
+    topk.gate_logit = gate_logit;
+    topk.gate_sig = gate_sig;
+    topk.logits_sum = logits_sum;
+    topk.tally = plan->tally;
+    fused_topk = n <= kFusedTopkMaxTok;
+    if (!fused_topk) {
+      if (int rc = launch_router_topk(topk, n, E, k, st)) return rc;
+      launches += 1;
     }
+    launches += 1;
     idx32 = idx;
     topw = wts;
   } else if (mode == kShared) {
@@ -230,7 +245,7 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     specs[1] = SchedSpec{0, kGemvUnitsDN, 1};
   } else if (path == ER_PATH_TC) {
     specs[0] = SchedSpec{tc_tok_tile(n), tc_units_gu(tc_tok_tile(n)), 0};
-    specs[1] = SchedSpec{tc_tok_tile(n), tc_units_dn(tc_tok_tile(n)), 1};
+    specs[1] = SchedSpec{tc_tok_tile(n), tc_units_dn(tc_tok_tile(n)), 1, shared_parts(w, n, path)};
   } else {
     specs[0] = SchedSpec{kSimtBM, kSimtBN, 0};
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
@@ -240,9 +255,14 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
   int8_t* xs1 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs1) : nullptr;
   float* xscale = path == ER_PATH_TC ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
   if (int rc = launch_dispatch(r.h, r.h_dtype, idx32, topw, n, k, E, H, w->inter, w->shared_inter, specs, shared,
-                               plan, perm_token, perm_w, pos_of, xs0, xs1, xscale, st))
+                               plan, perm_token, perm_w, pos_of, xs0, xs1, xscale, fused_topk ? &topk : nullptr, st))
     return rc;
   launches += 1;
+  if (mode == kBlock && r.topk_w_out) {
+    if (int rc = cuda_check(cudaMemcpyAsync(r.topk_w_out, topw, nk * 4, cudaMemcpyDeviceToDevice, st),
+                            "copy top-k weights"))
+      return rc;
+  }
   if (int rc = mark(2)) return rc;
 
   GroupArgs ga;
@@ -291,12 +311,10 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     tl.items_bound = b0;
     if (int rc = launch_tc_grouped(tl, st)) return rc;
     if (int rc = mark(3)) return rc;
-    if (nk > 0) {
-      if (int rc = launch_slice_rows(act_r, ER_DTYPE_F32, (int)nk, w->inter, as0_r, as1_r, ascale_r, st)) return rc;
-      launches += 1;
-    }
-    if (shared) {
-      if (int rc = launch_slice_rows(act_s, ER_DTYPE_F32, n, w->shared_inter, as0_s, as1_s, ascale_s, st)) return rc;
+    if (nk > 0 || shared) {
+      const SliceSet routed{act_r, (int)nk, w->inter, as0_r, as1_r, ascale_r};
+      const SliceSet shared_rows{act_s, shared ? n : 0, w->shared_inter, as0_s, as1_s, ascale_s};
+      if (int rc = launch_slice_sets(routed, shared_rows, st)) return rc;
       launches += 1;
     }
     tl.mode = 1;
@@ -309,6 +327,7 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     tl.xscale_s = ascale_s;
     tl.out_r = y_r;
     tl.out_s = y_s;
+    tl.shared_parts = specs[1].ks;
     tl.items_bound = b1;
     if (int rc = launch_tc_grouped(tl, st)) return rc;
   } else if (path == ER_PATH_GEMV) {
@@ -325,7 +344,7 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
   launches += 2 * per_stage;
   if (int rc = mark(4)) return rc;
   // K4
-  if (int rc = launch_combine(y_r, y_s, pos_of, idx32, n, k, H, &plan->error, r.y, st)) return rc;
+  if (int rc = launch_combine(y_r, y_s, specs[1].ks, pos_of, idx32, n, k, H, &plan->error, r.y, st)) return rc;
   launches += 1;
   if (r.launch_count) *r.launch_count += launches;
   return mark(5);
@@ -405,5 +424,5 @@ extern "C" int er_moe_combine(const float* y_rows, const int32_t* pos_of, const 
   if (!y || (k > 0 && (!y_rows || !pos_of || !idx))) return fail(ER_EINVAL, "er_moe_combine: null argument");
   if (((uintptr_t)y_rows | (uintptr_t)y_shared | (uintptr_t)y) & 15)
     return fail(ER_EINVAL, "er_moe_combine: rows must be 16-byte aligned");
-  return launch_combine(y_rows, y_shared, pos_of, idx, n, k, hidden, nullptr, y, (cudaStream_t)stream);
+  return launch_combine(y_rows, y_shared, 1, pos_of, idx, n, k, hidden, nullptr, y, (cudaStream_t)stream);
 }

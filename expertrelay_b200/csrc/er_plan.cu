@@ -17,99 +17,110 @@
 // the token order; nothing downstream depends on it: every output element is
 // computed from its own token's row alone, and the combine sums each token's
 // slots in ascending expert id through pos_of.
-#include "er_internal.cuh"
+#include "er_select.cuh"
 
 namespace er {
 
-// The plan from the per-expert tallies, by one warp: lane l owns entries
-// 9l .. 9l+8 of the per-expert lists (enough for E + 2 <= 258) and the scans
-// run over the lanes. Every caller gets the expert ranges' first positions in
-// `offs` (shared memory) and whether the tallies are consistent; with
-// write_plan it also writes the plan's groups, ranges and work-item schedules
-// for the expert kernels.
-__device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, int I, int Is, SchedSpec s0,
-                          SchedSpec s1, int shared, bool write_plan, int* hist, int* offs, int* act, int* bad_out) {
-  constexpr int kPer = 9;
-  const int lane = threadIdx.x & 31;
-  const int nk = n * k;
-  auto warp_excl_scan = [&](int v) {  // exclusive prefix of v over the lanes
-    int incl = v;
+// Exclusive prefix of v over the CTA (every thread calls; `tmp` holds one
+// int per warp); *total receives the sum over the CTA.
+__device__ __forceinline__ int cta_excl_scan(int v, int* tmp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = v;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    return incl - v;
-  };
-  for (int e = lane; e < E; e += 32) hist[e] = plan->tally[e];
-  __syncwarp();
-  int sum = 0, nact = 0;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = lane * kPer + j;
-    if (e < E) {
-      sum += hist[e];
-      nact += hist[e] > 0;
-    }
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
   }
-  int off = warp_excl_scan(sum), pos = warp_excl_scan(nact);
-  const int total = __shfl_sync(0xffffffffu, off + sum, 31);
-  const int na_routed = __shfl_sync(0xffffffffu, pos + nact, 31);
+  if (lane == 31) tmp[warp] = incl;
+  __syncthreads();
+  int base = 0, tot = 0;
+  for (int w = 0; w < nw; ++w) {
+    const int x = tmp[w];
+    base += w < warp ? x : 0;
+    tot += x;
+  }
+  __syncthreads();  // tmp is reused by the next scan
+  *total = tot;
+  return base + incl - v;
+}
+
+// The plan from the per-expert tallies, by the whole CTA (at least 256
+// threads; thread i owns entries 2i, 2i+1 of the per-expert and per-group
+// lists, enough for E + 2 <= 258). Every caller gets the expert ranges' first
+// positions in `offs` (shared memory) and whether the tallies are consistent;
+// with write_plan it also writes the plan's groups, ranges and work-item
+// schedules for the expert kernels. Ends with a __syncthreads.
+__device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, int I, int Is, SchedSpec s0,
+                          SchedSpec s1, int shared, bool write_plan, int* hist, int* offs, int* act, int* bad_out,
+                          int* tmp) {
+  const int tid = threadIdx.x;
+  const int nk = n * k;
+  int cnt[2], on[2];
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = lane * kPer + j;
+  for (int j = 0; j < 2; ++j) {
+    const int e = 2 * tid + j;
+    cnt[j] = e < E ? __ldcg(&plan->tally[e]) : 0;  // counted at L2 by atomics
+    on[j] = cnt[j] > 0;
+    if (e < E) hist[e] = cnt[j];
+  }
+  int total, na_routed;
+  int off = cta_excl_scan(cnt[0] + cnt[1], tmp, &total);
+  int pos = cta_excl_scan(on[0] + on[1], tmp, &na_routed);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int e = 2 * tid + j;
     if (e < E) {
       offs[e] = off;
       if (write_plan) {
-        plan->counts[e] = hist[e];
+        plan->counts[e] = cnt[j];
         plan->offsets[e] = off;
       }
-      off += hist[e];
-      if (hist[e] > 0) act[pos++] = e;
+      off += cnt[j];
+      if (on[j]) act[pos++] = e;
     }
   }
   // every pair lands in some expert's range: the counts must add up to n * k
   const bool bad = total != nk;
-  if (lane == 0) *bad_out = bad;
+  if (tid == 0) *bad_out = bad;
   if (!write_plan) {
-    __syncwarp();
+    __syncthreads();
     return;
   }
   const int na = na_routed + (shared && n > 0 ? 1 : 0);
-  if (lane == 0) {
+  if (tid == 0) {
     if (shared && n > 0) act[na_routed] = E;
     plan->counts[E] = n;
     plan->offsets[E] = 0;
   }
-  __syncwarp();
-  for (int a = lane; a < na; a += 32) plan->active[a] = act[a];
-  const SchedSpec specs[kNumSched] = {s0, s1};
-#pragma unroll
+  __syncthreads();
+  for (int a = tid; a < na; a += blockDim.x) plan->active[a] = act[a];
+#pragma unroll 1
   for (int s = 0; s < kNumSched; ++s) {
-    const SchedSpec sp = specs[s];
-    int items[kPer], local = 0;
+    const SchedSpec sp = s == 0 ? s0 : s1;
+    int items[2];
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int a = lane * kPer + j;
+    for (int j = 0; j < 2; ++j) {
+      const int a = 2 * tid + j;
       items[j] = 0;
       if (a < na) {
         const int g = act[a];
         const int rows = g == E ? n : hist[g];
         const int units = sp.which == 0 ? (g == E ? Is : I) : H;
         const int mt = sp.bm > 0 ? (rows + sp.bm - 1) / sp.bm : 1;
-        items[j] = mt * ((units + sp.bn - 1) / sp.bn);
+        const int parts = (g == E && sp.which == 1 && sp.ks > 1) ? sp.ks : 1;
+        items[j] = mt * ((units + sp.bn - 1) / sp.bn) * parts;
       }
-      local += items[j];
     }
-    int start_a = warp_excl_scan(local);
+    int sum;
+    int start = cta_excl_scan(items[0] + items[1], tmp, &sum);
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int a = lane * kPer + j;
-      if (a <= na) plan->item_start[s][a] = bad ? 0 : start_a;
-      start_a += items[j];
+    for (int j = 0; j < 2; ++j) {
+      const int a = 2 * tid + j;
+      if (a <= na) plan->item_start[s][a] = bad ? 0 : start;
+      start += items[j];
     }
   }
-  if (lane == 0) {
+  if (tid == 0) {
     plan->n = n;
     plan->E = E;
     plan->k = k;
@@ -119,38 +130,66 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
     plan->sched[1] = s1;
     plan->num_active = bad ? 0 : na;  // no work items on an inconsistent tally
   }
-  __syncwarp();
+  __syncthreads();
 }
 
-// Eight tokens per CTA, one warp each. Warp 0 first derives the expert
-// ranges from the tallies (CTA 0 also writes the plan). Then lane r < k of a
-// token's warp claims the position of slot r (its expert's range start plus
-// an atomic count, from 0); with SLICE the warp slices h[t] (K = H values)
-// and writes the slices to the k claimed rows and, for the shared expert, to
-// row nk + t. Rows of up to 2048 values stay in registers; longer rows are
-// read twice.
-template <typename XT, bool SLICE>
-__global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
+// One token per warp (8 per CTA; with KPER, top-k fused, one CTA of up to 16
+// warps for the whole batch: each warp first runs its token's softmax +
+// top-k, counting into plan->tally, before anything below). With SLICE and rows of up to 2048
+// values, each warp first slices its token's h row (K = H values) into two
+// int8 words per lane and step, held in registers; the CTA then derives the
+// expert ranges from the tallies (CTA 0 also writes the plan). Then lane r < k of a token's warp claims the
+// position of slot r (its expert's range start plus an atomic count, from 0)
+// and the warp writes the slices to the k claimed rows and, for the shared
+// expert, to row nk + t. Longer rows are read twice after the scan. The row
+// loop is not unrolled: this kernel runs once per block, mostly from a cold
+// instruction cache, so its code is kept short.
+template <typename XT, bool SLICE, int KPER>
+__global__ void __launch_bounds__(512) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
                                                        const float* __restrict__ w, int n, int k, int E, int H, int I,
                                                        int Is, SchedSpec spec0, SchedSpec spec1, int shared,
                                                        Plan* __restrict__ plan, int32_t* __restrict__ perm_token,
                                                        float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
                                                        int8_t* __restrict__ s0, int8_t* __restrict__ s1,
-                                                       float* __restrict__ scale) {
+                                                       float* __restrict__ scale, TopkArgs topk) {
   __shared__ int hist[kMaxExperts];
   __shared__ int offs[kMaxExperts];
   __shared__ int act[kMaxExperts + 1];
   __shared__ int bad;
+  __shared__ int scan_tmp[16];
   chain_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (warp == 0) plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad);
-  __syncthreads();
-  const int t = blockIdx.x * 8 + warp;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if constexpr (KPER > 0) {
+    if (t < n) topk_token<KPER>(topk, n, E, k, t, lane);
+    __threadfence();  // the tallies (L2 atomics) and ids before the scan reads them
+  }
+  constexpr int kRegVec = 16;  // float4 per lane held in registers: H <= 2048
+  const bool in_regs = SLICE && H <= 128 * kRegVec;
+  uint32_t q0[kRegVec], q1[kRegVec];
+  float amax = 0.f;
+  if (in_regs && t < n) {
+    const XT* x = h + (size_t)t * H;
+    float4 v[kRegVec];
+#pragma unroll
+    for (int i = 0; i < kRegVec; ++i) {
+      const int c = lane * 4 + 128 * i;
+      v[i] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      amax = fmaxf(amax, abs_max4(v[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+#pragma unroll
+    for (int i = 0; i < kRegVec; ++i) slice4(v[i], inv, q0[i], q1[i]);
+  }
+  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad, scan_tmp);
   if (t >= n || bad) return;  // nothing downstream reads positions of an inconsistent tally
   const int nk = n * k;
   int p = -1;
   if (lane < k) {
-    const int e = idx[(size_t)t * k + lane];
+    // ids and weights written by this kernel's top-k are read at L2, not through the read-only cache
+    const int e = KPER > 0 ? __ldcg(idx + (size_t)t * k + lane) : idx[(size_t)t * k + lane];
     if (e >= 0 && e < E) {
       const int c = atomicAdd(&plan->cursor[e], 1);
       if (c >= hist[e]) {  // only an inconsistent tally gets here
@@ -158,7 +197,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
       } else {
         p = offs[e] + c;
         perm_token[p] = t;
-        perm_w[p] = w[(size_t)t * k + lane];
+        perm_w[p] = KPER > 0 ? __ldcg(w + (size_t)t * k + lane) : w[(size_t)t * k + lane];
       }
     } else {
       atomicOr(&plan->error, 1);
@@ -166,47 +205,38 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
     pos_of[(size_t)t * k + lane] = p;
   }
   if constexpr (SLICE) {
-    int prow[kMaxTopK + 1];
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) prow[r] = __shfl_sync(0xffffffffu, p, r < k ? r : 31);
-    prow[kMaxTopK] = shared ? nk + t : -1;  // the shared expert's row
     const XT* x = h + (size_t)t * H;
-    auto put = [&](int c, float4 v, float inv) {
-      uint32_t w0, w1;
-      slice4(v, inv, w0, w1);
-#pragma unroll
-      for (int r = 0; r <= kMaxTopK; ++r) {
-        const int row = r < kMaxTopK ? (r < k ? prow[r] : -1) : prow[kMaxTopK];
-        if (row >= 0) {
-          *reinterpret_cast<uint32_t*>(s0 + (size_t)row * H + c) = w0;
-          *reinterpret_cast<uint32_t*>(s1 + (size_t)row * H + c) = w1;
-        }
-      }
-    };
-    float amax = 0.f;
-    constexpr int kRegVec = 16;  // float4 per lane held in registers: H <= 2048
-    if (H <= 128 * kRegVec) {
-      float4 v[kRegVec];
-#pragma unroll
-      for (int i = 0; i < kRegVec; ++i) {
-        const int c = lane * 4 + 128 * i;
-        v[i] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        amax = fmaxf(amax, abs_max4(v[i]));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float inv = amax > 0.f ? 127.f / amax : 0.f;
-#pragma unroll
-      for (int i = 0; i < kRegVec; ++i) {
-        const int c = lane * 4 + 128 * i;
-        if (c < H) put(c, v[i], inv);
-      }
-    } else {
+    if (!in_regs) {
       for (int c = lane * 4; c < H; c += 128) amax = fmaxf(amax, abs_max4(load4(x + c)));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float inv = amax > 0.f ? 127.f / amax : 0.f;
-      for (int c = lane * 4; c < H; c += 128) put(c, load4(x + c), inv);
+    }
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+    // rows r < k: the claimed positions; row k: the shared expert's row
+#pragma unroll 1
+    for (int r = 0; r <= k; ++r) {
+      const int pr = __shfl_sync(0xffffffffu, p, r < k ? r : 0);
+      const int row = r < k ? pr : (shared ? nk + t : -1);
+      if (row < 0) continue;
+      int8_t* d0 = s0 + (size_t)row * H;
+      int8_t* d1 = s1 + (size_t)row * H;
+      if (in_regs) {
+#pragma unroll
+        for (int i = 0; i < kRegVec; ++i) {
+          const int c = lane * 4 + 128 * i;
+          if (c < H) {
+            *reinterpret_cast<uint32_t*>(d0 + c) = q0[i];
+            *reinterpret_cast<uint32_t*>(d1 + c) = q1[i];
+          }
+        }
+      } else {
+        for (int c = lane * 4; c < H; c += 128) {
+          uint32_t w0, w1;
+          slice4(load4(x + c), inv, w0, w1);
+          *reinterpret_cast<uint32_t*>(d0 + c) = w0;
+          *reinterpret_cast<uint32_t*>(d1 + c) = w1;
+        }
+      }
     }
     if (lane < k && p >= 0) scale[p] = amax / 127.f;
     if (lane == 31 && shared) scale[nk + t] = amax / 127.f;
@@ -226,7 +256,7 @@ long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int 
   }
   const long long nt_r = s.which == 0 ? (I + s.bn - 1) / s.bn : (H + s.bn - 1) / s.bn;
   const long long nt_s = s.which == 0 ? (Is + s.bn - 1) / s.bn : (H + s.bn - 1) / s.bn;
-  return routed_rows_tiles * nt_r + shared_tiles * nt_s;
+  return routed_rows_tiles * nt_r + shared_tiles * nt_s * (s.which == 1 && s.ks > 1 ? s.ks : 1);
 }
 
 __global__ void __launch_bounds__(256) tally_kernel(const int32_t* __restrict__ ids, int m, int E,
@@ -244,21 +274,41 @@ int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaS
   return launch_chained(tally_kernel, dim3((m + 255) / 256), dim3(256), 0, st, "tally_kernel", ids, m, E, tally);
 }
 
+template <typename XT, bool SLICE>
+static int launch_dispatch_t(const XT* h, const int32_t* idx, const float* w, int n, int k, int E, int H, int I, int Is,
+                             const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
+                             int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk,
+                             cudaStream_t st) {
+  if (topk) {  // one CTA, one warp per token
+    const dim3 block(32 * (n > 8 ? 16 : 8));
+    if (E <= 64)
+      return launch_chained(dispatch_kernel<XT, SLICE, 2>, dim3(1), block, 0, st, "dispatch_kernel", h, idx, w, n, k,
+                            E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1, scale,
+                            *topk);
+    return launch_chained(dispatch_kernel<XT, SLICE, kMaxExperts / 32>, dim3(1), block, 0, st, "dispatch_kernel", h,
+                          idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0,
+                          s1, scale, *topk);
+  }
+  const int blocks = n > 0 ? (n + 7) / 8 : 1;  // CTA 0 writes the plan even for no tokens
+  return launch_chained(dispatch_kernel<XT, SLICE, 0>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel", h, idx, w,
+                        n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1, scale,
+                        TopkArgs{});
+}
+
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
                     int Is, const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
-                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, cudaStream_t st) {
-  const int blocks = n > 0 ? (n + 7) / 8 : 1;  // CTA 0 writes the plan even for no tokens
+                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk, cudaStream_t st) {
+  if (topk && (n > kFusedTopkMaxTok || topk->idx32 != idx || topk->wout != w || topk->tally != plan->tally))
+    return fail(ER_EINVAL, "dispatch: fused top-k needs n <= %d and its outputs as the dispatch inputs",
+                kFusedTopkMaxTok);
   if (!s0)
-    return launch_chained(dispatch_kernel<float, false>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel",
-                          (const float*)nullptr, idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan,
-                          perm_token, perm_w, pos_of, (int8_t*)nullptr, (int8_t*)nullptr, (float*)nullptr);
+    return launch_dispatch_t<float, false>(nullptr, idx, w, n, k, E, H, I, Is, specs, shared, plan, perm_token, perm_w,
+                                           pos_of, nullptr, nullptr, nullptr, topk, st);
   if (h_dtype == ER_DTYPE_BF16)
-    return launch_chained(dispatch_kernel<__nv_bfloat16, true>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel",
-                          (const __nv_bfloat16*)h, idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan,
-                          perm_token, perm_w, pos_of, s0, s1, scale);
-  return launch_chained(dispatch_kernel<float, true>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel",
-                        (const float*)h, idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token,
-                        perm_w, pos_of, s0, s1, scale);
+    return launch_dispatch_t<__nv_bfloat16, true>((const __nv_bfloat16*)h, idx, w, n, k, E, H, I, Is, specs, shared,
+                                                  plan, perm_token, perm_w, pos_of, s0, s1, scale, topk, st);
+  return launch_dispatch_t<float, true>((const float*)h, idx, w, n, k, E, H, I, Is, specs, shared, plan, perm_token,
+                                        perm_w, pos_of, s0, s1, scale, topk, st);
 }
 
 }  // namespace er

@@ -4,7 +4,7 @@
 // probs = softmax over all experts in fp32, selected = top-k largest first,
 // weights = probs of the selected experts, no renormalisation when
 // norm_topk_prob is False) and :358 (shared-expert gate logit h @ w_g^T).
-#include "er_internal.cuh"
+#include "er_select.cuh"
 
 namespace er {
 
@@ -180,119 +180,13 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__
   }
 }
 
-// Softmax over the E logits of one token held by a warp (lane l holds
-// experts l + 32 j in v[j]; max subtracted, expf, sum, divide) and top-k by
-// logit value, largest first, exact ties to the lower expert id. Ranking by
-// the logits equals ranking by the probabilities because every step of the
-// softmax is monotone; NaN logits rank as -inf. Writes token t's ids and
-// weights; tally (optional) counts the selected experts.
-template <int kPer>
-__device__ __forceinline__ void warp_select(const float (&v)[kPer], int E, int k, int norm, int t, int lane,
-                                            int64_t* __restrict__ idx64, int32_t* __restrict__ idx32,
-                                            float* __restrict__ wout, int* __restrict__ tally) {
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, v[j]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float ex[kPer], s = 0.f;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = lane + 32 * j;
-    ex[j] = (e < E) ? expf(v[j] - mx) : 0.f;
-    s += ex[j];
-  }
-  s = warp_sum(s);
-
-  uint32_t taken = 0;  // bit j: entry lane + 32 j already selected
-  int sel[kMaxTopK];
-  float pw[kMaxTopK];
-  float wsum = 0.f;
-  for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E && !(taken & (1u << j))) {
-        const float c = (v[j] != v[j]) ? -INFINITY : v[j];
-        if (c > bv || (c == bv && e < bi)) {
-          bv = c;
-          bi = e;
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    // the owner lane marks the entry and broadcasts its probability
-    const int owner = bi & 31, oj = bi >> 5;
-    float p = 0.f;
-    if (lane == owner) {
-#pragma unroll
-      for (int j = 0; j < kPer; ++j)
-        if (j == oj) {
-          taken |= 1u << j;
-          p = ex[j] / s;
-        }
-    }
-    p = __shfl_sync(0xffffffffu, p, owner);
-    sel[r] = bi;
-    pw[r] = p;
-    wsum += p;
-  }
-  if (tally)  // lane r counts slot r's expert
-    for (int r = 0; r < k; ++r)
-      if (lane == r) atomicAdd(&tally[sel[r]], 1);
-  if (lane == 0) {
-    for (int r = 0; r < k; ++r) {
-      const float w = norm ? pw[r] / wsum : pw[r];
-      if (idx64) idx64[(size_t)t * k + r] = sel[r];
-      if (idx32) idx32[(size_t)t * k + r] = sel[r];
-      if (wout) wout[(size_t)t * k + r] = w;
-    }
-  }
-}
-
 // One warp per token over logits summed from `nparts` K-slice partials.
 template <int kPer>
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int nparts, int gparts,
-                                                          int n, int E,
-                                                          int k, int norm, int64_t* __restrict__ idx64,
-                                                          int32_t* __restrict__ idx32,
-                                                          float* __restrict__ wout,
-                                                          const float* __restrict__ gate_logit,
-                                                          float* __restrict__ gate_sig,
-                                                          float* __restrict__ logits_sum, int* __restrict__ tally) {
+__global__ void __launch_bounds__(256) router_topk_kernel(TopkArgs a, int n, int E, int k) {
   chain_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
   if (t >= n) return;
-  const float* l = logits + (size_t)t * E;
-  float v[kPer];
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = lane + 32 * j;
-    v[j] = -INFINITY;
-    if (e < E) {  // partial logits of K slices, added in slice order
-      float a = l[e];
-      for (int p = 1; p < nparts; ++p) a += l[(size_t)p * n * E + e];
-      v[j] = a;
-      if (logits_sum) logits_sum[(size_t)t * E + e] = a;
-    }
-  }
-  warp_select<kPer>(v, E, k, norm, t, lane, idx64, idx32, wout, tally);
-  if (lane == 0 && gate_sig && gate_logit) {
-    float gl = gate_logit[t];
-    for (int p = 1; p < gparts; ++p) gl += gate_logit[(size_t)p * n + t];
-    gate_sig[t] = sigmoid_f(gl);
-  }
+  topk_token<kPer>(a, n, E, k, t, threadIdx.x & 31);
 }
 
 __global__ void __launch_bounds__(256) gate_sigmoid_kernel(const float* __restrict__ gate_logit, int nparts, int n,
@@ -332,19 +226,15 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
                         wr, wg, E, logits, gate_logit, tally, ntally);
 }
 
-int launch_router_topk(const float* logits, int nparts, int gparts, int n, int E, int k, int norm, int64_t* idx64,
-                       int32_t* idx32, float* wout, const float* gate_logit, float* gate_sig, float* logits_sum,
-                       int* tally, cudaStream_t st) {
+int launch_router_topk(const TopkArgs& a, int n, int E, int k, cudaStream_t st) {
   if (n <= 0) return ER_OK;
   const int warps_per_block = 8;
   const int blocks = (n + warps_per_block - 1) / warps_per_block;
   if (E <= 64)
     return launch_chained(router_topk_kernel<2>, dim3(blocks), dim3(warps_per_block * 32), 0, st,
-                          "router_topk_kernel", logits, nparts, gparts, n, E, k, norm, idx64, idx32, wout, gate_logit,
-                          gate_sig, logits_sum, tally);
+                          "router_topk_kernel", a, n, E, k);
   return launch_chained(router_topk_kernel<kMaxExperts / 32>, dim3(blocks), dim3(warps_per_block * 32), 0, st,
-                        "router_topk_kernel", logits, nparts, gparts, n, E, k, norm, idx64, idx32, wout, gate_logit,
-                        gate_sig, logits_sum, tally);
+                        "router_topk_kernel", a, n, E, k);
 }
 
 
@@ -358,6 +248,12 @@ extern "C" int er_router_topk(const float* logits, int n, int num_experts, int k
     return fail(ER_EINVAL, "er_router_topk: num_experts %d outside 1..%d", num_experts, kMaxExperts);
   if (k < 1 || k > kMaxTopK || k > num_experts)
     return fail(ER_EINVAL, "er_router_topk: k %d outside 1..min(%d, num_experts)", k, kMaxTopK);
-  return launch_router_topk(logits, 1, 1, n, num_experts, k, 0, idx64, idx32, probs_out, nullptr, nullptr, nullptr,
-                            nullptr, (cudaStream_t)stream);
+  TopkArgs a{};
+  a.logits = logits;
+  a.nparts = 1;
+  a.gparts = 1;
+  a.idx64 = idx64;
+  a.idx32 = idx32;
+  a.wout = probs_out;
+  return launch_router_topk(a, n, num_experts, k, (cudaStream_t)stream);
 }

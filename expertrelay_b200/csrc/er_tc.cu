@@ -278,14 +278,9 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // slices (slice4). Rows of up to 2048 values are held in registers and read
 // once; longer rows are read twice (max, then slices).
 template <typename XT>
-__global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ src, int rows, int K,
-                                                         int8_t* __restrict__ s0, int8_t* __restrict__ s1,
-                                                         float* __restrict__ scale) {
+__device__ __forceinline__ void slice_row_warp(const XT* __restrict__ src, int row, int K, int8_t* __restrict__ s0,
+                                               int8_t* __restrict__ s1, float* __restrict__ scale, int lane) {
   constexpr int kRegVec = 16;  // float4 per lane held in registers: K <= 2048
-  chain_wait();
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
   const XT* x = src + (size_t)row * K;
   int8_t* d0 = s0 + (size_t)row * K;
   int8_t* d1 = s1 + (size_t)row * K;
@@ -322,6 +317,15 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ 
   if (lane == 0) scale[row] = amax / 127.f;
 }
 
+template <typename XT>
+__global__ void __launch_bounds__(256) slice_rows_kernel(const XT* __restrict__ src, int rows, int K,
+                                                         int8_t* __restrict__ s0, int8_t* __restrict__ s1,
+                                                         float* __restrict__ scale) {
+  chain_wait();
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row < rows) slice_row_warp(src, row, K, s0, s1, scale, threadIdx.x & 31);
+}
+
 // ---------------------------------------------------------------------------
 // the GEMM
 // ---------------------------------------------------------------------------
@@ -342,7 +346,8 @@ struct TcArgs {
   const float* xscale_r;     // per-row slice scale of the B rows (routed / all rows in mode 0)
   const float* xscale_s;     // mode 1: shared rows
   float* out_r;              // mode 0: act routed [nk, I]; mode 1: y routed [nk, H]
-  float* out_s;              // mode 0: act shared [n, Is]; mode 1: y shared [n, H]
+  float* out_s;              // mode 0: act shared [n, Is]; mode 1: shared_parts partial y shared [n, H]
+  int shared_parts;          // mode 1: K parts of each shared-expert tile (1: no split)
   Plan* plan_rw;             // error bits
 };
 
@@ -401,7 +406,9 @@ struct TcItem {
   int npad;    // tokens rounded up to 16
   int brow0;   // first B row in the operand matrix
   int slot;    // arena slot of the routed record
-  int units, nkb;
+  int units;
+  int kb0, nkb;  // the item's k-blocks: [kb0, kb0 + nkb)
+  int part;      // mode 1 shared items: which K part (partial output) the item computes
 };
 
 // Copies the schedule `t.sched` of the plan into `pc` (all threads take part;
@@ -454,10 +461,23 @@ __device__ __forceinline__ bool tc_item(const TcArgs& t, const TcPlanCache* pc, 
   const int inter = it.shared ? t.g.Is : t.g.I;
   it.units = MODE == 0 ? inter : t.g.H;
   const int K = MODE == 0 ? t.g.H : inter;
-  it.nkb = (K + 128 * Geo::kKC - 1) / (128 * Geo::kKC);
+  const int blocks = (K + 128 * Geo::kKC - 1) / (128 * Geo::kKC);
   const int ntiles = (it.units + Geo::kUnits - 1) / Geo::kUnits;
-  it.tok0 = (local / ntiles) * TT;
-  it.unit0 = (local % ntiles) * Geo::kUnits;
+  int tile = local;
+  it.kb0 = 0;
+  it.nkb = blocks;
+  it.part = 0;
+  if (MODE == 1 && it.shared && t.shared_parts > 1) {
+    // the K parts of one tile are adjacent items (different CTAs); part p
+    // covers k-blocks [p span, min(blocks, (p + 1) span)), none empty
+    const int span = (blocks + t.shared_parts - 1) / t.shared_parts;
+    tile = local / t.shared_parts;
+    it.part = local % t.shared_parts;
+    it.kb0 = it.part * span;
+    it.nkb = min(blocks - it.kb0, span);
+  }
+  it.tok0 = (tile / ntiles) * TT;
+  it.unit0 = (tile % ntiles) * Geo::kUnits;
   it.nvalid = min(TT, pc->rows[lo] - it.tok0);
   it.npad = (it.nvalid + 15) & ~15;
   if (MODE == 0)
@@ -557,7 +577,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
 #pragma unroll
           for (int c = 0; c < Geo::kKC; ++c) {
             // chunks past K read as zeros (out-of-bounds fill) and add nothing
-            const int x = (kb * Geo::kKC + c) * 128;
+            const int x = ((it.kb0 + kb) * Geo::kKC + c) * 128;
             uint8_t* sa = st + c * Geo::kAChunkBytes;
             uint8_t* sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
             if (MODE == 0) {
@@ -700,7 +720,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       tc_fence_after();
       const uint32_t tbase = tmem_base + ab * kTcAccCols + ((uint32_t)(quad * 32) << 16);
       const int ld_out = MODE == 0 ? (it.shared ? t.g.Is : t.g.I) : t.g.H;
-      float* out_base = it.shared ? t.out_s : t.out_r;
+      float* out_base = it.shared ? t.out_s + (size_t)it.part * t.g.n * t.g.H : t.out_r;
       const int orow0 = (MODE == 0 && it.shared) ? it.tok0 : it.brow0;
 #pragma unroll 1
       for (int ci = 0; ci < Geo::kChunks; ++ci) {
@@ -912,12 +932,9 @@ static int launch_tc_mode(const TcMaps& maps, const TcArgs& t, long long items_b
 // each thread holding kVec float4 of it, so the row is read once; the CTA
 // reduces the row maximum through shared memory.
 template <typename XT, int kVec>
-__global__ void __launch_bounds__(256) slice_long_rows_kernel(const XT* __restrict__ src, int K,
-                                                              int8_t* __restrict__ s0, int8_t* __restrict__ s1,
-                                                              float* __restrict__ scale) {
+__device__ __forceinline__ void slice_row_cta(const XT* __restrict__ src, int row, int K, int8_t* __restrict__ s0,
+                                              int8_t* __restrict__ s1, float* __restrict__ scale) {
   __shared__ float red[8];
-  chain_wait();
-  const int row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const XT* x = src + (size_t)row * K;
   float4 v[kVec];
@@ -949,6 +966,45 @@ __global__ void __launch_bounds__(256) slice_long_rows_kernel(const XT* __restri
     }
   }
   if (tid == 0) scale[row] = amax / 127.f;
+}
+
+template <typename XT, int kVec>
+__global__ void __launch_bounds__(256) slice_long_rows_kernel(const XT* __restrict__ src, int K,
+                                                              int8_t* __restrict__ s0, int8_t* __restrict__ s1,
+                                                              float* __restrict__ scale) {
+  chain_wait();
+  slice_row_cta<XT, kVec>(src, blockIdx.x, K, s0, s1, scale);
+}
+
+// Both row sets of the down step's operand (the routed act rows, K = I, and
+// the shared expert's, K = Is) in one launch: CTAs [0, a_blocks) slice set a,
+// the rest set b; each set one warp per row (K <= 2048) or one CTA per row.
+__device__ __forceinline__ void slice_set(const SliceSet& s, int b) {
+  if (s.K <= 2048) {
+    const int row = b * 8 + (threadIdx.x >> 5);
+    if (row < s.rows) slice_row_warp(s.src, row, s.K, s.s0, s.s1, s.scale, threadIdx.x & 31);
+  } else {
+    slice_row_cta<float, 8>(s.src, b, s.K, s.s0, s.s1, s.scale);
+  }
+}
+
+__global__ void __launch_bounds__(256) slice_sets_kernel(SliceSet a, int a_blocks, SliceSet b) {
+  chain_wait();
+  if ((int)blockIdx.x < a_blocks)
+    slice_set(a, blockIdx.x);
+  else
+    slice_set(b, blockIdx.x - a_blocks);
+}
+
+static int slice_set_blocks(const SliceSet& s) { return s.rows <= 0 ? 0 : (s.K <= 2048 ? (s.rows + 7) / 8 : s.rows); }
+
+int launch_slice_sets(const SliceSet& a, const SliceSet& b, cudaStream_t st) {
+  for (const SliceSet* s : {&a, &b})
+    if (s->rows > 0 && (s->K <= 0 || s->K % 4 || s->K > 8192))
+      return fail(ER_EINVAL, "slice: row length %d (a multiple of 4 up to 8192)", s->K);
+  const int ab = slice_set_blocks(a), bb = slice_set_blocks(b);
+  if (ab + bb == 0) return ER_OK;
+  return launch_chained(slice_sets_kernel, dim3(ab + bb), dim3(256), 0, st, "slice_sets_kernel", a, ab, b);
 }
 
 int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, int8_t* s1, float* scale,
@@ -1026,6 +1082,7 @@ int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
   t.xscale_s = L.xscale_s;
   t.out_r = L.out_r;
   t.out_s = L.out_s;
+  t.shared_parts = L.mode == 1 && L.shared_parts > 1 ? L.shared_parts : 1;
   t.plan_rw = const_cast<Plan*>(a.plan);
   // 16-token tiles on single SMs, 128-token tiles on SM pairs (tc_cta_group)
   if (L.mode == 0)
