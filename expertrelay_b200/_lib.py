@@ -141,6 +141,8 @@ SIGNATURES: dict[str, tuple] = {
     "er_cache_resize": (_i, [_vp, _i, _vp, C.POINTER(_i)]),
     "er_cache_lookup": (_i, [_vp, _i, _i, C.POINTER(_i), C.POINTER(_i)]),
     "er_cache_stats_get": (_i, [_vp, C.POINTER(CacheStats)]),
+    "er_trace_record_bytes": (C.c_size_t, [_i, _i]),
+    "er_trace_pack_layer": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _vp]),
 }
 
 _lib: C.CDLL | None = None

@@ -36,6 +36,7 @@ class PagedMoeStack:
         norm_topk_prob: bool = False,
     ):
         self.cache = cache
+        self.norm_topk_prob = norm_topk_prob
         self.prefetcher = prefetcher
         self.prefetch_enabled = prefetcher is not None
         self.layers = [
@@ -48,16 +49,22 @@ class PagedMoeStack:
         self.top_k = self.layers[0].top_k
         self.prefetches_skipped_low_confidence = 0
 
-    def moe(self, layer: int, h: torch.Tensor, path: int = _lib.PATH_AUTO) -> torch.Tensor:
-        """One layer's MoE block output for h [n, H] (the layer's QwenMoe._moe)."""
+    def moe(self, layer: int, h: torch.Tensor, path: int = _lib.PATH_AUTO, *, trace=None,
+            return_routing: bool = False):
+        """One layer's MoE block output for h [n, H] (the layer's QwenMoe._moe).
+        `trace`: an ExpertTraceWriter between begin() and end(); this layer's
+        router logits, choices, weights and the Fate logits for the next
+        layer go to it (qwen_moe.py:311-338). return_routing: also the
+        [n, k] int64 expert ids."""
         blk = self.layers[layer]
         cache = self.cache
         n = h.shape[0]
         logits = blk.router_logits(h)
         idx = torch.empty((n, self.top_k), dtype=torch.int64, device=h.device)
+        wts = torch.empty((n, self.top_k), dtype=torch.float32, device=h.device)
         stream = torch.cuda.current_stream(h.device).cuda_stream
         rc = _lib.lib().er_router_topk(logits.data_ptr(), n, self.num_experts, self.top_k, idx.data_ptr(), None,
-                                       None, stream)
+                                       wts.data_ptr(), stream)
         _lib.check(rc, "er_router_topk")
         needed = np.unique(idx.cpu().numpy())  # the host decides which records to fetch
         addrs = cache.acquire(layer, needed)
@@ -65,18 +72,27 @@ class PagedMoeStack:
         table[needed] = addrs
         blk.use_arena(cache.arena_base, cache.num_slots)
         blk.set_expert_table(torch.from_numpy(table.view(np.int64)))
-        if self.prefetch_enabled and layer + 1 < len(self.layers):
-            fate = self.layers[layer + 1].router_logits(h).cpu().numpy()
-            choice = self.prefetcher.choose(fate)
+        has_next = layer + 1 < len(self.layers)
+        fate = None
+        if (self.prefetch_enabled or trace is not None) and has_next:
+            # the next layer's router on this layer's input (the Fate guess)
+            fate = self.layers[layer + 1].router_logits(h)
+        if self.prefetch_enabled and has_next:
+            choice = self.prefetcher.choose(fate.cpu().numpy())
             self.prefetches_skipped_low_confidence += choice.skipped_low_confidence
             cache.prefetch(layer + 1, choice.experts, keep=[(layer, int(e)) for e in needed])
+        if trace is not None:
+            if self.norm_topk_prob:  # the block's weights, renormalised as it uses them
+                wts = wts / wts.sum(dim=-1, keepdim=True)
+            trace.layer(layer, logits, idx, wts, fate)
         y = blk.forward(h, logits=logits, path=path)
         cache.end_layer(layer)
-        return y
+        return (y, idx) if return_routing else y
 
-    def forward(self, h: torch.Tensor, path: int = _lib.PATH_AUTO) -> torch.Tensor:
+    def forward(self, h: torch.Tensor, path: int = _lib.PATH_AUTO, *, trace=None) -> torch.Tensor:
         """All layers in order, each adding its MoE output to the residual
-        stream: h <- h + moe_l(h)."""
+        stream: h <- h + moe_l(h). `trace`: a writer between begin() and
+        end() (the caller's, who knows the tokens' positions and ids)."""
         for layer in range(len(self.layers)):
-            h = h + self.moe(layer, h, path)
+            h = h + self.moe(layer, h, path, trace=trace)
         return h

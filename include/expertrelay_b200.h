@@ -24,6 +24,7 @@
  *   er_record_*        store/layout.py:53-115, store/int4.py:165-244
  *                                                         expert record layouts
  *   er_cache_*         cache/expert_cache.py:92-402       CachedExpertSource (HBM slots)
+ *   er_trace_*         runtime/expert_trace.py:34-135     ExpertTraceWriter records
  */
 #ifndef EXPERTRELAY_B200_H
 #define EXPERTRELAY_B200_H
@@ -284,6 +285,24 @@ ER_API int er_cache_resize(er_cache* c, int slots, void* new_arena, int* slots_o
 /* slot and ER_SLOT_* state of a key (slot -1 when absent); polls its copy */
 ER_API int er_cache_lookup(er_cache* c, int layer, int expert, int* slot, int* state);
 ER_API int er_cache_stats_get(er_cache* c, er_cache_stats* out);
+
+/* ---- expert-usage trace (runtime/expert_trace.py) ----
+ * Record bytes of one (token, layer) record (record_dtype, expert_trace.py:
+ * 34-65: 10 + 7 top_k + 4 num_experts); 0 when num_experts >= 255 (u8 ids)
+ * or top_k is outside 1..8. */
+ER_API size_t er_trace_record_bytes(int num_experts, int top_k);
+/* One layer's records of a forward call (ExpertTraceWriter.layer,
+ * expert_trace.py:114-135), written on the device into `records` (the call's
+ * n * num_layers records, token major): positions / tokens [n] u32, logits
+ * [n, E] f32 (stored f16), experts [n, k] int64 (experts_are_i64) or int32,
+ * weights [n, k] f32, fate_logits [n, E] f32 or NULL (the Fate logits given
+ * with the previous layer: stored f16 and their top-k; NULL: NO_EXPERT and
+ * zeros). prev_in / prev_out: [num_layers, k] u8 previous-token experts
+ * before and after this call (distinct buffers unless n == 1). */
+ER_API int er_trace_pack_layer(void* records, int n, int num_layers, int layer, const uint32_t* positions,
+                               const uint32_t* tokens, int phase, const float* logits, const void* experts,
+                               int experts_are_i64, const float* weights, const float* fate_logits,
+                               const uint8_t* prev_in, uint8_t* prev_out, int num_experts, int top_k, void* stream);
 
 #ifdef __cplusplus
 }

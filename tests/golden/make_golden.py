@@ -264,13 +264,69 @@ def full_fixtures() -> dict:
     return out
 
 
+# (num_layers, num_experts, top_k, prefill tokens) of the trace fixtures
+TRACE_CASES = ((3, 8, 2, 5), (2, 60, 4, 3))
+
+
+def trace_inputs(case: int) -> list[dict]:
+    """Seeded writer calls for trace case `case`: a prefill call, then two
+    one-token decode calls. Logits hold values that float16 rounds to
+    infinity, to subnormals and to zero, and a tie inside the top-k."""
+    layers, experts, k, n0 = TRACE_CASES[case]
+    rng = np.random.default_rng(100 + case)
+    calls, pos = [], 0
+    for n, phase in ((n0, 0), (1, 1), (1, 1)):
+        call = {"positions": np.arange(pos, pos + n, dtype=np.int64),
+                "tokens": rng.integers(0, 151936, n).astype(np.int64), "phase": phase, "layers": []}
+        pos += n
+        for layer in range(layers):
+            logits = rng.normal(0, 3, (n, experts)).astype(np.float32)
+            logits[0, 0] = 70000.0  # float16 overflow
+            logits[0, 1] = 3e-6     # float16 subnormal
+            logits[-1, 2] = -1e-9   # rounds to -0
+            sel = np.argsort(-logits, axis=1, kind="stable")[:, :k].astype(np.int64)
+            p = np.exp(logits - logits.max(axis=1, keepdims=True))
+            p /= p.sum(axis=1, keepdims=True)
+            weights = np.take_along_axis(p, sel, axis=1).astype(np.float32)
+            fate = None
+            if layer + 1 < layers:
+                fate = rng.normal(0, 2, (n, experts)).astype(np.float32)
+                fate[0, 3] = fate[0, 5] = fate[0].max() + 1.0  # an exact tie at the top (lower id first)
+            call["layers"].append({"logits": logits, "selected": sel, "weights": weights, "fate": fate})
+        calls.append(call)
+    return calls
+
+
+def trace_fixtures(tmp: Path) -> dict:
+    """The reference ExpertTraceWriter's file for each trace case."""
+    from expertrelay.runtime.expert_trace import ExpertTraceWriter
+
+    out = {}
+    for case, (layers, experts, k, _) in enumerate(TRACE_CASES):
+        path = tmp / f"trace{case}.ert"
+        w = ExpertTraceWriter(path, num_layers=layers, num_experts=experts, top_k=k,
+                              metadata={"prompt_id": f"case{case}", "model": "synthetic"})
+        for call in trace_inputs(case):
+            w.begin(call["positions"], call["tokens"], call["phase"])
+            for layer, lc in enumerate(call["layers"]):
+                w.layer(layer, lc["logits"], lc["selected"], lc["weights"], lc["fate"])
+            w.end()
+        out[f"file{case}"] = np.frombuffer(path.read_bytes(), dtype=np.uint8)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--skip-full", action="store_true")
+    ap.add_argument("--only", choices=("trace",), help="regenerate one fixture file only")
     args = ap.parse_args()
     ref = Path(args.reference)
     _import_reference(ref)
+    with tempfile.TemporaryDirectory() as tmp:
+        np.savez_compressed(HERE / "trace.npz", **trace_fixtures(Path(tmp)))
+    if args.only == "trace":
+        return
     np.savez_compressed(HERE / "quant.npz", **quantizer_fixtures())
     np.savez_compressed(HERE / "gptq.npz", **gptq_fixtures())
     np.savez_compressed(HERE / "linear.npz", **linear_fixtures())
