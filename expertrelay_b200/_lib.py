@@ -14,7 +14,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).with_name("libexpertrelay_b200.so")
 
-ER_OK, ER_EINVAL, ER_ECUDA, ER_ETIMEOUT, ER_ENOSPACE = 0, 1, 2, 3, 4
+ER_OK, ER_EINVAL, ER_ECUDA, ER_ETIMEOUT, ER_ENOSPACE, ER_EIO = 0, 1, 2, 3, 4, 5
 DTYPE_F32, DTYPE_BF16 = 0, 1
 FMT_INT8, FMT_INT4, FMT_INT4_ZP = 0, 1, 2
 PATH_AUTO, PATH_GEMV, PATH_GEMM, PATH_TC = 0, 1, 2, 3
@@ -142,6 +142,11 @@ SIGNATURES: dict[str, tuple] = {
     "er_cache_lookup": (_i, [_vp, _i, _i, C.POINTER(_i), C.POINTER(_i)]),
     "er_cache_stats_get": (_i, [_vp, C.POINTER(CacheStats)]),
     "er_trace_record_bytes": (C.c_size_t, [_i, _i]),
+    "er_store_open": (_i, [C.c_char_p, _i, C.POINTER(_vp)]),
+    "er_store_close": (_i, [_vp]),
+    "er_store_info": (_i, [_vp, C.POINTER(C.c_uint64), C.POINTER(_i)]),
+    "er_store_read": (_i, [_vp, C.c_uint64, C.c_uint64, _vp]),
+    "er_store_read_many": (_i, [_vp, _i, _vp, C.c_uint64, _vp, _i]),
     "er_trace_pack_layer": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _vp]),
 }
 
@@ -170,10 +175,13 @@ def last_error() -> str:
 
 def check(rc: int, what: str) -> None:
     """Raise for a nonzero status: ValueError for bad arguments or too little
-    workspace, RuntimeError for CUDA errors and device-side timeouts."""
+    workspace, OSError for failed or short file reads, RuntimeError for CUDA
+    errors and device-side timeouts."""
     if rc == ER_OK:
         return
     msg = f"{what}: {last_error()}"
     if rc in (ER_EINVAL, ER_ENOSPACE):
         raise ValueError(msg)
+    if rc == ER_EIO:
+        raise OSError(msg)
     raise RuntimeError(msg)

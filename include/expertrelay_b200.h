@@ -25,6 +25,8 @@
  *                                                         expert record layouts
  *   er_cache_*         cache/expert_cache.py:92-402       CachedExpertSource (HBM slots)
  *   er_trace_*         runtime/expert_trace.py:34-135     ExpertTraceWriter records
+ *   er_store_*         store/unbuffered_io.py:135-149,    one aligned read per expert record
+ *                      store/expert_reader.py:92-101      (ExpertStoreReader.read_into)
  */
 #ifndef EXPERTRELAY_B200_H
 #define EXPERTRELAY_B200_H
@@ -48,6 +50,7 @@ extern "C" {
 #define ER_ECUDA 2     /* a CUDA runtime call or launch failed */
 #define ER_ETIMEOUT 3  /* a bounded device-side wait gave up */
 #define ER_ENOSPACE 4  /* workspace (or fixed scratch) too small */
+#define ER_EIO 5       /* a file read failed or came up short */
 
 /* ---- activation dtypes ------------------------------------------------- */
 #define ER_DTYPE_F32 0
@@ -303,6 +306,22 @@ ER_API int er_trace_pack_layer(void* records, int n, int num_layers, int layer, 
                                const uint32_t* tokens, int phase, const float* logits, const void* experts,
                                int experts_are_i64, const float* weights, const float* fate_logits,
                                const uint8_t* prev_in, uint8_t* prev_out, int num_experts, int top_k, void* stream);
+
+/* ---- expert store reads (store/unbuffered_io.py, store/expert_reader.py) ----
+ * experts.bin opened for reads that bypass the page cache (O_DIRECT; with
+ * ER_STORE_BUFFERED, or on a filesystem without O_DIRECT, plain reads). A
+ * read is offset / size / destination all multiples of 4096 (ER_EINVAL
+ * otherwise, "unaligned unbuffered read" as the reference), into HOST memory
+ * (normally pinned), and fails with ER_EIO on an I/O error or a short read. */
+typedef struct er_store er_store;
+#define ER_STORE_BUFFERED 1
+ER_API int er_store_open(const char* path, int flags, er_store** out);
+ER_API int er_store_close(er_store* s);
+ER_API int er_store_info(const er_store* s, uint64_t* file_bytes, int* direct);
+ER_API int er_store_read(er_store* s, uint64_t offset, uint64_t nbytes, void* dst);
+/* count reads of nbytes each (offsets[i] -> dsts[i]) on up to `threads` threads */
+ER_API int er_store_read_many(er_store* s, int count, const uint64_t* offsets, uint64_t nbytes, void* const* dsts,
+                              int threads);
 
 #ifdef __cplusplus
 }

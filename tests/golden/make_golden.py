@@ -315,17 +315,55 @@ def trace_fixtures(tmp: Path) -> dict:
     return out
 
 
+STORE_SHAPE = {"hidden_size": 64, "moe_intermediate_size": 32, "num_layers": 2, "num_experts": 3}
+
+
+def store_fixture(out_dir: Path) -> None:
+    """A tiny int8 expert store (experts.bin + experts_index.json) written
+    with the reference's record and index writers (store/layout.py:117-133,
+    179-188) at the offsets its builder uses (expert_offset, :152-153)."""
+    from expertrelay.store.layout import (
+        ExpertIndexEntry,
+        ExpertRecordLayout,
+        expert_offset,
+        serialize_expert_record,
+        write_expert_index,
+    )
+    from expertrelay.store.quantize import quantize_rowwise_int8
+
+    cfg = STORE_SHAPE
+    layout = ExpertRecordLayout.from_config(cfg)
+    rng = np.random.default_rng(42)
+    out_dir.mkdir(parents=True, exist_ok=True)
+    entries, blob = [], bytearray()
+    for layer in range(cfg["num_layers"]):
+        for expert in range(cfg["num_experts"]):
+            quantized = {m: quantize_rowwise_int8(rng.normal(0, 0.02, s).astype(np.float32)) for m, s in layout.matrices}
+            record = serialize_expert_record(layout, quantized)
+            offset = expert_offset(layer, expert, cfg["num_experts"], layout.record_size)
+            blob[len(blob):offset + layout.record_size] = bytes(offset + layout.record_size - len(blob))
+            blob[offset:offset + layout.record_size] = record
+            entries.append(ExpertIndexEntry(layer=layer, expert=expert, offset=offset, size=layout.record_size,
+                                            shapes={m: list(sh) for m, sh in layout.matrices},
+                                            sha256=hashlib.sha256(record).hexdigest(), quant_error={}))
+    (out_dir / "experts.bin").write_bytes(bytes(blob))
+    write_expert_index(out_dir / "experts_index.json", layout, entries)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--skip-full", action="store_true")
-    ap.add_argument("--only", choices=("trace",), help="regenerate one fixture file only")
+    ap.add_argument("--only", choices=("trace", "store"), help="regenerate one fixture only")
     args = ap.parse_args()
     ref = Path(args.reference)
     _import_reference(ref)
-    with tempfile.TemporaryDirectory() as tmp:
-        np.savez_compressed(HERE / "trace.npz", **trace_fixtures(Path(tmp)))
-    if args.only == "trace":
+    if args.only in (None, "trace"):
+        with tempfile.TemporaryDirectory() as tmp:
+            np.savez_compressed(HERE / "trace.npz", **trace_fixtures(Path(tmp)))
+    if args.only in (None, "store"):
+        store_fixture(HERE / "store_small")
+    if args.only is not None:
         return
     np.savez_compressed(HERE / "quant.npz", **quantizer_fixtures())
     np.savez_compressed(HERE / "gptq.npz", **gptq_fixtures())
