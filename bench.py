@@ -53,6 +53,11 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-shape side measurement")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample budget")
+    ap.add_argument("--no-full-model", action="store_true", help="skip the whole-model decode measurement")
+    ap.add_argument("--model-layers", type=int, default=24, help="decoder layers of the whole-model measurement")
+    ap.add_argument("--prompt-tokens", type=int, default=512)
+    ap.add_argument("--new-tokens", type=int, default=128)
+    ap.add_argument("--cache-frac", type=float, default=0.25, help="HBM expert-cache share of the routed records")
     return ap.parse_args()
 
 
@@ -494,11 +499,57 @@ def main() -> None:
         line["decode"] = decode_side(args, dev, mb, block, peaks, peak_src)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(block, x, args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_full_model:
+        del mb
+        torch.cuda.empty_cache()
+        line["full_model"] = full_model_side(args, dev)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def full_model_side(args, dev) -> dict:
+    """Whole-model greedy decoding (Qwen1.5-MoE-A2.7B shapes, random init):
+    a seeded uniform prompt in one call, then one token per call; routed
+    experts paged through an HBM cache of cache_frac of the records from
+    pinned host memory, with the Fate prefetch. Decode tokens/s counts the
+    one-token calls (each a full forward: embedding, 24 layers, lm_head)."""
+    from expertrelay_b200.model import QwenMoeModel
+
+    cfg = dict(synth.QWEN_MODEL, num_hidden_layers=args.model_layers)
+    t0 = time.perf_counter()
+    host, records = synth.make_model_gpu(cfg, seed=args.seed + 17, device=dev)
+    t_build = time.perf_counter() - t0
+    n_records = records.shape[0] * records.shape[1]
+    slots = max(cfg["num_experts"] + 1, int(round(args.cache_frac * n_records)))
+    model = QwenMoeModel(host, records=records, cache_records=slots, prefetch=True, device=dev)
+    prompt = np.random.default_rng(args.seed + 4242).integers(0, cfg["vocab_size"], args.prompt_tokens)
+    model.generate(prompt[:16], 4)  # warm-up: kernels, allocator, cache bookkeeping
+    s0 = model.cache.stats
+    tokens, t_prompt, steps = model.generate(prompt, args.new_tokens)
+    s1 = model.cache.stats
+    rs = model.records.layout.record_size
+    dec_s = float(np.sum(steps))
+    delta = {k: getattr(s1, k) - getattr(s0, k) for k in ("loads", "demand_reads", "cache_hits", "prefetch_hits",
+                                                           "prefetch_waits", "prefetches_issued", "prefetch_reads",
+                                                           "prefetches_wasted")}
+    model.close()
+    return {
+        "workload": (f"Qwen1.5-MoE-A2.7B shapes, random init, {cfg['num_hidden_layers']} layers, int8 experts; "
+                     f"{args.prompt_tokens}-token seeded uniform prompt, {args.new_tokens} greedy tokens, batch 1; "
+                     f"HBM expert cache {slots} of {n_records} records, the rest in pinned host RAM, Fate prefetch"),
+        "decode_tokens_per_s": (len(steps) / dec_s) if steps else None,
+        "ms_per_decode_token": dec_s / max(len(steps), 1) * 1e3,
+        "decode_ms_p50": float(np.median(steps)) * 1e3 if steps else None,
+        "prompt_ms": t_prompt * 1e3,
+        "prompt_tokens_per_s": args.prompt_tokens / t_prompt,
+        "expert_bytes_copied_GB": (delta["demand_reads"] + delta["prefetch_reads"]) * rs / 1e9,
+        "cache": delta,
+        "build_s": t_build,
+        "timing": "host wall clock around each generate() call (synchronous: argmax read back per token)",
+    }
 
 
 def decode_side(args, dev, mb, block, peaks, peak_src) -> dict:

@@ -108,6 +108,65 @@ static int launch_linear(const float* x, long long ldx, const void* w, const flo
   return launch_check("linear_tiled_kernel");
 }
 
+// ---------------------------------------------------------------------------
+// int8 weight streaming for a few rows (decode): y[m, out] = (x @ Q^T) * s (+ b)
+// One warp per output row; each lane reads 16 codes per step (one 16-byte
+// load, not kept in L1), every row of x (m <= MT) from L1, and the warp sums
+// its lanes at the end. The weights cross HBM once; x stays cached.
+// ---------------------------------------------------------------------------
+template <int MT>
+__global__ void __launch_bounds__(256) int8_gemv_kernel(const float* __restrict__ x, long long ldx,
+                                                        const int8_t* __restrict__ q, const float* __restrict__ s,
+                                                        const float* __restrict__ bias, float* __restrict__ y,
+                                                        int m, int out, int in) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= out) return;
+  const int8_t* qr = q + (size_t)row * in;
+  float acc[MT];
+#pragma unroll
+  for (int i = 0; i < MT; ++i) acc[i] = 0.f;
+  for (int c = lane * 16; c < in; c += 32 * 16) {
+    const uint4 raw = ld_stream_u4(qr + c);
+    const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+    float w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = (float)b[j];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+      if (i < m) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)i * ldx + c);
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+          const float4 xv = __ldg(xr + j4);
+          acc[i] = fmaf(w[4 * j4], xv.x, acc[i]);
+          acc[i] = fmaf(w[4 * j4 + 1], xv.y, acc[i]);
+          acc[i] = fmaf(w[4 * j4 + 2], xv.z, acc[i]);
+          acc[i] = fmaf(w[4 * j4 + 3], xv.w, acc[i]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MT; ++i) acc[i] = warp_sum(acc[i]);
+  if (lane == 0) {
+    const float sc = s[row], bv = bias ? bias[row] : 0.f;
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+      if (i < m) y[(size_t)i * out + row] = bias ? acc[i] * sc + bv : acc[i] * sc;
+  }
+}
+
+static int launch_int8_gemv(const float* x, long long ldx, const int8_t* q, const float* s, const float* bias,
+                            float* y, int m, int out, int in, cudaStream_t st) {
+  const dim3 grid((out + 7) / 8), block(256);
+  if (m <= 1) int8_gemv_kernel<1><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+  else if (m <= 2) int8_gemv_kernel<2><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+  else if (m <= 4) int8_gemv_kernel<4><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+  else int8_gemv_kernel<8><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+  return launch_check("int8_gemv_kernel");
+}
+
 static int check_linear_args(const char* name, const float* x, long long ldx, const void* w, float* y, int m, int out,
                              int in) {
   if (m < 0 || out < 0 || in < 0) return fail(ER_EINVAL, "%s: negative size", name);
@@ -234,6 +293,9 @@ int er_int8_linear(const float* x, long long ldx, const int8_t* q, const float* 
                    int m, int out, int in, void* stream) {
   if (int rc = check_linear_args("er_int8_linear", x, ldx, q, y, m, out, in)) return rc;
   if (out > 0 && !scales) return fail(ER_EINVAL, "er_int8_linear: null scales");
+  // a few rows, aligned rows of 16-byte multiples: stream the weights once
+  if (m > 0 && m <= 8 && out > 0 && in % 16 == 0 && ldx % 4 == 0 && !(((uintptr_t)x | (uintptr_t)q) & 15))
+    return launch_int8_gemv(x, ldx, q, scales, bias, y, m, out, in, (cudaStream_t)stream);
   return launch_linear<1>(x, ldx, q, scales, nullptr, nullptr, 1, bias, y, m, out, in, (cudaStream_t)stream);
 }
 

@@ -187,3 +187,156 @@ def make_workload(name: str, seed: int = 0, **overrides) -> tuple[HostBlock, np.
     if spec["zipf"]:
         apply_zipf_routing(block, x, spec["zipf"], seed)
     return block, x
+
+
+# ---------------------------------------------------------------------------
+# the whole decoder (runtime/qwen_moe.py:376-432)
+# ---------------------------------------------------------------------------
+
+# Qwen1.5-MoE-A2.7B's config.json fields the forward pass reads
+QWEN_MODEL = {
+    "vocab_size": 151936,
+    "hidden_size": 2048,
+    "num_hidden_layers": 24,
+    "num_attention_heads": 16,
+    "num_key_value_heads": 16,
+    "num_experts": 60,
+    "num_experts_per_tok": 4,
+    "moe_intermediate_size": 1408,
+    "shared_expert_intermediate_size": 5632,
+    "norm_topk_prob": False,
+    "rms_norm_eps": 1e-6,
+    "rope_theta": 1e6,
+}
+
+
+@dataclass
+class HostLayer:
+    """A decoder layer's non-MoE weights: int8 (q, scales) projections, fp32
+    q/k/v biases and RMSNorm weights."""
+
+    input_norm: np.ndarray
+    post_norm: np.ndarray
+    proj: dict  # "q_proj" | "k_proj" | "v_proj" | "o_proj" -> (int8 q, float32 scales)
+    bias: dict  # "q_proj" | "k_proj" | "v_proj" -> float32
+
+
+@dataclass
+class HostModel:
+    """A whole Qwen2-MoE decoder on the host: config (config.json fields),
+    embedding and lm_head as int8 rows, final norm, per-layer weights and
+    MoE blocks (routed records included)."""
+
+    config: dict
+    embed: tuple
+    lm_head: tuple
+    final_norm: np.ndarray
+    layers: list
+    blocks: list
+
+    def tensors(self) -> dict:
+        """Checkpoint-named tensors, as the reference's ResidentWeights holds
+        them: (q, scales) for int8 matrices, arrays for fp32 ones."""
+        out = {"model.embed_tokens.weight": self.embed, "lm_head.weight": self.lm_head,
+               "model.norm.weight": self.final_norm}
+        for i, (lay, blk) in enumerate(zip(self.layers, self.blocks)):
+            p = f"model.layers.{i}."
+            out[p + "input_layernorm.weight"] = lay.input_norm
+            out[p + "post_attention_layernorm.weight"] = lay.post_norm
+            for m, qs in lay.proj.items():
+                out[p + f"self_attn.{m}.weight"] = qs
+            for m, b in lay.bias.items():
+                out[p + f"self_attn.{m}.bias"] = b
+            out[p + "mlp.gate.weight"] = blk.router
+            out[p + "mlp.shared_expert_gate.weight"] = blk.shared_gate
+            for m, qs in blk.shared.items():
+                out[p + f"mlp.shared_expert.{m}.weight"] = qs
+        return out
+
+
+def make_model(config: dict | None = None, seed: int = 0, sigma: float = 0.02) -> HostModel:
+    """Seeded random-init decoder (numpy; for models small enough to build on
+    the host): projections ~ N(0, sigma) then int8 per row, biases ~ N(0,
+    sigma), norm weights 1 + N(0, 0.1), embedding and lm_head rows ~ N(0, 1)
+    and N(0, sigma) then int8, MoE blocks from make_block(seed * 1000 + layer)."""
+    c = dict(QWEN_MODEL if config is None else config)
+    H, V, L = c["hidden_size"], c["vocab_size"], c["num_hidden_layers"]
+    heads, kvh = c["num_attention_heads"], c["num_key_value_heads"]
+    d = H // heads
+    rng = np.random.default_rng(seed)
+    embed = quant.int8_rowwise(_normal(rng, (V, H), 1.0))
+    lm_head = quant.int8_rowwise(_normal(rng, (V, H), sigma))
+    final_norm = (1.0 + _normal(rng, (H,), 0.1)).astype(np.float32)
+    layers, blocks = [], []
+    for i in range(L):
+        lr = np.random.default_rng([seed, 1, i])
+        shapes = {"q_proj": (heads * d, H), "k_proj": (kvh * d, H), "v_proj": (kvh * d, H), "o_proj": (H, heads * d)}
+        proj = {m: quant.int8_rowwise(_normal(lr, s, sigma)) for m, s in shapes.items()}
+        bias = {m: _normal(lr, (shapes[m][0],), sigma) for m in ("q_proj", "k_proj", "v_proj")}
+        layers.append(HostLayer((1.0 + _normal(lr, (H,), 0.1)).astype(np.float32),
+                                (1.0 + _normal(lr, (H,), 0.1)).astype(np.float32), proj, bias))
+        blocks.append(make_block(seed * 1000 + i, hidden=H, inter=c["moe_intermediate_size"],
+                                 shared_inter=c["shared_expert_intermediate_size"], num_experts=c["num_experts"],
+                                 top_k=c["num_experts_per_tok"], sigma=sigma))
+    return HostModel(c, embed, lm_head, final_norm, layers, blocks)
+
+
+def make_model_gpu(config: dict | None = None, seed: int = 0, sigma: float = 0.02, device="cuda"):
+    """The same kind of random-init decoder at full size, generated on the
+    GPU (torch's seeded generator) and quantized there, so a 24-layer model's
+    12.5 GB of routed-expert records take seconds rather than the minutes
+    numpy would: returns (HostModel whose blocks carry no routed records,
+    pinned [layers, experts, record_size] uint8 records). Not bit-equal to
+    make_model's weights (another generator)."""
+    import torch
+
+    c = dict(QWEN_MODEL if config is None else config)
+    H, V, L = c["hidden_size"], c["vocab_size"], c["num_hidden_layers"]
+    heads, kvh = c["num_attention_heads"], c["num_key_value_heads"]
+    E, I, Is, k = c["num_experts"], c["moe_intermediate_size"], c["shared_expert_intermediate_size"], c["num_experts_per_tok"]
+    d = H // heads
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+
+    def normal(shape, s):
+        return torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * s
+
+    def q8(w):  # per-row int8, as quant.int8_rowwise
+        sc = w.abs().amax(dim=-1) / 127.0
+        sc = torch.where(sc > 0, sc, torch.ones_like(sc))
+        q = torch.clamp(torch.round(w / sc.unsqueeze(-1)), -127, 127).to(torch.int8)
+        return q, sc
+
+    def host(qs):
+        return qs[0].cpu().numpy(), qs[1].cpu().numpy()
+
+    embed = host(q8(normal((V, H), 1.0)))
+    lm_head = host(q8(normal((V, H), sigma)))
+    final_norm = (1.0 + normal((H,), 0.1)).cpu().numpy()
+    layout = RecordLayout(FMT_INT8, H, I)
+    rs = layout.record_size
+    records = torch.empty((L, E, rs), dtype=torch.uint8, pin_memory=True)
+    layers, blocks = [], []
+    for i in range(L):
+        shapes = {"q_proj": (heads * d, H), "k_proj": (kvh * d, H), "v_proj": (kvh * d, H), "o_proj": (H, heads * d)}
+        proj = {m: host(q8(normal(s, sigma))) for m, s in shapes.items()}
+        bias = {m: normal((shapes[m][0],), sigma).cpu().numpy() for m in ("q_proj", "k_proj", "v_proj")}
+        layers.append(HostLayer((1.0 + normal((H,), 0.1)).cpu().numpy(), (1.0 + normal((H,), 0.1)).cpu().numpy(),
+                                proj, bias))
+        router = normal((E, H), sigma).cpu().numpy()
+        shared_gate = normal((1, H), sigma).cpu().numpy()
+        sh_shapes = {"gate_proj": (Is, H), "up_proj": (Is, H), "down_proj": (H, Is)}
+        shared = {m: host(q8(normal(s, sigma))) for m, s in sh_shapes.items()}
+        # the layer's routed records, laid out on the GPU, then into pinned memory
+        rec = torch.zeros((E, rs), dtype=torch.uint8, device=dev)
+        mats = {m: q8(normal((E, *layout.shape(m)), sigma)) for m in ("gate_proj", "up_proj", "down_proj")}
+        for m, (q, sc) in mats.items():
+            wo, so = layout.weight_offset(m), layout.scale_offset(m)
+            rec[:, wo : wo + q[0].numel()] = q.reshape(E, -1).view(torch.uint8)
+            rec[:, so : so + sc.shape[1] * 4] = sc.contiguous().view(torch.uint8).reshape(E, -1)
+        records[i].copy_(rec)
+        del rec, mats
+        blocks.append(HostBlock(H, I, Is, E, k, "int8", 0, router, shared_gate, shared, [], None,
+                                {"seed": seed, "sigma": sigma, "generator": "torch.cuda"}))
+    return HostModel(c, embed, lm_head, final_norm, layers, blocks), records

@@ -25,6 +25,9 @@
  *                                                         expert record layouts
  *   er_cache_*         cache/expert_cache.py:92-402       CachedExpertSource (HBM slots)
  *   er_trace_*         runtime/expert_trace.py:34-135     ExpertTraceWriter records
+ *   er_rms_norm, er_rope_kv, er_embed_int8
+ *                      runtime/qwen_moe.py:121-138, 250-270, weights.py:62-64
+ *                                                         decoder-layer norm, RoPE + KV cache, embedding
  *   er_store_*         store/unbuffered_io.py:135-149,    one aligned read per expert record
  *                      store/expert_reader.py:92-101      (ExpertStoreReader.read_into)
  */
@@ -306,6 +309,24 @@ ER_API int er_trace_pack_layer(void* records, int n, int num_layers, int layer, 
                                const uint32_t* tokens, int phase, const float* logits, const void* experts,
                                int experts_are_i64, const float* weights, const float* fate_logits,
                                const uint8_t* prev_in, uint8_t* prev_out, int num_experts, int top_k, void* stream);
+
+/* ---- the decoder layer's other parts (runtime/qwen_moe.py) ----
+ * x_out = x + add (when add is not NULL; x_out may be x), h = weight * x_out /
+ * sqrt(mean(x_out^2) + eps) per row of `hidden` fp32 values (rms_norm, :121-123,
+ * with the residual add before it fused). */
+ER_API int er_rms_norm(const float* x, const float* add, const float* weight, float eps, int n, int hidden,
+                       float* x_out, float* h, void* stream);
+/* RoPE (rope_tables and the rotation, :126-138, 255-256; inv_freq = 1 /
+ * theta^(2i/d)) on q [n, heads, d] in place and on k [n, kv_heads, d], for
+ * positions pos0 .. pos0 + n - 1; the rotated k and v [n, kv_heads, d] go to
+ * rows pos0.. of the layer's caches [max_seq, kv_heads, d] (:264-270;
+ * ER_EINVAL when pos0 + n > max_seq, like the reference's ValueError). */
+ER_API int er_rope_kv(float* q, const float* k, const float* v, int n, int heads, int kv_heads, int head_dim,
+                      int pos0, float theta, float* k_cache, float* v_cache, int max_seq, void* stream);
+/* out[t] = q[ids[t]] * scales[ids[t]] (Int8Matrix.dequantized_rows,
+ * runtime/weights.py:62-64); an id outside [0, vocab) sets *bad and a NaN row */
+ER_API int er_embed_int8(const int8_t* q, const float* scales, long long vocab, int hidden, const int64_t* ids, int n,
+                         float* out, int* bad, void* stream);
 
 /* ---- expert store reads (store/unbuffered_io.py, store/expert_reader.py) ----
  * experts.bin opened for reads that bypass the page cache (O_DIRECT; with

@@ -315,6 +315,67 @@ def trace_fixtures(tmp: Path) -> dict:
     return out
 
 
+# a small Qwen2-MoE decoder for the whole-model fixtures (the reference's
+# QwenMoe.forward on it, numpy backend)
+TINY_MODEL = {
+    "vocab_size": 96,
+    "hidden_size": 256,
+    "num_hidden_layers": 3,
+    "num_attention_heads": 4,
+    "num_key_value_heads": 4,
+    "num_experts": 16,
+    "num_experts_per_tok": 4,
+    "moe_intermediate_size": 128,
+    "shared_expert_intermediate_size": 384,
+    "norm_topk_prob": False,
+    "rms_norm_eps": 1e-6,
+    "rope_theta": 1e6,
+}
+TINY_MODEL_GQA = {**TINY_MODEL, "num_key_value_heads": 2, "norm_topk_prob": True}
+MODEL_CASES = ((TINY_MODEL, 11), (TINY_MODEL_GQA, 12))
+MODEL_PROMPT, MODEL_NEW = 9, 4
+
+
+def model_fixtures() -> dict:
+    """The reference forward pass (runtime/qwen_moe.py:376-432) on seeded
+    synthetic decoders (expertrelay_b200.synth.make_model, regenerated by
+    the tests from the same seeds): all-position logits of a prompt, then
+    greedy decoding one token per call, with each call's logits."""
+    from expertrelay.runtime.qwen_moe import KVCache, ModelConfig, QwenMoe
+    from expertrelay.runtime.weights import ExpertSource, Int8Matrix, ResidentWeights, SourceStats
+
+    from expertrelay_b200 import synth
+
+    out = {}
+    for case, (cfg, seed) in enumerate(MODEL_CASES):
+        host = synth.make_model(cfg, seed=seed)
+        tensors = {k: (Int8Matrix(*v) if isinstance(v, tuple) else v) for k, v in host.tensors().items()}
+
+        class MemSource(ExpertSource):
+            def __init__(self):
+                self.stats = SourceStats()
+
+            def load(self, layer, expert):
+                self.stats.loads += 1
+                return {m: Int8Matrix(*qs) for m, qs in host.blocks[layer].experts[expert].items()}
+
+        model = QwenMoe(ModelConfig.from_hf(cfg), ResidentWeights(tensors, 0), MemSource())
+        kv = KVCache(model.c, MODEL_PROMPT + MODEL_NEW)
+        prompt = np.random.default_rng(seed).integers(0, cfg["vocab_size"], MODEL_PROMPT)
+        logits, _ = model.forward(prompt, kv, all_logits=True)
+        out[f"prompt{case}"] = prompt
+        out[f"prompt_logits{case}"] = logits.astype(np.float32)
+        tok, toks, steps = int(np.argmax(logits[-1])), [], []
+        for _ in range(MODEL_NEW):
+            toks.append(tok)
+            step, _ = model.forward(np.array([tok]), kv)
+            steps.append(step.astype(np.float32))
+            tok = int(np.argmax(step))
+        out[f"tokens{case}"] = np.array(toks, dtype=np.int64)
+        out[f"step_logits{case}"] = np.stack(steps)
+    return out
+
+
 STORE_SHAPE = {"hidden_size": 64, "moe_intermediate_size": 32, "num_layers": 2, "num_experts": 3}
 
 
@@ -354,7 +415,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--skip-full", action="store_true")
-    ap.add_argument("--only", choices=("trace", "store"), help="regenerate one fixture only")
+    ap.add_argument("--only", choices=("trace", "store", "model"), help="regenerate one fixture only")
     args = ap.parse_args()
     ref = Path(args.reference)
     _import_reference(ref)
@@ -363,6 +424,8 @@ def main() -> None:
             np.savez_compressed(HERE / "trace.npz", **trace_fixtures(Path(tmp)))
     if args.only in (None, "store"):
         store_fixture(HERE / "store_small")
+    if args.only in (None, "model"):
+        np.savez_compressed(HERE / "model.npz", **model_fixtures())
     if args.only is not None:
         return
     np.savez_compressed(HERE / "quant.npz", **quantizer_fixtures())
