@@ -502,7 +502,10 @@ def main() -> None:
     if rank == 0 and world == 1 and not args.no_full_model:
         del mb
         torch.cuda.empty_cache()
-        line["full_model"] = full_model_side(args, dev)
+        try:
+            line["full_model"] = full_model_side(args, dev)
+        except (RuntimeError, ValueError, OSError, MemoryError) as e:  # reported, the main line still prints
+            line["full_model"] = {"error": f"{type(e).__name__}: {e}"[:400]}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -516,6 +519,9 @@ def full_model_side(args, dev) -> dict:
     experts paged through an HBM cache of cache_frac of the records from
     pinned host memory, with the Fate prefetch. Decode tokens/s counts the
     one-token calls (each a full forward: embedding, 24 layers, lm_head)."""
+    import torch
+
+    from expertrelay_b200 import synth
     from expertrelay_b200.model import QwenMoeModel
 
     cfg = dict(synth.QWEN_MODEL, num_hidden_layers=args.model_layers)
