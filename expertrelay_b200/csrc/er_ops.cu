@@ -157,6 +157,85 @@ __global__ void __launch_bounds__(256) int8_gemv_kernel(const float* __restrict_
   }
 }
 
+// fp32 weights, a few rows: one warp per output row, x rows (m <= MT) from L1
+template <int MT>
+__global__ void __launch_bounds__(256) f32_gemv_kernel(const float* __restrict__ x, long long ldx,
+                                                       const float* __restrict__ w, const float* __restrict__ bias,
+                                                       float* __restrict__ y, int m, int out, int in) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= out) return;
+  const float* wr = w + (size_t)row * in;
+  float acc[MT];
+#pragma unroll
+  for (int i = 0; i < MT; ++i) acc[i] = 0.f;
+  for (int c = lane * 4; c < in; c += 32 * 4) {
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c));
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+      if (i < m) {
+        const float4 xv = __ldg(reinterpret_cast<const float4*>(x + (size_t)i * ldx + c));
+        acc[i] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[i]))));
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MT; ++i) acc[i] = warp_sum(acc[i]);
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+      if (i < m) y[(size_t)i * out + row] = bias ? acc[i] + bias[row] : acc[i];
+  }
+}
+
+// fp32 weights, few output rows (a router: 60 x 2048), many input rows: CTA
+// (o, chunk) holds weight row o in shared memory and gives each warp one
+// input row at a time of its 64-row chunk.
+__global__ void __launch_bounds__(256) f32_rows_kernel(const float* __restrict__ x, long long ldx,
+                                                       const float* __restrict__ w, const float* __restrict__ bias,
+                                                       float* __restrict__ y, int m, int out, int in) {
+  extern __shared__ float wrow[];
+  const int o = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int c = threadIdx.x * 4; c < in; c += blockDim.x * 4)
+    *reinterpret_cast<float4*>(wrow + c) = __ldg(reinterpret_cast<const float4*>(w + (size_t)o * in + c));
+  __syncthreads();
+  const float b = bias ? bias[o] : 0.f;
+  const int r_end = min(m, (int)(blockIdx.y + 1) * 64);
+  for (int r = blockIdx.y * 64 + warp; r < r_end; r += 8) {
+    const float* xr = x + (size_t)r * ldx;
+    float acc = 0.f;
+    for (int c = lane * 4; c < in; c += 32 * 4) {
+      const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + c));
+      const float4 wv = *reinterpret_cast<const float4*>(wrow + c);
+      acc = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc))));
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[(size_t)r * out + o] = acc + b;
+  }
+}
+
+static int launch_f32_small(const float* x, long long ldx, const float* w, const float* bias, float* y, int m, int out,
+                            int in, cudaStream_t st) {
+  if (m <= 8) {
+    const dim3 grid((out + 7) / 8), block(256);
+    if (m <= 1) f32_gemv_kernel<1><<<grid, block, 0, st>>>(x, ldx, w, bias, y, m, out, in);
+    else if (m <= 2) f32_gemv_kernel<2><<<grid, block, 0, st>>>(x, ldx, w, bias, y, m, out, in);
+    else if (m <= 4) f32_gemv_kernel<4><<<grid, block, 0, st>>>(x, ldx, w, bias, y, m, out, in);
+    else f32_gemv_kernel<8><<<grid, block, 0, st>>>(x, ldx, w, bias, y, m, out, in);
+    return launch_check("f32_gemv_kernel");
+  }
+  const size_t smem = (size_t)in * sizeof(float);
+  if (smem > 48 * 1024) {
+    if (int rc = cuda_check(cudaFuncSetAttribute(f32_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem),
+                            "f32 rows smem attribute"))
+      return rc;
+  }
+  f32_rows_kernel<<<dim3(out, (m + 63) / 64), 256, smem, st>>>(x, ldx, w, bias, y, m, out, in);
+  return launch_check("f32_rows_kernel");
+}
+
 static int launch_int8_gemv(const float* x, long long ldx, const int8_t* q, const float* s, const float* bias,
                             float* y, int m, int out, int in, cudaStream_t st) {
   const dim3 grid((out + 7) / 8), block(256);
@@ -286,6 +365,11 @@ size_t er_record_offset(int fmt, int hidden, int inter, int group, int which, in
 int er_linear_f32(const float* x, long long ldx, const float* w, const float* bias, float* y, int m, int out, int in,
                   void* stream) {
   if (int rc = check_linear_args("er_linear_f32", x, ldx, w, y, m, out, in)) return rc;
+  // a few rows, or few output rows (a router) over many: vector kernels
+  // with a dot product per warp; the tiled kernel for the rest
+  const bool vec_ok = in % 4 == 0 && ldx % 4 == 0 && !(((uintptr_t)x | (uintptr_t)w) & 15) && in <= 16384;
+  if (m > 0 && out > 0 && vec_ok && (m <= 8 || out <= 256))
+    return launch_f32_small(x, ldx, w, bias, y, m, out, in, (cudaStream_t)stream);
   return launch_linear<0>(x, ldx, w, nullptr, nullptr, nullptr, 1, bias, y, m, out, in, (cudaStream_t)stream);
 }
 

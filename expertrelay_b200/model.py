@@ -151,7 +151,7 @@ class QwenMoeModel:
                    "er_rms_norm")
         return h
 
-    def _attention(self, layer: int, h: torch.Tensor, kv: KVCache) -> torch.Tensor:
+    def _attention(self, layer: int, h: torch.Tensor, kv: KVCache, allowed: torch.Tensor) -> torch.Tensor:
         c, w = self.c, self.layers[layer]
         n, d = h.shape[0], c.head_dim
         q = self._linear(h, w["q_proj"], w["q_proj_bias"])
@@ -165,9 +165,6 @@ class QwenMoeModel:
         if c.num_kv_heads != c.num_heads:
             rep = c.num_heads // c.num_kv_heads
             keys, values = keys.repeat_interleave(rep, dim=1), values.repeat_interleave(rep, dim=1)
-        # causal: query start + i sees keys 0 .. start + i
-        allowed = (torch.arange(end, device=self.device)[None, :]
-                   <= (start + torch.arange(n, device=self.device))[:, None]).to(torch.uint8)
         out = torch.empty((n, c.num_heads * d), dtype=torch.float32, device=self.device)
         _lib.check(_lib.lib().er_attention(q.data_ptr(), keys.contiguous().data_ptr(), values.contiguous().data_ptr(),
                                            allowed.data_ptr(), out.data_ptr(), n, end, c.num_heads, d,
@@ -189,9 +186,13 @@ class QwenMoeModel:
         if expert_trace is not None:
             positions = kv.length + np.arange(n)
             expert_trace.begin(positions, np.asarray(token_ids), PHASE_PREFILL if kv.length == 0 else PHASE_DECODE)
+        # causal: query start + i sees keys 0 .. start + i (the same for every layer)
+        start, end = kv.length, kv.length + n
+        allowed = (torch.arange(end, device=self.device)[None, :]
+                   <= (start + torch.arange(n, device=self.device))[:, None]).to(torch.uint8)
         h = self._norm(x, self.layers[0]["in_norm"])
         for layer in range(c.num_layers):
-            a = self._attention(layer, h, kv)
+            a = self._attention(layer, h, kv, allowed)
             h = self._norm(x, self.layers[layer]["post_norm"], add=a)
             y = self.stack.moe(layer, h, self.path, trace=expert_trace)
             if layer + 1 < c.num_layers:

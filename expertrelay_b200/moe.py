@@ -152,7 +152,11 @@ class MoeBlock:
         """Device addresses of each expert's record (e.g. HBM cache slots)."""
         if addresses.numel() != self.num_experts:
             raise ValueError("one address per expert")
-        self.expert_table.copy_(addresses.to(self.device, torch.int64), non_blocking=True)
+        if addresses.device.type == "cpu" and addresses.dtype == torch.int64:
+            # straight from host memory: asynchronous when the source is pinned
+            self.expert_table.copy_(addresses, non_blocking=addresses.is_pinned())
+        else:
+            self.expert_table.copy_(addresses.to(self.device, torch.int64), non_blocking=True)
 
     def workspace_bytes(self, n: int, path: int = _lib.PATH_AUTO) -> int:
         return int(_lib.lib().er_moe_workspace_bytes(C.byref(self._w), int(n), int(path)))

@@ -47,6 +47,9 @@ class PagedMoeStack:
         ]
         self.num_experts = self.layers[0].num_experts
         self.top_k = self.layers[0].top_k
+        # per layer, the expert table staged in pinned memory so its copy to the
+        # device is asynchronous (a layer's buffer is reused only a forward later)
+        self._table_host = [torch.empty(self.num_experts, dtype=torch.int64, pin_memory=True) for _ in self.layers]
         self.prefetches_skipped_low_confidence = 0
 
     def moe(self, layer: int, h: torch.Tensor, path: int = _lib.PATH_AUTO, *, trace=None,
@@ -68,10 +71,11 @@ class PagedMoeStack:
         _lib.check(rc, "er_router_topk")
         needed = np.unique(idx.cpu().numpy())  # the host decides which records to fetch
         addrs = cache.acquire(layer, needed)
-        table = np.full(self.num_experts, int(addrs[0]), dtype=np.uint64)  # unrouted experts: never read
+        table = self._table_host[layer].numpy().view(np.uint64)
+        table[:] = int(addrs[0])  # unrouted experts: never read
         table[needed] = addrs
         blk.use_arena(cache.arena_base, cache.num_slots)
-        blk.set_expert_table(torch.from_numpy(table.view(np.int64)))
+        blk.set_expert_table(self._table_host[layer])
         has_next = layer + 1 < len(self.layers)
         fate = None
         if (self.prefetch_enabled or trace is not None) and has_next:
