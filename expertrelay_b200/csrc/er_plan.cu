@@ -52,14 +52,14 @@ __device__ __forceinline__ int cta_excl_scan(int v, int* tmp, int* total) {
 // schedules for the expert kernels. Ends with a __syncthreads.
 __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, int I, int Is, SchedSpec s0,
                           SchedSpec s1, int shared, bool write_plan, int* hist, int* offs, int* act, int* bad_out,
-                          int* tmp) {
+                          int* tmp, const int* tally = nullptr) {
   const int tid = threadIdx.x;
   const int nk = n * k;
   int cnt[2], on[2];
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int e = 2 * tid + j;
-    cnt[j] = e < E ? __ldcg(&plan->tally[e]) : 0;  // counted at L2 by atomics
+    cnt[j] = e < E ? (tally ? tally[e] : __ldcg(&plan->tally[e])) : 0;  // plan->tally: counted at L2 by atomics
     on[j] = cnt[j] > 0;
     if (e < E) hist[e] = cnt[j];
   }
@@ -133,9 +133,7 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
   __syncthreads();
 }
 
-// One token per warp (8 per CTA; with KPER, top-k fused, one CTA of up to 16
-// warps for the whole batch: each warp first runs its token's softmax +
-// top-k, counting into plan->tally, before anything below). With SLICE and rows of up to 2048
+// One token per warp, 8 per CTA. With SLICE and rows of up to 2048
 // values, each warp first slices its token's h row (K = H values) into two
 // int8 words per lane and step, held in registers; the CTA then derives the
 // expert ranges from the tallies (CTA 0 also writes the plan). Then lane r < k of a token's warp claims the
@@ -144,14 +142,14 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
 // expert, to row nk + t. Longer rows are read twice after the scan. The row
 // loop is not unrolled: this kernel runs once per block, mostly from a cold
 // instruction cache, so its code is kept short.
-template <typename XT, bool SLICE, int KPER>
-__global__ void __launch_bounds__(512) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
+template <typename XT, bool SLICE>
+__global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
                                                        const float* __restrict__ w, int n, int k, int E, int H, int I,
                                                        int Is, SchedSpec spec0, SchedSpec spec1, int shared,
                                                        Plan* __restrict__ plan, int32_t* __restrict__ perm_token,
                                                        float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
                                                        int8_t* __restrict__ s0, int8_t* __restrict__ s1,
-                                                       float* __restrict__ scale, TopkArgs topk) {
+                                                       float* __restrict__ scale) {
   __shared__ int hist[kMaxExperts];
   __shared__ int offs[kMaxExperts];
   __shared__ int act[kMaxExperts + 1];
@@ -159,11 +157,7 @@ __global__ void __launch_bounds__(512) dispatch_kernel(const XT* __restrict__ h,
   __shared__ int scan_tmp[16];
   chain_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if constexpr (KPER > 0) {
-    if (t < n) topk_token<KPER>(topk, n, E, k, t, lane);
-    __threadfence();  // the tallies (L2 atomics) and ids before the scan reads them
-  }
+  const int t = blockIdx.x * 8 + warp;
   constexpr int kRegVec = 16;  // float4 per lane held in registers: H <= 2048
   const bool in_regs = SLICE && H <= 128 * kRegVec;
   uint32_t q0[kRegVec], q1[kRegVec];
@@ -188,8 +182,7 @@ __global__ void __launch_bounds__(512) dispatch_kernel(const XT* __restrict__ h,
   const int nk = n * k;
   int p = -1;
   if (lane < k) {
-    // ids and weights written by this kernel's top-k are read at L2, not through the read-only cache
-    const int e = KPER > 0 ? __ldcg(idx + (size_t)t * k + lane) : idx[(size_t)t * k + lane];
+    const int e = idx[(size_t)t * k + lane];
     if (e >= 0 && e < E) {
       const int c = atomicAdd(&plan->cursor[e], 1);
       if (c >= hist[e]) {  // only an inconsistent tally gets here
@@ -197,7 +190,7 @@ __global__ void __launch_bounds__(512) dispatch_kernel(const XT* __restrict__ h,
       } else {
         p = offs[e] + c;
         perm_token[p] = t;
-        perm_w[p] = KPER > 0 ? __ldcg(w + (size_t)t * k + lane) : w[(size_t)t * k + lane];
+        perm_w[p] = w[(size_t)t * k + lane];
       }
     } else {
       atomicOr(&plan->error, 1);
@@ -243,6 +236,89 @@ __global__ void __launch_bounds__(512) dispatch_kernel(const XT* __restrict__ h,
   }
 }
 
+// Small batches (n <= kFusedTopkMaxTok), top-k fused: CTA c of n owns token
+// c. Every CTA runs the softmax + top-k of all n tokens (a warp each) into
+// shared memory and derives the plan from those tallies (CTA 0 writes it, the
+// top-k outputs of token c are written by CTA c), so the positions need no
+// atomics: slot j of token t goes to its expert's range start plus the
+// number of earlier (token, slot) pairs of the same expert. Warp 0 of CTA c
+// then slices token c's h row into its k rows and the shared row, so the
+// rows' stores spread over n SMs.
+template <typename XT, bool SLICE, int KPER>
+__global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restrict__ h, int n, int k, int E, int H,
+                                                             int I, int Is, SchedSpec spec0, SchedSpec spec1,
+                                                             int shared, Plan* __restrict__ plan,
+                                                             int32_t* __restrict__ perm_token,
+                                                             float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
+                                                             int8_t* __restrict__ s0, int8_t* __restrict__ s1,
+                                                             float* __restrict__ scale, TopkArgs topk) {
+  __shared__ int hist[kMaxExperts];
+  __shared__ int offs[kMaxExperts];
+  __shared__ int act[kMaxExperts + 1];
+  __shared__ int tally_s[kMaxExperts];
+  __shared__ int sel_s[kFusedTopkMaxTok * kMaxTopK];
+  __shared__ float w_s[kFusedTopkMaxTok * kMaxTopK];
+  __shared__ int bad;
+  __shared__ int scan_tmp[16];
+  chain_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int me = blockIdx.x;  // this CTA's token
+  for (int e = threadIdx.x; e < E; e += blockDim.x) tally_s[e] = 0;
+  __syncthreads();
+  if (warp < n) {
+    TopkArgs a = topk;
+    a.idx64 = nullptr;
+    a.idx32 = sel_s;
+    a.wout = w_s;
+    a.tally = tally_s;
+    if (warp != me) {  // the token's own CTA writes its gate and summed logits
+      a.gate_sig = nullptr;
+      a.logits_sum = nullptr;
+    }
+    topk_token<KPER>(a, n, E, k, warp, lane);
+  }
+  __syncthreads();
+  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, me == 0, hist, offs, act, &bad, scan_tmp, tally_s);
+  if (me >= n || bad || warp != 0) return;
+  const int nk = n * k;
+  int p = -1;
+  if (lane < k) {
+    const int e = sel_s[me * k + lane];
+    const float wt = w_s[me * k + lane];
+    if (topk.idx32) topk.idx32[(size_t)me * k + lane] = e;
+    if (topk.idx64) topk.idx64[(size_t)me * k + lane] = e;
+    if (topk.wout) topk.wout[(size_t)me * k + lane] = wt;
+    int before = 0;  // earlier (token, slot) pairs routed to e
+    for (int i = 0; i < me * k + lane; ++i) before += sel_s[i] == e;
+    p = offs[e] + before;
+    perm_token[p] = me;
+    perm_w[p] = wt;
+    pos_of[(size_t)me * k + lane] = p;
+  }
+  if constexpr (SLICE) {
+    const XT* x = h + (size_t)me * H;
+    float amax = 0.f;
+    for (int c = lane * 4; c < H; c += 128) amax = fmaxf(amax, abs_max4(load4(x + c)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+    for (int c = lane * 4; c < H; c += 128) {
+      uint32_t w0, w1;
+      slice4(load4(x + c), inv, w0, w1);
+#pragma unroll 1
+      for (int r = 0; r <= k; ++r) {  // rows r < k: the slots' positions; row k: the shared expert's row
+        const int pr = __shfl_sync(0xffffffffu, p, r < k ? r : 0);
+        const int row = r < k ? pr : (shared ? nk + me : -1);
+        if (row < 0) continue;
+        *reinterpret_cast<uint32_t*>(s0 + (size_t)row * H + c) = w0;
+        *reinterpret_cast<uint32_t*>(s1 + (size_t)row * H + c) = w1;
+      }
+    }
+    if (lane < k) scale[p] = amax / 127.f;
+    if (lane == 31 && shared) scale[nk + me] = amax / 127.f;
+  }
+}
+
 long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int I, int Is) {
   const long long nk = (long long)n * k;
   const long long active = nk < E ? nk : E;  // routed groups with at least one token
@@ -279,20 +355,19 @@ static int launch_dispatch_t(const XT* h, const int32_t* idx, const float* w, in
                              const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
                              int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk,
                              cudaStream_t st) {
-  if (topk) {  // one CTA, one warp per token
-    const dim3 block(32 * (n > 8 ? 16 : 8));
+  if (topk) {  // a CTA per token (at least one: CTA 0 writes the plan), a warp per token inside each
+    const dim3 grid(n > 0 ? n : 1), block(32 * (n > 8 ? 16 : 8));
     if (E <= 64)
-      return launch_chained(dispatch_kernel<XT, SLICE, 2>, dim3(1), block, 0, st, "dispatch_kernel", h, idx, w, n, k,
-                            E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1, scale,
-                            *topk);
-    return launch_chained(dispatch_kernel<XT, SLICE, kMaxExperts / 32>, dim3(1), block, 0, st, "dispatch_kernel", h,
-                          idx, w, n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0,
-                          s1, scale, *topk);
+      return launch_chained(dispatch_small_kernel<XT, SLICE, 2>, grid, block, 0, st, "dispatch_small_kernel", h, n,
+                            k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1,
+                            scale, *topk);
+    return launch_chained(dispatch_small_kernel<XT, SLICE, kMaxExperts / 32>, grid, block, 0, st,
+                          "dispatch_small_kernel", h, n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token,
+                          perm_w, pos_of, s0, s1, scale, *topk);
   }
   const int blocks = n > 0 ? (n + 7) / 8 : 1;  // CTA 0 writes the plan even for no tokens
-  return launch_chained(dispatch_kernel<XT, SLICE, 0>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel", h, idx, w,
-                        n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1, scale,
-                        TopkArgs{});
+  return launch_chained(dispatch_kernel<XT, SLICE>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel", h, idx, w, n,
+                        k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1, scale);
 }
 
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
