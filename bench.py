@@ -13,6 +13,14 @@ inside the timed region. Each step is timed with CUDA events on the
 launching stream after an L2 flush (a 256 MiB write), and the dominant
 kernel is timed live through the block's stage events.
 
+On one GPU the line also carries `decode` (the same block at 8 decode
+tokens) and `full_model`: greedy decoding through the whole 24-layer
+Qwen1.5-MoE-A2.7B-shaped decoder (random init, a 512-token seeded prompt,
+128 tokens, batch 1) with a quarter of the routed experts in the HBM cache
+and the rest paged from pinned host memory with the Fate prefetch
+(--no-full-model skips it; --model-layers, --prompt-tokens, --new-tokens,
+--cache-frac size it).
+
 --impl reference times the CPU implementation of the path (the oracle, a
 restatement of the reference's numpy/BLAS code) on this host's cores on the
 same workload; under torchrun only rank 0 runs it.

@@ -110,51 +110,84 @@ static int launch_linear(const float* x, long long ldx, const void* w, const flo
 
 // ---------------------------------------------------------------------------
 // int8 weight streaming for a few rows (decode): y[m, out] = (x @ Q^T) * s (+ b)
-// One warp per output row; each lane reads 16 codes per step (one 16-byte
-// load, not kept in L1), every row of x (m <= MT) from L1, and the warp sums
-// its lanes at the end. The weights cross HBM once; x stays cached.
+// Each warp owns R output rows (R = 4 for tall matrices such as the lm_head,
+// 1 when that would leave SMs idle); each lane reads 16 codes of every one of
+// them per step (16-byte loads, not kept in L1, all issued before the math),
+// every row of x (m <= MT) from L1, and the warp sums its lanes at the end.
+// The weights cross HBM once; x stays cached.
 // ---------------------------------------------------------------------------
-template <int MT>
+template <int MT, int kGemvRows>
 __global__ void __launch_bounds__(256) int8_gemv_kernel(const float* __restrict__ x, long long ldx,
                                                         const int8_t* __restrict__ q, const float* __restrict__ s,
                                                         const float* __restrict__ bias, float* __restrict__ y,
                                                         int m, int out, int in) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int row0 = (blockIdx.x * 8 + (threadIdx.x >> 5)) * kGemvRows;
   const int lane = threadIdx.x & 31;
-  if (row >= out) return;
-  const int8_t* qr = q + (size_t)row * in;
-  float acc[MT];
+  if (row0 >= out) return;
+  float acc[kGemvRows][MT];
 #pragma unroll
-  for (int i = 0; i < MT; ++i) acc[i] = 0.f;
+  for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+    for (int i = 0; i < MT; ++i) acc[r][i] = 0.f;
   for (int c = lane * 16; c < in; c += 32 * 16) {
-    const uint4 raw = ld_stream_u4(qr + c);
-    const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
-    float w[16];
+    uint4 raw[kGemvRows];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) w[j] = (float)b[j];
+    for (int r = 0; r < kGemvRows; ++r)
+      raw[r] = row0 + r < out ? ld_stream_u4(q + (size_t)(row0 + r) * in + c) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
       if (i < m) {
         const float4* xr = reinterpret_cast<const float4*>(x + (size_t)i * ldx + c);
+        float xv[16];
 #pragma unroll
         for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 xv = __ldg(xr + j4);
-          acc[i] = fmaf(w[4 * j4], xv.x, acc[i]);
-          acc[i] = fmaf(w[4 * j4 + 1], xv.y, acc[i]);
-          acc[i] = fmaf(w[4 * j4 + 2], xv.z, acc[i]);
-          acc[i] = fmaf(w[4 * j4 + 3], xv.w, acc[i]);
+          const float4 v = __ldg(xr + j4);
+          xv[4 * j4] = v.x;
+          xv[4 * j4 + 1] = v.y;
+          xv[4 * j4 + 2] = v.z;
+          xv[4 * j4 + 3] = v.w;
+        }
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r) {
+          const int8_t* b = reinterpret_cast<const int8_t*>(&raw[r]);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[r][i] = fmaf((float)b[j], xv[j], acc[r][i]);
         }
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < MT; ++i) acc[i] = warp_sum(acc[i]);
-  if (lane == 0) {
-    const float sc = s[row], bv = bias ? bias[row] : 0.f;
+  for (int r = 0; r < kGemvRows; ++r) {
 #pragma unroll
-    for (int i = 0; i < MT; ++i)
-      if (i < m) y[(size_t)i * out + row] = bias ? acc[i] * sc + bv : acc[i] * sc;
+    for (int i = 0; i < MT; ++i) acc[r][i] = warp_sum(acc[r][i]);
+    const int row = row0 + r;
+    if (lane == 0 && row < out) {
+      const float sc = s[row], bv = bias ? bias[row] : 0.f;
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+        if (i < m) y[(size_t)i * out + row] = bias ? acc[r][i] * sc + bv : acc[r][i] * sc;
+    }
   }
+}
+
+template <int R>
+static void launch_int8_gemv_r(const float* x, long long ldx, const int8_t* q, const float* s, const float* bias,
+                               float* y, int m, int out, int in, cudaStream_t st) {
+  const dim3 grid((out + 8 * R - 1) / (8 * R)), block(256);
+  if (m <= 1) int8_gemv_kernel<1, R><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+  else if (m <= 2) int8_gemv_kernel<2, R><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+  else if (m <= 4) int8_gemv_kernel<4, R><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+  else int8_gemv_kernel<8, R><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
+}
+
+static int launch_int8_gemv(const float* x, long long ldx, const int8_t* q, const float* s, const float* bias,
+                            float* y, int m, int out, int in, cudaStream_t st) {
+  // four rows per warp only while that still gives every SM several CTAs
+  if (out >= 4 * 8 * 148 * 4)
+    launch_int8_gemv_r<4>(x, ldx, q, s, bias, y, m, out, in, st);
+  else
+    launch_int8_gemv_r<1>(x, ldx, q, s, bias, y, m, out, in, st);
+  return launch_check("int8_gemv_kernel");
 }
 
 // fp32 weights, a few rows: one warp per output row, x rows (m <= MT) from L1
@@ -236,15 +269,6 @@ static int launch_f32_small(const float* x, long long ldx, const float* w, const
   return launch_check("f32_rows_kernel");
 }
 
-static int launch_int8_gemv(const float* x, long long ldx, const int8_t* q, const float* s, const float* bias,
-                            float* y, int m, int out, int in, cudaStream_t st) {
-  const dim3 grid((out + 7) / 8), block(256);
-  if (m <= 1) int8_gemv_kernel<1><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
-  else if (m <= 2) int8_gemv_kernel<2><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
-  else if (m <= 4) int8_gemv_kernel<4><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
-  else int8_gemv_kernel<8><<<grid, block, 0, st>>>(x, ldx, q, s, bias, y, m, out, in);
-  return launch_check("int8_gemv_kernel");
-}
 
 static int check_linear_args(const char* name, const float* x, long long ldx, const void* w, float* y, int m, int out,
                              int in) {
