@@ -297,21 +297,51 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
   }
   if constexpr (SLICE) {
     const XT* x = h + (size_t)me * H;
+    // rows of up to 2048 values: all of the lane's loads issued at once and
+    // held in registers (a loop of dependent loads costs a round trip each)
+    constexpr int kRegVec = 16;
+    const bool in_regs = H <= 128 * kRegVec;
+    float4 v[kRegVec];
     float amax = 0.f;
-    for (int c = lane * 4; c < H; c += 128) amax = fmaxf(amax, abs_max4(load4(x + c)));
+    if (in_regs) {
+#pragma unroll
+      for (int i = 0; i < kRegVec; ++i) {
+        const int c = lane * 4 + 128 * i;
+        v[i] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < kRegVec; ++i) amax = fmaxf(amax, abs_max4(v[i]));
+    } else {
+      for (int c = lane * 4; c < H; c += 128) amax = fmaxf(amax, abs_max4(load4(x + c)));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float inv = amax > 0.f ? 127.f / amax : 0.f;
-    for (int c = lane * 4; c < H; c += 128) {
-      uint32_t w0, w1;
-      slice4(load4(x + c), inv, w0, w1);
 #pragma unroll 1
-      for (int r = 0; r <= k; ++r) {  // rows r < k: the slots' positions; row k: the shared expert's row
-        const int pr = __shfl_sync(0xffffffffu, p, r < k ? r : 0);
-        const int row = r < k ? pr : (shared ? nk + me : -1);
-        if (row < 0) continue;
-        *reinterpret_cast<uint32_t*>(s0 + (size_t)row * H + c) = w0;
-        *reinterpret_cast<uint32_t*>(s1 + (size_t)row * H + c) = w1;
+    for (int r = 0; r <= k; ++r) {  // rows r < k: the slots' positions; row k: the shared expert's row
+      const int pr = __shfl_sync(0xffffffffu, p, r < k ? r : 0);
+      const int row = r < k ? pr : (shared ? nk + me : -1);
+      if (row < 0) continue;
+      int8_t* d0 = s0 + (size_t)row * H;
+      int8_t* d1 = s1 + (size_t)row * H;
+      if (in_regs) {
+#pragma unroll
+        for (int i = 0; i < kRegVec; ++i) {
+          const int c = lane * 4 + 128 * i;
+          if (c < H) {
+            uint32_t w0, w1;
+            slice4(v[i], inv, w0, w1);
+            *reinterpret_cast<uint32_t*>(d0 + c) = w0;
+            *reinterpret_cast<uint32_t*>(d1 + c) = w1;
+          }
+        }
+      } else {
+        for (int c = lane * 4; c < H; c += 128) {
+          uint32_t w0, w1;
+          slice4(load4(x + c), inv, w0, w1);
+          *reinterpret_cast<uint32_t*>(d0 + c) = w0;
+          *reinterpret_cast<uint32_t*>(d1 + c) = w1;
+        }
       }
     }
     if (lane < k) scale[p] = amax / 127.f;
