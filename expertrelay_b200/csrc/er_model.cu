@@ -56,23 +56,31 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, const flo
 }
 
 // One CTA per token: rotate the token's q heads and k heads (position
-// pos0 + t), then write k and v into the cache rows pos0 + t. Thread j < d/2
-// of a head handles the pair (j, j + d/2): out_j = x_j cos_j - x_{j+d/2} sin_j,
-// out_{j+d/2} = x_{j+d/2} cos_j + x_j sin_j (cos/sin of both halves equal).
+// pos0 + t), then write k and v into the cache rows pos0 + t. The d/2
+// angles' cos and sin are computed once per token into shared memory; then
+// thread j < d/2 of a head handles the pair (j, j + d/2): out_j = x_j cos_j -
+// x_{j+d/2} sin_j, out_{j+d/2} = x_{j+d/2} cos_j + x_j sin_j (cos/sin of
+// both halves equal).
 __global__ void __launch_bounds__(256) rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k,
                                                       const float* __restrict__ v, int heads, int kv_heads, int d,
                                                       int pos0, float theta, float* __restrict__ k_cache,
                                                       float* __restrict__ v_cache) {
+  extern __shared__ float cs[];  // [d/2] cos, then [d/2] sin
   chain_wait();
   const int t = blockIdx.x;
   const int half = d / 2;
   const float pos = (float)(pos0 + t);
-  for (int i = threadIdx.x; i < (heads + kv_heads) * half; i += blockDim.x) {
-    const int head = i / half, j = i % half;
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
     // inv_freq_j = 1 / theta^(2j / d), in fp32 like the reference's table
     const float inv_freq = 1.0f / powf(theta, (float)(2 * j) / (float)d);
     const float ang = pos * inv_freq;
-    const float c = cosf(ang), s = sinf(ang);
+    cs[j] = cosf(ang);
+    cs[half + j] = sinf(ang);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < (heads + kv_heads) * half; i += blockDim.x) {
+    const int head = i / half, j = i % half;
+    const float c = cs[j], s = cs[half + j];
     if (head < heads) {
       float* qh = q + ((size_t)t * heads + head) * d;
       const float a = qh[j], b = qh[j + half];
@@ -140,8 +148,9 @@ extern "C" int er_rope_kv(float* q, const float* k, const float* v, int n, int h
     return fail(ER_EINVAL, "sequence length %d exceeds the KV cache (%d)", pos0 + n, max_seq);
   if (n == 0) return ER_OK;
   if (!q || !k || !v || !k_cache || !v_cache) return fail(ER_EINVAL, "er_rope_kv: null argument");
-  return launch_chained(rope_kv_kernel, dim3(n), dim3(256), 0, (cudaStream_t)stream, "rope_kv_kernel", q, k, v, heads,
-                        kv_heads, head_dim, pos0, theta, k_cache, v_cache);
+  if (head_dim > 8192) return fail(ER_EINVAL, "er_rope_kv: head_dim %d above 8192", head_dim);
+  return launch_chained(rope_kv_kernel, dim3(n), dim3(256), (size_t)head_dim * sizeof(float), (cudaStream_t)stream,
+                        "rope_kv_kernel", q, k, v, heads, kv_heads, head_dim, pos0, theta, k_cache, v_cache);
 }
 
 extern "C" int er_embed_int8(const int8_t* q, const float* scales, long long vocab, int hidden, const int64_t* ids,

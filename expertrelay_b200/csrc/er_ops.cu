@@ -327,6 +327,78 @@ __global__ void __launch_bounds__(128) attention_kernel(const float* __restrict_
   }
 }
 
+// The same with vector loads (d a multiple of 4, rows 16-byte aligned): a
+// warp per key for the scores (one coalesced pass over the key row, lanes
+// splitting d), then for p @ v each thread owns output columns and walks
+// half of the keys, four loads in flight, halves added through shared memory.
+// One CTA per (query, head), 256 threads.
+__global__ void __launch_bounds__(256) attention_vec_kernel(const float* __restrict__ q,
+                                                            const float* __restrict__ keys,
+                                                            const float* __restrict__ values,
+                                                            const uint8_t* __restrict__ allowed,
+                                                            float* __restrict__ out, int n, int kv, int heads, int d,
+                                                            float scale) {
+  extern __shared__ float sm[];  // [kv] scores, then [2][d] partial outputs (the two halves of the keys)
+  float* sc = sm;
+  float* part = sm + kv;  // [2][d] (two halves of the keys)
+  __shared__ float red[8];
+  const int i = blockIdx.x / heads, hh = blockIdx.x % heads;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* qv = q + ((size_t)i * heads + hh) * d;
+  for (int j = warp; j < kv; j += 8) {
+    const float* kp = keys + ((size_t)j * heads + hh) * d;
+    float s = 0.f;
+    for (int c = lane * 4; c < d; c += 128) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(qv + c));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(kp + c));
+      s = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, s))));
+    }
+    s = warp_sum(s) * scale;
+    if (lane == 0) sc[j] = allowed[(size_t)i * kv + j] ? s : -INFINITY;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int j = threadIdx.x; j < kv; j += blockDim.x) mx = fmaxf(mx, sc[j]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w2 = 1; w2 < 8; ++w2) mx = fmaxf(mx, red[w2]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < kv; j += blockDim.x) {
+    const float e = expf(sc[j] - mx);
+    sc[j] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int w2 = 0; w2 < 8; ++w2) sum += red[w2];
+  const float inv = 1.0f / sum;
+  // p @ v: thread t takes column c = t mod 128 (+128 per pass) and half t / 128 of the keys
+  const int half = threadIdx.x >> 7, col = threadIdx.x & 127;
+  const int j_mid = (kv + 1) / 2, j0 = half ? j_mid : 0, j1 = half ? kv : j_mid;
+  for (int c = col; c < d; c += 128) {
+    const float* vp = values + (size_t)hh * d + c;
+    const size_t stride = (size_t)heads * d;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int j = j0;
+    for (; j + 3 < j1; j += 4) {
+      a0 = fmaf(sc[j] * inv, vp[(size_t)j * stride], a0);
+      a1 = fmaf(sc[j + 1] * inv, vp[(size_t)(j + 1) * stride], a1);
+      a2 = fmaf(sc[j + 2] * inv, vp[(size_t)(j + 2) * stride], a2);
+      a3 = fmaf(sc[j + 3] * inv, vp[(size_t)(j + 3) * stride], a3);
+    }
+    for (; j < j1; ++j) a0 = fmaf(sc[j] * inv, vp[(size_t)j * stride], a0);
+    part[half * d + c] = (a0 + a1) + (a2 + a3);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x)
+    out[((size_t)i * heads + hh) * d + c] = part[c] + part[d + c];
+}
+
 // ---------------------------------------------------------------------------
 // weight reconstruction: bit-exact fp32 (store/quantize.py:45-46,
 // store/int4.py:142-144, bench/gptq_conversion_check.py:42-55)
@@ -423,6 +495,20 @@ int er_attention(const float* q, const float* keys, const float* values, const u
   if (n < 0 || kv < 0 || heads <= 0 || d <= 0) return fail(ER_EINVAL, "er_attention: bad sizes");
   if (n == 0) return ER_OK;
   if (!q || !keys || !values || !allowed || !out) return fail(ER_EINVAL, "er_attention: null pointer");
+  const bool vec = d % 4 == 0 && !(((uintptr_t)q | (uintptr_t)keys | (uintptr_t)values) & 15);
+  if (vec) {
+    const size_t smem_v = ((size_t)kv + 2 * (size_t)d) * sizeof(float);
+    if (smem_v > 200 * 1024) return fail(ER_EINVAL, "er_attention: kv %d too long for one CTA", kv);
+    if (smem_v > 48 * 1024) {
+      if (int rc = cuda_check(cudaFuncSetAttribute(attention_vec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   200 * 1024),
+                              "attention smem attribute"))
+        return rc;
+    }
+    attention_vec_kernel<<<n * heads, 256, smem_v, (cudaStream_t)stream>>>(q, keys, values, allowed, out, n, kv, heads,
+                                                                           d, 1.0f / sqrtf((float)d));
+    return launch_check("attention_vec_kernel");
+  }
   const size_t smem = (size_t)kv * sizeof(float);
   if (smem > 200 * 1024) return fail(ER_EINVAL, "er_attention: kv %d too long for one CTA", kv);
   if (smem > 48 * 1024) {

@@ -88,17 +88,25 @@ def test_int4_linear_on_gptq_weights(be, n):
     np.testing.assert_allclose(be.int4_linear(x, packed, s, 32), exact, rtol=RTOL, atol=ATOL)
 
 
-def test_linear_and_attention_match_float64(be):
+# (rows, out, in): the few-rows vector kernel, the router-shaped rows kernel,
+# the tiled kernel, and an unaligned width that falls back to the tiled one
+@pytest.mark.parametrize(("n", "out_dim", "in_dim"), [(4, 7, 32), (40, 60, 2048), (40, 300, 96), (1, 60, 2050)])
+def test_linear_matches_float64(be, n, out_dim, in_dim):
     rng = np.random.default_rng(1)
-    w = rng.normal(0, 0.1, (7, 32)).astype(np.float32)
-    x = rng.normal(0, 1, (4, 32)).astype(np.float32)
-    np.testing.assert_allclose(be.linear(x, w), x.astype(np.float64) @ w.T, rtol=RTOL, atol=ATOL)
-    b = rng.normal(0, 1, 7).astype(np.float32)
-    np.testing.assert_allclose(be.linear(x, w, b), x.astype(np.float64) @ w.T + b, rtol=RTOL, atol=ATOL)
+    w = rng.normal(0, 0.1, (out_dim, in_dim)).astype(np.float32)
+    x = rng.normal(0, 1, (n, in_dim)).astype(np.float32)
+    tol = ATOL * max(1.0, np.sqrt(in_dim / 96))
+    np.testing.assert_allclose(be.linear(x, w), x.astype(np.float64) @ w.T, rtol=RTOL, atol=tol)
+    b = rng.normal(0, 1, out_dim).astype(np.float32)
+    np.testing.assert_allclose(be.linear(x, w, b), x.astype(np.float64) @ w.T + b, rtol=RTOL, atol=tol)
+
+
+# (queries, keys, heads, head dim): vector kernel (d % 4 == 0) and the scalar one
+@pytest.mark.parametrize(("n", "k", "heads", "d"), [(3, 8, 4, 16), (1, 300, 16, 128), (5, 37, 2, 130)])
+def test_attention_matches_float64(be, n, k, heads, d):
     rng = np.random.default_rng(2)
-    n, k, heads, d = 3, 8, 4, 16
     q, keys, values = (rng.normal(0, 1, (m, heads, d)).astype(np.float32) for m in (n, k, k))
-    allowed = np.arange(k)[None, :] <= (5 + np.arange(n))[:, None]
+    allowed = np.arange(k)[None, :] <= (k - n + np.arange(n))[:, None]
     scores = np.einsum("qhd,khd->hqk", q.astype(np.float64), keys) / np.sqrt(d)
     scores = np.where(allowed[None], scores, -np.inf)
     probs = np.exp(scores - scores.max(-1, keepdims=True))
