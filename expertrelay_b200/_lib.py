@@ -143,7 +143,7 @@ SIGNATURES: dict[str, tuple] = {
     "er_cache_stats_get": (_i, [_vp, C.POINTER(CacheStats)]),
     "er_trace_record_bytes": (C.c_size_t, [_i, _i]),
     "er_rms_norm": (_i, [_vp, _vp, _vp, C.c_float, _i, _i, _vp, _vp, _vp]),
-    "er_rope_kv": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, C.c_float, _vp, _vp, _i, _vp]),
+    "er_rope_kv": (_i, [_vp, C.c_longlong, _vp, _i, _i, _i, _i, _i, C.c_float, _vp, _vp, _i, _vp]),
     "er_embed_int8": (_i, [_vp, _vp, C.c_longlong, _i, _vp, _i, _vp, _vp, _vp]),
     "er_store_open": (_i, [C.c_char_p, _i, C.POINTER(_vp)]),
     "er_store_close": (_i, [_vp]),

@@ -55,14 +55,15 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, const flo
   }
 }
 
-// One CTA per token: rotate the token's q heads and k heads (position
-// pos0 + t), then write k and v into the cache rows pos0 + t. The d/2
+// One CTA per token: the token's row of the fused q|k|v projection (row
+// stride ld); rotate its q heads into q_out and its k heads (position
+// pos0 + t) into the cache rows pos0 + t, and copy v there. The d/2
 // angles' cos and sin are computed once per token into shared memory; then
 // thread j < d/2 of a head handles the pair (j, j + d/2): out_j = x_j cos_j -
 // x_{j+d/2} sin_j, out_{j+d/2} = x_{j+d/2} cos_j + x_j sin_j (cos/sin of
 // both halves equal).
-__global__ void __launch_bounds__(256) rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k,
-                                                      const float* __restrict__ v, int heads, int kv_heads, int d,
+__global__ void __launch_bounds__(256) rope_kv_kernel(const float* __restrict__ qkv, long long ld,
+                                                      float* __restrict__ q_out, int heads, int kv_heads, int d,
                                                       int pos0, float theta, float* __restrict__ k_cache,
                                                       float* __restrict__ v_cache) {
   extern __shared__ float cs[];  // [d/2] cos, then [d/2] sin
@@ -81,19 +82,21 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(float* __restrict__ q, con
   for (int i = threadIdx.x; i < (heads + kv_heads) * half; i += blockDim.x) {
     const int head = i / half, j = i % half;
     const float c = cs[j], s = cs[half + j];
+    const float* row = qkv + (size_t)t * ld;
     if (head < heads) {
-      float* qh = q + ((size_t)t * heads + head) * d;
+      const float* qh = row + (size_t)head * d;
+      float* qo = q_out + ((size_t)t * heads + head) * d;
       const float a = qh[j], b = qh[j + half];
-      qh[j] = a * c - b * s;
-      qh[j + half] = b * c + a * s;
+      qo[j] = a * c - b * s;
+      qo[j + half] = b * c + a * s;
     } else {
       const int kh = head - heads;
-      const float* kr = k + ((size_t)t * kv_heads + kh) * d;
+      const float* kr = row + (size_t)(heads + kh) * d;
       float* kc = k_cache + ((size_t)(pos0 + t) * kv_heads + kh) * d;
       const float a = kr[j], b = kr[j + half];
       kc[j] = a * c - b * s;
       kc[j + half] = b * c + a * s;
-      const float* vr = v + ((size_t)t * kv_heads + kh) * d;
+      const float* vr = row + (size_t)(heads + kv_heads + kh) * d;
       float* vc = v_cache + ((size_t)(pos0 + t) * kv_heads + kh) * d;
       vc[j] = vr[j];
       vc[j + half] = vr[j + half];
@@ -139,7 +142,7 @@ extern "C" int er_rms_norm(const float* x, const float* add, const float* weight
                         weight, eps, hidden, x_out, h);
 }
 
-extern "C" int er_rope_kv(float* q, const float* k, const float* v, int n, int heads, int kv_heads, int head_dim,
+extern "C" int er_rope_kv(const float* qkv, long long ld, float* q_out, int n, int heads, int kv_heads, int head_dim,
                           int pos0, float theta, float* k_cache, float* v_cache, int max_seq, void* stream) {
   if (n < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || head_dim % 2 || pos0 < 0)
     return fail(ER_EINVAL, "er_rope_kv: n %d, heads %d / %d, head_dim %d, pos0 %d", n, heads, kv_heads, head_dim,
@@ -147,10 +150,12 @@ extern "C" int er_rope_kv(float* q, const float* k, const float* v, int n, int h
   if (pos0 + n > max_seq)
     return fail(ER_EINVAL, "sequence length %d exceeds the KV cache (%d)", pos0 + n, max_seq);
   if (n == 0) return ER_OK;
-  if (!q || !k || !v || !k_cache || !v_cache) return fail(ER_EINVAL, "er_rope_kv: null argument");
+  if (!qkv || !q_out || !k_cache || !v_cache) return fail(ER_EINVAL, "er_rope_kv: null argument");
+  if (ld < (long long)(heads + 2 * kv_heads) * head_dim)
+    return fail(ER_EINVAL, "er_rope_kv: row stride %lld shorter than q|k|v (%d)", ld, (heads + 2 * kv_heads) * head_dim);
   if (head_dim > 8192) return fail(ER_EINVAL, "er_rope_kv: head_dim %d above 8192", head_dim);
   return launch_chained(rope_kv_kernel, dim3(n), dim3(256), (size_t)head_dim * sizeof(float), (cudaStream_t)stream,
-                        "rope_kv_kernel", q, k, v, heads, kv_heads, head_dim, pos0, theta, k_cache, v_cache);
+                        "rope_kv_kernel", qkv, ld, q_out, heads, kv_heads, head_dim, pos0, theta, k_cache, v_cache);
 }
 
 extern "C" int er_embed_int8(const int8_t* q, const float* scales, long long vocab, int hidden, const int64_t* ids,

@@ -107,10 +107,12 @@ class QwenMoeModel:
         self.layers = []
         for lay in host.layers:
             w = {"in_norm": _dev(lay.input_norm, torch.float32, dev), "post_norm": _dev(lay.post_norm, torch.float32, dev)}
-            for m, (q, s) in lay.proj.items():
-                w[m] = (_dev(q, torch.int8, dev), _dev(s, torch.float32, dev))
-            for m, b in lay.bias.items():
-                w[m + "_bias"] = _dev(b, torch.float32, dev)
+            # q, k and v as one projection (rows stacked: one weight stream, one launch)
+            qkv = ("q_proj", "k_proj", "v_proj")
+            w["qkv"] = (_dev(np.concatenate([lay.proj[m][0] for m in qkv]), torch.int8, dev),
+                        _dev(np.concatenate([lay.proj[m][1] for m in qkv]), torch.float32, dev))
+            w["qkv_bias"] = _dev(np.concatenate([lay.bias[m] for m in qkv]), torch.float32, dev)
+            w["o_proj"] = (_dev(lay.proj["o_proj"][0], torch.int8, dev), _dev(lay.proj["o_proj"][1], torch.float32, dev))
             self.layers.append(w)
         if records is None:
             records = HostRecords.from_blocks(host.blocks)
@@ -154,12 +156,11 @@ class QwenMoeModel:
     def _attention(self, layer: int, h: torch.Tensor, kv: KVCache, allowed: torch.Tensor) -> torch.Tensor:
         c, w = self.c, self.layers[layer]
         n, d = h.shape[0], c.head_dim
-        q = self._linear(h, w["q_proj"], w["q_proj_bias"])
-        k = self._linear(h, w["k_proj"], w["k_proj_bias"])
-        v = self._linear(h, w["v_proj"], w["v_proj_bias"])
+        qkv = self._linear(h, w["qkv"], w["qkv_bias"])
+        q = torch.empty((n, c.num_heads * d), dtype=torch.float32, device=self.device)
         start, end = kv.length, kv.length + n
-        _lib.check(_lib.lib().er_rope_kv(q.data_ptr(), k.data_ptr(), v.data_ptr(), n, c.num_heads, c.num_kv_heads, d,
-                                         start, c.rope_theta, kv.k[layer].data_ptr(), kv.v[layer].data_ptr(),
+        _lib.check(_lib.lib().er_rope_kv(qkv.data_ptr(), qkv.shape[1], q.data_ptr(), n, c.num_heads, c.num_kv_heads,
+                                         d, start, c.rope_theta, kv.k[layer].data_ptr(), kv.v[layer].data_ptr(),
                                          kv.max_seq, self._stream()), "er_rope_kv")
         keys, values = kv.k[layer, :end], kv.v[layer, :end]
         if c.num_kv_heads != c.num_heads:

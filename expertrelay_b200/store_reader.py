@@ -72,7 +72,7 @@ def write_expert_store(store_dir, layout: RecordLayout, records: dict[tuple[int,
     store_dir.mkdir(parents=True, exist_ok=True)
     rs = layout.record_size
     entries = []
-    end = max(expert_offset(l, e, num_experts, rs) + rs for l, e in records) if records else 0
+    end = max(expert_offset(lay, e, num_experts, rs) + rs for lay, e in records) if records else 0
     with open(store_dir / EXPERTS_BIN, "wb") as f:
         f.truncate(end)
         for (layer, expert), rec in sorted(records.items()):
@@ -192,7 +192,7 @@ def load_host_records(store_dir, *, layers: int | None = None, pinned: bool = Tr
     layout, entries = read_expert_index(store_dir / EXPERTS_INDEX)
     nl = layers if layers is not None else max(e.layer for e in entries) + 1
     ne = max(e.expert for e in entries) + 1
-    want = {(l, x) for l in range(nl) for x in range(ne)}
+    want = {(lay, x) for lay in range(nl) for x in range(ne)}
     have = {(e.layer, e.expert): e for e in entries}
     if want - set(have):
         missing = sorted(want - set(have))[:4]
@@ -201,7 +201,7 @@ def load_host_records(store_dir, *, layers: int | None = None, pinned: bool = Tr
     buf = aligned_host_buffer(nl * ne * rs, pinned=pinned)
     keys = sorted(want)
     offsets = (C.c_uint64 * len(keys))(*[have[k].offset for k in keys])
-    dsts = (C.c_void_p * len(keys))(*[buf.data_ptr() + (l * ne + x) * rs for l, x in keys])
+    dsts = (C.c_void_p * len(keys))(*[buf.data_ptr() + (lay * ne + x) * rs for lay, x in keys])
     st = _Store(store_dir / EXPERTS_BIN, direct)
     try:
         _lib.check(_lib.lib().er_store_read_many(st.handle, len(keys), offsets, rs, dsts, threads),

@@ -317,11 +317,12 @@ ER_API int er_trace_pack_layer(void* records, int n, int num_layers, int layer, 
 ER_API int er_rms_norm(const float* x, const float* add, const float* weight, float eps, int n, int hidden,
                        float* x_out, float* h, void* stream);
 /* RoPE (rope_tables and the rotation, :126-138, 255-256; inv_freq = 1 /
- * theta^(2i/d)) on q [n, heads, d] in place and on k [n, kv_heads, d], for
- * positions pos0 .. pos0 + n - 1; the rotated k and v [n, kv_heads, d] go to
- * rows pos0.. of the layer's caches [max_seq, kv_heads, d] (:264-270;
- * ER_EINVAL when pos0 + n > max_seq, like the reference's ValueError). */
-ER_API int er_rope_kv(float* q, const float* k, const float* v, int n, int heads, int kv_heads, int head_dim,
+ * theta^(2i/d)) for positions pos0 .. pos0 + n - 1. qkv: n rows (stride ld
+ * floats) of the fused projection [q heads*d | k kv_heads*d | v kv_heads*d];
+ * the rotated q goes to q_out [n, heads, d], the rotated k and the v to rows
+ * pos0.. of the layer's caches [max_seq, kv_heads, d] (:264-270; ER_EINVAL
+ * when pos0 + n > max_seq, like the reference's ValueError). */
+ER_API int er_rope_kv(const float* qkv, long long ld, float* q_out, int n, int heads, int kv_heads, int head_dim,
                       int pos0, float theta, float* k_cache, float* v_cache, int max_seq, void* stream);
 /* out[t] = q[ids[t]] * scales[ids[t]] (Int8Matrix.dequantized_rows,
  * runtime/weights.py:62-64); an id outside [0, vocab) sets *bad and a NaN row */
