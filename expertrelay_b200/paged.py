@@ -69,6 +69,12 @@ class PagedMoeStack:
         rc = _lib.lib().er_router_topk(logits.data_ptr(), n, self.num_experts, self.top_k, idx.data_ptr(), None,
                                        wts.data_ptr(), stream)
         _lib.check(rc, "er_router_topk")
+        has_next = layer + 1 < len(self.layers)
+        fate = None
+        if (self.prefetch_enabled or trace is not None) and has_next:
+            # the next layer's router on this layer's input (the Fate guess),
+            # queued before the ids are read back so one wait covers both
+            fate = self.layers[layer + 1].router_logits(h)
         needed = np.unique(idx.cpu().numpy())  # the host decides which records to fetch
         addrs = cache.acquire(layer, needed)
         table = self._table_host[layer].numpy().view(np.uint64)
@@ -76,11 +82,6 @@ class PagedMoeStack:
         table[needed] = addrs
         blk.use_arena(cache.arena_base, cache.num_slots)
         blk.set_expert_table(self._table_host[layer])
-        has_next = layer + 1 < len(self.layers)
-        fate = None
-        if (self.prefetch_enabled or trace is not None) and has_next:
-            # the next layer's router on this layer's input (the Fate guess)
-            fate = self.layers[layer + 1].router_logits(h)
         if self.prefetch_enabled and has_next:
             choice = self.prefetcher.choose(fate.cpu().numpy())
             self.prefetches_skipped_low_confidence += choice.skipped_low_confidence
