@@ -21,6 +21,11 @@ and the rest paged from pinned host memory with the Fate prefetch
 (--no-full-model skips it; --model-layers, --prompt-tokens, --new-tokens,
 --cache-frac size it).
 
+On every N the line carries `expert_parallel`: the MoE layer of the
+expert-parallel prefill (32 x 2048 tokens split over the N ranks, the 60
+experts spread over the GPUs, NCCL all-to-all of rows and results), timed
+as max over ranks (--no-ep skips it).
+
 --impl reference times the CPU implementation of the path (the oracle, a
 restatement of the reference's numpy/BLAS code) on this host's cores on the
 same workload; under torchrun only rank 0 runs it.
@@ -66,6 +71,10 @@ def parse_args():
     ap.add_argument("--prompt-tokens", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=128)
     ap.add_argument("--cache-frac", type=float, default=0.25, help="HBM expert-cache share of the routed records")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel layer measurement")
+    ap.add_argument("--ep-tokens", type=int, default=65536, help="tokens of the expert-parallel layer (all ranks)")
+    ap.add_argument("--ep-microbatch", type=int, default=4096)
+    ap.add_argument("--ep-steps", type=int, default=10)
     return ap.parse_args()
 
 
@@ -507,6 +516,8 @@ def main() -> None:
         line["decode"] = decode_side(args, dev, mb, block, peaks, peak_src)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(block, x, args.cpu_seconds)
+    if not args.no_ep:
+        line["expert_parallel"] = expert_parallel_side(args, dev, block, world, rank, flush)
     if rank == 0 and world == 1 and not args.no_full_model:
         del mb
         torch.cuda.empty_cache()
@@ -519,6 +530,94 @@ def main() -> None:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict:
+    """The MoE layer of the expert-parallel prefill workload: 32 sequences x
+    2048 tokens (65,536, --ep-tokens) split evenly over the ranks (the total
+    is fixed: strong scaling), bf16 activations, the block's router without
+    the Zipf scaling (a random-init model routes near-uniformly). The 60
+    experts are spread contiguously over the ranks (30/30, 15 x 4,
+    8,8,8,8,7,7,7,7) and each rank runs ExpertParallelMoe on the tensor-core
+    path: all-to-all of counts, of the rows (bf16) with their expert ids and
+    weights, the owner's experts, all-to-all of the results (fp32) back, the
+    gated shared expert and the ordered combine. A rank processes its tokens
+    in microbatches of --ep-microbatch. Every rank takes the same collective
+    steps; a failure while building is agreed on first, so that no rank
+    waits in a collective for one that gave up."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+
+    from expertrelay_b200 import _lib
+    from expertrelay_b200.ep import EpCudaOps, ExpertParallelMoe, expert_partition
+
+    total, mbatch = args.ep_tokens, args.ep_microbatch
+    per = total // world
+    chunks = max(1, per // mbatch)
+    err = None
+    try:
+        if per % mbatch:
+            raise ValueError(f"{per} tokens per rank are not a multiple of the {mbatch}-token microbatch")
+        ep_block = dataclasses.replace(block, router=block.meta.get("router_base", block.router), meta={})
+        ep = ExpertParallelMoe(EpCudaOps(ep_block, rank, world, dev, _lib.PATH_TC))
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(args.seed * 1000 + 577 + rank)
+        h = torch.randn((per, block.hidden), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    except (RuntimeError, ValueError, MemoryError) as e:
+        err = f"{type(e).__name__}: {e}"[:300]
+    bad = torch.tensor([1 if err else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+    if int(bad.item()):
+        return {"error": err or "another rank failed to set up"}
+
+    def step(stats=None):
+        for c in range(chunks):
+            ep(h[c * mbatch:(c + 1) * mbatch])
+            if stats is not None:
+                send, recv = ep.last_counts
+                stats[0] += sum(v for r, v in enumerate(send) if r != rank)
+                stats[1] += sum(recv)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    steps = max(3, min(args.steps, args.ep_steps))
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stats = [0, 0]  # rows this rank sent to other ranks, rows it computed
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        step(stats if i == 0 else None)
+        ends[i].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(starts, ends)), stats[1]], dtype=torch.float64,
+                     device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0].item()) / steps
+    row_out = block.hidden * 2 + 8  # bf16 row + expert id + weight
+    return {
+        "workload": (f"MoE layer of the expert-parallel prefill: {total} tokens (32 x 2048) over {world} GPU(s), "
+                     f"{per} per rank in {chunks} microbatch(es) of {mbatch}; int8 experts, bf16 activations, "
+                     f"near-uniform routing"),
+        "value": total / (ms / 1e3),
+        "unit": "tokens/s",
+        "ms_per_step": ms,
+        "steps": steps,
+        "scaling": "strong",
+        "experts_per_rank": [hi - lo for lo, hi in expert_partition(block.num_experts, world)],
+        "rows_computed_max_rank": int(t[1].item()),
+        "rank0_bytes_sent_per_step": int(stats[0] * row_out),
+        "rank0_bytes_returned_per_step": int(stats[0] * block.hidden * 4),
+        "collectives": "NCCL all_to_all_single: counts, rows + ids + weights, results" if world > 1 else "none",
+        "timing": "CUDA events around each step (host waits for the counts included), max over ranks, L2 flushed",
+    }
 
 
 def full_model_side(args, dev) -> dict:

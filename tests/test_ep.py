@@ -1,6 +1,6 @@
 """Expert parallelism, host side: the expert partition and the exchange of
-ExpertParallelMoe (counts, rows out, results back, combine) on two gloo
-ranks on the CPU.
+ExpertParallelMoe (counts, rows out, results back, combine) on two and four
+gloo ranks on the CPU.
 
 The per-rank steps run on the host here (HostOps, built on the oracle), with
 the same contracts as the CUDA steps (expertrelay_b200.ep.EpCudaOps): rows of
@@ -125,7 +125,7 @@ def _rank_main(rank: int, world: int, port: int, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_exchange_on_gloo_matches_the_whole_block(world):
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
@@ -136,5 +136,7 @@ def test_exchange_on_gloo_matches_the_whole_block(world):
     for rank, (err, (send, recv)) in res.items():
         assert err < 1e-5, f"rank {rank}: rel-L2 {err:.2e}"
         assert sum(send) == (5 + 7 * rank) * SHAPE["top_k"]
-    # what rank 0 sent to rank 1 is what rank 1 received from rank 0
-    assert res[0][1][0][1] == res[1][1][1][0] and res[1][1][0][0] == res[0][1][1][1]
+    # what rank a sent to rank b is what rank b received from rank a
+    for a in range(world):
+        for b in range(world):
+            assert res[a][1][0][b] == res[b][1][1][a], f"rank {a} -> rank {b}"

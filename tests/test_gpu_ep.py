@@ -31,12 +31,13 @@ def _expected(block, h, path, device):
     return mb.forward(h, logits=mb.router_logits(h), path=path)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("path", list(PATHS))
-def test_one_rank_equals_the_block(cuda, path):
+def test_one_rank_equals_the_block(cuda, path, dtype):
     block = synth.make_block(4, num_experts=16)
     ep = ExpertParallelMoe(EpCudaOps(block, 0, 1, cuda, PATHS[path]))
     for n in (3, 40, 300):
-        h = torch.from_numpy(synth.make_tokens(60 + n, n)).to(cuda)
+        h = torch.from_numpy(synth.make_tokens(60 + n, n)).to(cuda).to(dtype)
         y = ep(h)
         ref = _expected(block, h, PATHS[path], cuda)
         torch.cuda.synchronize()
@@ -56,15 +57,17 @@ def _rank_main(rank: int, world: int, port: int):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
     try:
         block = synth.make_block(4)  # Qwen shapes: 60 experts, 30 per rank
-        for path in (_lib.PATH_TC, _lib.PATH_GEMV):
+        for path, dtype in ((_lib.PATH_TC, torch.float32), (_lib.PATH_GEMV, torch.float32),
+                            (_lib.PATH_TC, torch.bfloat16)):
             ep = ExpertParallelMoe(EpCudaOps(block, rank, world, dev, path))
             for n in (8, 96 + 32 * rank):  # ragged across ranks
-                h = torch.from_numpy(synth.make_tokens(70 + 10 * rank + n, n)).to(dev)
+                h = torch.from_numpy(synth.make_tokens(70 + 10 * rank + n, n)).to(dev).to(dtype)
                 y = ep(h)
                 ref = _expected(block, h, path, dev)
                 torch.cuda.synchronize()
                 if not torch.equal(y, ref):
-                    raise AssertionError(f"rank {rank} path {path} n={n}: max diff {(y - ref).abs().max().item()}")
+                    diff = (y - ref).abs().max().item()
+                    raise AssertionError(f"rank {rank} path {path} {dtype} n={n}: max diff {diff}")
         dist.barrier()
     finally:
         dist.destroy_process_group()
