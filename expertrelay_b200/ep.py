@@ -14,7 +14,9 @@ replicated router, shared gate and shared expert. Per layer, on each rank:
   4. compute the received rows with its own experts (er_moe_rows);
   5. send the results back (all-to-all), the reverse of 3;
   6. add each token's slots in ascending expert id, plus the gated shared
-     expert computed locally (er_moe_shared, er_moe_combine).
+     expert computed locally (er_moe_shared, er_moe_combine); the shared
+     expert needs only the rank's own tokens, so it is queued right after
+     routing and, on GPUs, runs on a side stream beside steps 2-5.
 
 Every routed row's result depends only on that row, and the combine adds in
 the reference's order, so the output equals the single-GPU block's on the
@@ -98,7 +100,12 @@ class EpCudaOps:
             arena_slots=n_local if block.layout.fmt == FMT_INT8 else 0,
         )
         self.cursor = torch.zeros(ranks, dtype=torch.int32, device=self.device)
-        self._ws: torch.Tensor | None = None
+        self._ws: torch.Tensor | None = None  # the routed rows' workspace
+        # the shared expert runs on a side stream, beside the exchange and the
+        # routed rows, with a workspace of its own
+        self._ws_shared: torch.Tensor | None = None
+        self._side = torch.cuda.Stream(self.device)
+        self._shared_done = torch.cuda.Event()
 
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
@@ -152,20 +159,33 @@ class EpCudaOps:
         return y
 
     def shared(self, h: torch.Tensor) -> torch.Tensor:
+        """The gated shared expert of this rank's tokens, queued on a side
+        stream after the work already queued for h, so that it overlaps the
+        exchange and the routed rows; combine() waits for it."""
         n = h.shape[0]
         y = torch.empty((n, self.hidden), dtype=torch.float32, device=self.device)
         if n == 0:
             return y
         w = self.full._w
-        ws = self._workspace(_lib.lib().er_moe_shared_workspace_bytes(C.byref(w), n, self.path))
+        nbytes = _lib.lib().er_moe_shared_workspace_bytes(C.byref(w), n, self.path)
+        if self._ws_shared is None or self._ws_shared.numel() < nbytes:
+            self._side.synchronize()  # the old workspace may still be in use there
+            self._ws_shared = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        ws = self._ws_shared
+        self._side.wait_stream(torch.cuda.current_stream(self.device))
         dtype = _lib.DTYPE_BF16 if h.dtype == torch.bfloat16 else _lib.DTYPE_F32
         _lib.check(_lib.lib().er_moe_shared(C.byref(w), h.data_ptr(), dtype, n, y.data_ptr(), self.path,
-                                            ws.data_ptr(), ws.numel(), self._stream()), "er_moe_shared")
+                                            ws.data_ptr(), ws.numel(), self._side.cuda_stream), "er_moe_shared")
+        self._shared_done.record(self._side)
+        # the caching allocator must not hand these to other work before the side stream is done
+        y.record_stream(self._side)
+        h.record_stream(self._side)
         return y
 
     def combine(self, y_ret, pos_of, idx, y_s) -> torch.Tensor:
         n = idx.shape[0]
         y = torch.empty((n, self.hidden), dtype=torch.float32, device=self.device)
+        torch.cuda.current_stream(self.device).wait_event(self._shared_done)
         _lib.check(_lib.lib().er_moe_combine(y_ret.data_ptr() if y_ret.numel() else None, pos_of.data_ptr(),
                                              idx.data_ptr(), y_s.data_ptr(), n, self.top_k, self.hidden,
                                              y.data_ptr(), self._stream()), "er_moe_combine")
@@ -194,14 +214,21 @@ class ExpertParallelMoe:
     def forward(self, h):
         ops = self.ops
         _, idx, w = ops.route(h)
+        # the shared expert needs only h: queued first (the CUDA steps run it
+        # on a side stream, overlapping everything up to the combine)
+        y_s = ops.shared(h)
         counts = ops.count(idx)
-        recv_counts = torch.empty_like(counts)
-        self._a2a(recv_counts, counts, None, None)
+        recv_counts = counts
+        if self.ranks > 1:
+            recv_counts = torch.empty_like(counts)
+            self._a2a(recv_counts, counts, None, None)
         send = [int(c) for c in counts.cpu().tolist()]
         recv = [int(c) for c in recv_counts.cpu().tolist()]
         self.last_counts = (send, recv)
         offsets = torch.tensor(np.concatenate([[0], np.cumsum(send)[:-1]]).astype(np.int32), device=counts.device)
         x_send, e_send, w_send, pos_of = ops.pack(h, idx, w, offsets, sum(send))
+        if self.ranks == 1:  # nothing to exchange: the packed rows are the received rows
+            return ops.combine(ops.rows(x_send, e_send, w_send), pos_of, idx, y_s)
         hidden = x_send.shape[1]
         x_recv = torch.empty((sum(recv), hidden), dtype=x_send.dtype, device=x_send.device)
         e_recv = torch.empty(sum(recv), dtype=e_send.dtype, device=e_send.device)
@@ -212,7 +239,6 @@ class ExpertParallelMoe:
         y_recv = ops.rows(x_recv, e_recv, w_recv)
         y_ret = torch.empty((sum(send), hidden), dtype=y_recv.dtype, device=y_recv.device)
         self._a2a(y_ret, y_recv, send, recv)
-        y_s = ops.shared(h)
         return ops.combine(y_ret, pos_of, idx, y_s)
 
     __call__ = forward
