@@ -542,7 +542,8 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
     path: all-to-all of counts, of the rows (bf16) with their expert ids and
     weights, the owner's experts, all-to-all of the results (fp32) back, the
     gated shared expert and the ordered combine. A rank processes its tokens
-    in microbatches of --ep-microbatch. Every rank takes the same collective
+    in microbatches of --ep-microbatch (ExpertParallelMoe.forward_many: all
+    microbatches routed and counted, then one read-back of the counts). Every rank takes the same collective
     steps; a failure while building is agreed on first, so that no rank
     waits in a collective for one that gave up."""
     import dataclasses
@@ -573,13 +574,14 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
     if int(bad.item()):
         return {"error": err or "another rank failed to set up"}
 
+    parts = [h[c * mbatch:(c + 1) * mbatch] for c in range(chunks)]
+
     def step(stats=None):
-        for c in range(chunks):
-            ep(h[c * mbatch:(c + 1) * mbatch])
-            if stats is not None:
-                send, recv = ep.last_counts
-                stats[0] += sum(v for r, v in enumerate(send) if r != rank)
-                stats[1] += sum(recv)
+        ep.forward_many(parts)
+        if stats is not None:
+            send, recv = ep.last_counts
+            stats[0] += sum(v for r, v in enumerate(send) if r != rank)
+            stats[1] += sum(recv)
 
     for _ in range(max(args.warmup, 3)):
         step()

@@ -105,7 +105,6 @@ class EpCudaOps:
         # routed rows, with a workspace of its own
         self._ws_shared: torch.Tensor | None = None
         self._side = torch.cuda.Stream(self.device)
-        self._shared_done = torch.cuda.Event()
 
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
@@ -176,7 +175,9 @@ class EpCudaOps:
         dtype = _lib.DTYPE_BF16 if h.dtype == torch.bfloat16 else _lib.DTYPE_F32
         _lib.check(_lib.lib().er_moe_shared(C.byref(w), h.data_ptr(), dtype, n, y.data_ptr(), self.path,
                                             ws.data_ptr(), ws.numel(), self._side.cuda_stream), "er_moe_shared")
-        self._shared_done.record(self._side)
+        done = torch.cuda.Event()
+        done.record(self._side)
+        y.er_ready = done  # what combine() waits for
         # the caching allocator must not hand these to other work before the side stream is done
         y.record_stream(self._side)
         h.record_stream(self._side)
@@ -185,7 +186,9 @@ class EpCudaOps:
     def combine(self, y_ret, pos_of, idx, y_s) -> torch.Tensor:
         n = idx.shape[0]
         y = torch.empty((n, self.hidden), dtype=torch.float32, device=self.device)
-        torch.cuda.current_stream(self.device).wait_event(self._shared_done)
+        ready = getattr(y_s, "er_ready", None)
+        if ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(ready)
         _lib.check(_lib.lib().er_moe_combine(y_ret.data_ptr() if y_ret.numel() else None, pos_of.data_ptr(),
                                              idx.data_ptr(), y_s.data_ptr(), n, self.top_k, self.hidden,
                                              y.data_ptr(), self._stream()), "er_moe_combine")
@@ -212,20 +215,41 @@ class ExpertParallelMoe:
             dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
     def forward(self, h):
+        return self.forward_many([h])[0]
+
+    __call__ = forward
+
+    def forward_many(self, hs):
+        """forward() over several microbatches of this rank's tokens (every
+        rank passes the same number), with one host wait for all of their
+        counts: each microbatch is routed, its shared expert queued (the CUDA
+        steps run it on a side stream, overlapping everything up to its
+        combine) and its rows counted before the counts are read back, so the
+        device does not idle while the host reads each microbatch's counts.
+        last_counts then holds the rows sent to / received from each rank,
+        summed over the microbatches."""
         ops = self.ops
-        _, idx, w = ops.route(h)
-        # the shared expert needs only h: queued first (the CUDA steps run it
-        # on a side stream, overlapping everything up to the combine)
-        y_s = ops.shared(h)
-        counts = ops.count(idx)
+        routed = []
+        for h in hs:
+            _, idx, w = ops.route(h)
+            routed.append((h, idx, w, ops.shared(h), ops.count(idx)))
+        if not routed:
+            return []
+        # counts[j, r]: microbatch j's rows for rank r; exchanged as [r, j]
+        counts = torch.stack([r[4] for r in routed]).t().contiguous()
         recv_counts = counts
         if self.ranks > 1:
             recv_counts = torch.empty_like(counts)
             self._a2a(recv_counts, counts, None, None)
-        send = [int(c) for c in counts.cpu().tolist()]
-        recv = [int(c) for c in recv_counts.cpu().tolist()]
-        self.last_counts = (send, recv)
-        offsets = torch.tensor(np.concatenate([[0], np.cumsum(send)[:-1]]).astype(np.int32), device=counts.device)
+        send_all = counts.cpu().numpy().T.astype(np.int64)  # [microbatch, rank]
+        recv_all = recv_counts.cpu().numpy().T.astype(np.int64)
+        self.last_counts = ([int(v) for v in send_all.sum(0)], [int(v) for v in recv_all.sum(0)])
+        return [self._exchange(h, idx, w, y_s, [int(v) for v in send], [int(v) for v in recv])
+                for (h, idx, w, y_s, _), send, recv in zip(routed, send_all, recv_all)]
+
+    def _exchange(self, h, idx, w, y_s, send, recv):
+        ops = self.ops
+        offsets = torch.tensor(np.concatenate([[0], np.cumsum(send)[:-1]]).astype(np.int32), device=idx.device)
         x_send, e_send, w_send, pos_of = ops.pack(h, idx, w, offsets, sum(send))
         if self.ranks == 1:  # nothing to exchange: the packed rows are the received rows
             return ops.combine(ops.rows(x_send, e_send, w_send), pos_of, idx, y_s)
@@ -240,5 +264,3 @@ class ExpertParallelMoe:
         y_ret = torch.empty((sum(send), hidden), dtype=y_recv.dtype, device=y_recv.device)
         self._a2a(y_ret, y_recv, send, recv)
         return ops.combine(y_ret, pos_of, idx, y_s)
-
-    __call__ = forward

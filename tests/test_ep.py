@@ -120,7 +120,16 @@ def _rank_main(rank: int, world: int, port: int, results):
         ep = ExpertParallelMoe(HostOps(block, rank, world))
         y = ep(h).numpy()
         ref = O.moe_block(h.numpy(), oracle_weights(block)).y
-        results[rank] = (O.rel_l2(y, ref), ep.last_counts)
+        counts = ep.last_counts
+        # several microbatches with one count exchange; one of them empty on rank 0
+        parts = [torch.from_numpy(synth.make_tokens(40 + rank + j, m, SHAPE["hidden"]))
+                 for j, m in enumerate((3 + rank, 0 if rank == 0 else 2, 6))]
+        many = ep.forward_many(parts)
+        err_many = max(O.rel_l2(y_j.numpy(), O.moe_block(p.numpy(), oracle_weights(block)).y)
+                       for y_j, p in zip(many, parts) if p.shape[0])
+        assert all(y_j.shape == p.shape for y_j, p in zip(many, parts))
+        assert sum(ep.last_counts[0]) == sum(p.shape[0] for p in parts) * SHAPE["top_k"]
+        results[rank] = (max(O.rel_l2(y, ref), err_many), counts)
     finally:
         dist.destroy_process_group()
 

@@ -36,12 +36,19 @@ def _expected(block, h, path, device):
 def test_one_rank_equals_the_block(cuda, path, dtype):
     block = synth.make_block(4, num_experts=16)
     ep = ExpertParallelMoe(EpCudaOps(block, 0, 1, cuda, PATHS[path]))
+    hs = []
     for n in (3, 40, 300):
         h = torch.from_numpy(synth.make_tokens(60 + n, n)).to(cuda).to(dtype)
         y = ep(h)
         ref = _expected(block, h, PATHS[path], cuda)
         torch.cuda.synchronize()
         assert torch.equal(y, ref), f"n={n}"
+        hs.append(h)
+    # the same batches as microbatches of one call (one count read-back)
+    for h, y in zip(hs, ep.forward_many(hs)):
+        ref = _expected(block, h, PATHS[path], cuda)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref), f"forward_many, n={h.shape[0]}"
 
 
 def _free_port() -> int:
@@ -68,6 +75,13 @@ def _rank_main(rank: int, world: int, port: int):
                 if not torch.equal(y, ref):
                     diff = (y - ref).abs().max().item()
                     raise AssertionError(f"rank {rank} path {path} {dtype} n={n}: max diff {diff}")
+            hs = [torch.from_numpy(synth.make_tokens(90 + 10 * rank + n, n)).to(dev).to(dtype)
+                  for n in (16, 200 + 24 * rank)]
+            for j, (h, y) in enumerate(zip(hs, ep.forward_many(hs))):
+                ref = _expected(block, h, path, dev)
+                torch.cuda.synchronize()
+                if not torch.equal(y, ref):
+                    raise AssertionError(f"rank {rank} path {path} {dtype} forward_many microbatch {j} differs")
         dist.barrier()
     finally:
         dist.destroy_process_group()
