@@ -117,9 +117,11 @@ class EpCudaOps:
     def route(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """(router logits [n, E], expert ids int32 [n, k], weights [n, k])."""
         n = h.shape[0]
-        logits = self.full.router_logits(h)
         idx = torch.empty((n, self.top_k), dtype=torch.int32, device=self.device)
         w = torch.empty((n, self.top_k), dtype=torch.float32, device=self.device)
+        if n == 0:  # an empty microbatch still takes part in the exchange
+            return torch.empty((0, self.num_experts), dtype=torch.float32, device=self.device), idx, w
+        logits = self.full.router_logits(h)
         _lib.check(_lib.lib().er_router_topk(logits.data_ptr(), n, self.num_experts, self.top_k, None,
                                              idx.data_ptr(), w.data_ptr(), self._stream()), "er_router_topk")
         return logits, idx, w
