@@ -642,14 +642,30 @@ def full_model_side(args, dev) -> dict:
     model = QwenMoeModel(host, records=records, cache_records=slots, prefetch=True, device=dev)
     prompt = np.random.default_rng(args.seed + 4242).integers(0, cfg["vocab_size"], args.prompt_tokens)
     model.generate(prompt[:16], 4)  # warm-up: kernels, allocator, cache bookkeeping
-    s0 = model.cache.stats
-    tokens, t_prompt, steps = model.generate(prompt, args.new_tokens)
-    s1 = model.cache.stats
+    keys = ("loads", "demand_reads", "cache_hits", "prefetch_hits", "prefetch_waits", "prefetches_issued",
+            "prefetch_reads", "prefetches_wasted", "prefetches_skipped_budget")
+
+    def run():
+        s0 = model.cache.stats
+        out = model.generate(prompt, args.new_tokens)
+        s1 = model.cache.stats
+        return out, {k: getattr(s1, k) - getattr(s0, k) for k in keys}
+
+    (tokens, t_prompt, steps), delta = run()
+    # the same generation with the adaptive read budget (prefetch copies capped per layer window)
+    model.stack.prefetch_adaptive = True
+    (tokens_a, _, steps_a), delta_a = run()
+    win = model.stack.window[:-1]
+    adaptive = {
+        "decode_tokens_per_s": (len(steps_a) / float(np.sum(steps_a))) if steps_a else None,
+        "ms_per_decode_token": float(np.sum(steps_a)) / max(len(steps_a), 1) * 1e3,
+        "same_tokens": tokens_a == tokens,
+        "record_copy_ms": model.stack.read_seconds * 1e3 if model.stack.read_seconds else None,
+        "window_ms_median": float(np.median(win[np.isfinite(win)])) * 1e3 if np.isfinite(win).any() else None,
+        "cache": delta_a,
+    }
     rs = model.records.layout.record_size
     dec_s = float(np.sum(steps))
-    delta = {k: getattr(s1, k) - getattr(s0, k) for k in ("loads", "demand_reads", "cache_hits", "prefetch_hits",
-                                                           "prefetch_waits", "prefetches_issued", "prefetch_reads",
-                                                           "prefetches_wasted")}
     model.close()
     return {
         "workload": (f"Qwen1.5-MoE-A2.7B shapes, random init, {cfg['num_hidden_layers']} layers, int8 experts; "
@@ -662,6 +678,7 @@ def full_model_side(args, dev) -> dict:
         "prompt_tokens_per_s": args.prompt_tokens / t_prompt,
         "expert_bytes_copied_GB": (delta["demand_reads"] + delta["prefetch_reads"]) * rs / 1e9,
         "cache": delta,
+        "adaptive_budget": adaptive,
         "build_s": t_build,
         "timing": "host wall clock around each generate() call (synchronous: argmax read back per token)",
     }

@@ -90,10 +90,13 @@ class QwenMoeModel:
     fields); records: the routed experts as [layers, experts, record_size]
     uint8 (pinned host memory; default: the host blocks' records);
     cache_records: HBM slots for routed records (default: all of them);
-    prefetch: the Fate policy's prefetch of the next layer's experts."""
+    prefetch: the Fate policy's prefetch of the next layer's experts;
+    prefetch_adaptive: cap the prefetch's copies on one-token calls at what
+    fits in each layer's measured window (runtime/generate.py:112)."""
 
     def __init__(self, host, *, records: torch.Tensor | None = None, cache_records: int | None = None,
-                 prefetch: bool = False, device="cuda", path: int = _lib.PATH_AUTO):
+                 prefetch: bool = False, prefetch_adaptive: bool = False, device="cuda",
+                 path: int = _lib.PATH_AUTO):
         if not torch.cuda.is_available():
             raise RuntimeError("QwenMoeModel needs a CUDA device (the B200 path has no CPU fallback)")
         self.device = dev = torch.device(device)
@@ -124,6 +127,7 @@ class QwenMoeModel:
         self.cache = HbmExpertCache(records, capacity_bytes=slots * rs, device=dev)
         policy = PrefetchPolicy(top_k=c.top_k) if prefetch else None
         self.stack = PagedMoeStack(host.blocks, self.cache, prefetcher=policy, norm_topk_prob=c.norm_topk_prob)
+        self.stack.prefetch_adaptive = prefetch_adaptive
         self._bad = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def close(self) -> None:

@@ -43,15 +43,20 @@ def test_model_matches_reference(case, path, cuda):
     model.close()
 
 
-@pytest.mark.parametrize("prefetch", [False, True])
+@pytest.mark.parametrize("prefetch", [False, True, "adaptive"])
 def test_small_cache_changes_nothing(prefetch, cuda):
     cfg, seed = MODEL_CASES[0]
     host = synth.make_model(cfg, seed=seed)
     g = golden("model")
     outs = []
     for slots, pf in ((None, False), (18, prefetch)):  # 18 slots for 48 records: layers evict each other
-        model = QwenMoeModel(host, device=cuda, cache_records=slots, prefetch=pf)
+        model = QwenMoeModel(host, device=cuda, cache_records=slots, prefetch=bool(pf),
+                             prefetch_adaptive=pf == "adaptive")
         tokens, _, _ = model.generate(g["prompt0"], MODEL_NEW)
+        if pf == "adaptive":  # the decode calls measured every layer's window and one copy's time
+            st = model.stack
+            assert np.isfinite(st.window[:-1]).all() and (st.window[:-1] > 0).all()
+            assert st.read_seconds is not None and 0 < st.read_seconds < 0.1
         kv = model.new_cache(MODEL_PROMPT + 1)
         outs.append((tokens, model.forward(g["prompt0"], kv, all_logits=True).cpu()))
         model.close()

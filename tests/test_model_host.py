@@ -55,3 +55,21 @@ def test_oracle_decode_calls_equal_one_call():
     steps = [o.forward([int(t)], kv2) for t in ids[3:]]
     for i, lg in enumerate(steps):
         np.testing.assert_allclose(lg, full[3 + i], rtol=2e-5, atol=2e-5)
+
+
+def test_read_budget_and_window_follow_the_runtime():
+    """The adaptive prefetch cap (runtime/qwen_moe.py:361-374): top_k until a
+    window is measured, then window / copy time rounded, at least one; the
+    window is a running average with weight 0.5 on the newest call."""
+    from expertrelay_b200.paged import WINDOW_EMA, read_budget, update_window
+
+    assert WINDOW_EMA == 0.5
+    assert read_budget(float("nan"), 1.6e-4, 4) == 4
+    assert read_budget(5e-4, 1.6e-4, 4) == 3  # 3.125 copies fit
+    assert read_budget(3.0, 2.0, 4) == 2 and read_budget(5.0, 2.0, 4) == 2  # Python's round: halves to even
+    assert read_budget(1e-6, 1.6e-4, 4) == 1  # always at least one
+    assert read_budget(1.0, 1.6e-4, 4) == 6250  # the budget is not capped at top_k
+    w = float("nan")
+    for new, want in ((2e-4, 2e-4), (4e-4, 3e-4), (4e-4, 3.5e-4)):
+        w = update_window(w, new)
+        assert w == pytest.approx(want)
