@@ -1,0 +1,40 @@
+"""bench.py's reference arm on the CPU: one JSON line with the contract's
+keys from rank 0, nothing (and exit status 0) from any other rank."""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _run(env_extra):
+    env = dict(os.environ, **env_extra)
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "decode8_int8",
+           "--steps", "1", "--warmup", "0"]
+    return subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+
+
+def test_reference_arm_prints_one_contract_line():
+    p = _run({"RANK": "0"})
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [ln for ln in p.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["value"] > 0 and line["higher_is_better"] is True
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
+    assert line["config"]["workload"] == "decode8_int8"
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    p = _run({"RANK": "1"})
+    assert p.returncode == 0, p.stderr[-2000:]
+    assert p.stdout.strip() == ""
