@@ -149,7 +149,7 @@ SIGNATURES: dict[str, tuple] = {
     "er_store_close": (_i, [_vp]),
     "er_store_info": (_i, [_vp, C.POINTER(C.c_uint64), C.POINTER(_i)]),
     "er_store_read": (_i, [_vp, C.c_uint64, C.c_uint64, _vp]),
-    "er_store_read_many": (_i, [_vp, _i, _vp, C.c_uint64, _vp, _i]),
+    "er_store_read_many": (_i, [_vp, _i, _vp, C.c_uint64, _vp, _i, _vp]),
     "er_trace_pack_layer": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _vp]),
 }
 

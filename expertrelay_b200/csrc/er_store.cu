@@ -110,18 +110,24 @@ extern "C" int er_store_read(er_store* s, uint64_t offset, uint64_t nbytes, void
 }
 
 extern "C" int er_store_read_many(er_store* s, int count, const uint64_t* offsets, uint64_t nbytes,
-                                  void* const* dsts, int threads) {
+                                  void* const* dsts, int threads, int* failed) {
+  if (failed) *failed = -1;
   if (!s || count < 0 || (count > 0 && (!offsets || !dsts)))
     return fail(ER_EINVAL, "er_store_read_many: bad arguments (count %d)", count);
   for (int i = 0; i < count; ++i)  // every read checked before any starts
-    if (offsets[i] % kStoreAlign || nbytes % kStoreAlign || (uintptr_t)dsts[i] % kStoreAlign)
+    if (offsets[i] % kStoreAlign || nbytes % kStoreAlign || (uintptr_t)dsts[i] % kStoreAlign) {
+      if (failed) *failed = i;
       return fail(ER_EINVAL, "unaligned unbuffered read: offset=%llu nbytes=%llu address=%p",
                   (unsigned long long)offsets[i], (unsigned long long)nbytes, dsts[i]);
+    }
   if (threads < 1) threads = 1;
   if (threads > count) threads = count;
   if (threads <= 1) {
     for (int i = 0; i < count; ++i)
-      if (int rc = store_read_one(s, offsets[i], nbytes, dsts[i])) return rc;
+      if (int rc = store_read_one(s, offsets[i], nbytes, dsts[i])) {
+        if (failed) *failed = i;
+        return rc;
+      }
     return ER_OK;
   }
   std::atomic<int> next{0};
@@ -144,6 +150,9 @@ extern "C" int er_store_read_many(er_store* s, int count, const uint64_t* offset
   for (int t = 0; t < threads; ++t) pool.emplace_back(worker);
   for (auto& t : pool) t.join();
   const int bad = first_bad.load();
-  if (bad >= 0) return fail(status[bad], "er_store_read_many: read %d: %s", bad, bad_msg.c_str());
+  if (bad >= 0) {
+    if (failed) *failed = bad;
+    return fail(status[bad], "er_store_read_many: read %d: %s", bad, bad_msg.c_str());
+  }
   return ER_OK;
 }

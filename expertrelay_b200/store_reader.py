@@ -203,9 +203,15 @@ def load_host_records(store_dir, *, layers: int | None = None, pinned: bool = Tr
     offsets = (C.c_uint64 * len(keys))(*[have[k].offset for k in keys])
     dsts = (C.c_void_p * len(keys))(*[buf.data_ptr() + (lay * ne + x) * rs for lay, x in keys])
     st = _Store(store_dir / EXPERTS_BIN, direct)
+    failed = C.c_int(-1)
     try:
-        _lib.check(_lib.lib().er_store_read_many(st.handle, len(keys), offsets, rs, dsts, threads),
-                   "er_store_read_many")
+        rc = _lib.lib().er_store_read_many(st.handle, len(keys), offsets, rs, dsts, threads, C.byref(failed))
+        try:
+            _lib.check(rc, "er_store_read_many")
+        except (OSError, ValueError) as e:
+            if 0 <= failed.value < len(keys):  # name the expert, as the reference's cache does
+                raise RuntimeError(f"background read of expert {keys[failed.value]} failed") from e
+            raise
     finally:
         st.close()
     return HostRecords(buf.view(nl, ne, rs), layout, pin=False)

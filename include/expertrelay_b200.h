@@ -341,9 +341,11 @@ ER_API int er_store_open(const char* path, int flags, er_store** out);
 ER_API int er_store_close(er_store* s);
 ER_API int er_store_info(const er_store* s, uint64_t* file_bytes, int* direct);
 ER_API int er_store_read(er_store* s, uint64_t offset, uint64_t nbytes, void* dst);
-/* count reads of nbytes each (offsets[i] -> dsts[i]) on up to `threads` threads */
+/* count reads of nbytes each (offsets[i] -> dsts[i]) on up to `threads` threads;
+ * on a failed read, *failed (when given) receives its index i, else -1, so the
+ * caller can name the expert whose read failed (cache/expert_cache.py:281-282) */
 ER_API int er_store_read_many(er_store* s, int count, const uint64_t* offsets, uint64_t nbytes, void* const* dsts,
-                              int threads);
+                              int threads, int* failed);
 
 #ifdef __cplusplus
 }

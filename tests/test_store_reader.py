@@ -101,6 +101,23 @@ def test_short_read_is_an_error(tmp_path):
 
 
 @pytest.mark.parametrize("threads", [1, 4])
+def test_failed_bulk_read_names_the_expert(tmp_path, threads):
+    """A record whose read comes up short fails the whole load with the
+    reference cache's error for a failed read (cache/expert_cache.py:
+    281-282): RuntimeError naming the (layer, expert) key, chained from the
+    read's OSError."""
+
+    def beyond(doc):
+        e = next(e for e in doc["entries"] if (e["layer"], e["expert"]) == (1, 2))
+        e["offset"] = 100 * 8192  # past the end of experts.bin
+
+    d = _index(tmp_path, beyond)
+    with pytest.raises(RuntimeError, match=r"background read of expert \(1, 2\) failed") as info:
+        load_host_records(d, pinned=False, threads=threads)
+    assert isinstance(info.value.__cause__, OSError) and "short read" in str(info.value.__cause__)
+
+
+@pytest.mark.parametrize("threads", [1, 4])
 def test_load_host_records(threads):
     blob = np.frombuffer((STORE / EXPERTS_BIN).read_bytes(), dtype=np.uint8)
     recs = load_host_records(STORE, pinned=False, threads=threads)
