@@ -21,6 +21,9 @@ and the rest paged from pinned host memory with the Fate prefetch
 (--no-full-model skips it; --model-layers, --prompt-tokens, --new-tokens,
 --cache-frac size it).
 
+On one GPU the line also carries `gptq`: the block with int4 GPTQ-style
+experts (asymmetric, group 128) at 1 and 512 tokens (--no-gptq skips it).
+
 On every N the line carries `expert_parallel`: the MoE layer of the
 expert-parallel prefill (32 x 2048 tokens split over the N ranks, the 60
 experts spread over the GPUs, NCCL all-to-all of rows and results), timed
@@ -71,6 +74,7 @@ def parse_args():
     ap.add_argument("--prompt-tokens", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=128)
     ap.add_argument("--cache-frac", type=float, default=0.25, help="HBM expert-cache share of the routed records")
+    ap.add_argument("--no-gptq", action="store_true", help="skip the int4 GPTQ block measurement")
     ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel layer measurement")
     ap.add_argument("--ep-tokens", type=int, default=65536, help="tokens of the expert-parallel layer (all ranks)")
     ap.add_argument("--ep-microbatch", type=int, default=4096)
@@ -516,6 +520,11 @@ def main() -> None:
         line["decode"] = decode_side(args, dev, mb, block, peaks, peak_src)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(block, x, args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_gptq:
+        try:
+            line["gptq"] = gptq_side(args, dev, peaks, peak_src)
+        except (RuntimeError, ValueError, MemoryError) as e:  # reported, the main line still prints
+            line["gptq"] = {"error": f"{type(e).__name__}: {e}"[:400]}
     if not args.no_ep:
         line["expert_parallel"] = expert_parallel_side(args, dev, block, world, rank, flush)
     if rank == 0 and world == 1 and not args.no_full_model:
@@ -682,6 +691,61 @@ def full_model_side(args, dev) -> dict:
         "build_s": t_build,
         "timing": "host wall clock around each generate() call (synchronous: argmax read back per token)",
     }
+
+
+def gptq_side(args, dev, peaks, peak_src) -> dict:
+    """The MoE block with int4 GPTQ-style routed experts (asymmetric 4-bit,
+    group 128 along the input, fp16 scales, 4-bit zero points; the shared
+    expert int8), at 1 decode token (exact-fp32 weight-streaming GEMV) and at
+    512 tokens (exact-fp32 SIMT GEMM). Each step replays the captured forward
+    after an L2 flush. Both report the block's algorithmic weight bytes
+    against HBM and its FLOPs against dense bf16 (512 tokens sits near the
+    ridge between the two)."""
+    import torch
+
+    from expertrelay_b200 import _lib, synth
+    from expertrelay_b200.moe import MoeBlock
+
+    block, _ = synth.make_workload("gptq_asym_decode1", seed=args.seed)
+    mb = MoeBlock.from_host_block(block, device=dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(args.steps, 20)
+    out = {}
+    for name, n, path, pname in (("decode1", 1, _lib.PATH_GEMV, "gemv"), ("prefill512", 512, _lib.PATH_GEMM, "gemm")):
+        h = torch.from_numpy(synth.make_tokens(args.seed, n, block.hidden)).to(dev)
+        _, _, idx, _ = mb.forward(h, path=path, return_routing=True)
+        acct = accounting(block, n, idx.cpu().numpy(), 4)
+        cap = mb.capture(n, path=path)
+        cap.h.copy_(h)
+        for _ in range(max(args.warmup, 3)):
+            cap.replay()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            t0.record()
+            cap.replay()
+            t1.record()
+            t1.synchronize()
+            tot += t0.elapsed_time(t1)
+        sec = tot / steps / 1e3
+        gbs = acct["block_weight_bytes"] / sec / 1e9
+        tfs = acct["block_flops"] / sec / 1e12
+        out[name] = {
+            "tokens": n, "path": pname, "ms_per_block": sec * 1e3, "tokens_per_s": n / sec,
+            "unique_experts": acct["unique_experts"],
+            "hbm": {"achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+                    "algorithmic_bytes": acct["block_weight_bytes"], "peak_source": f"of {peak_src}"},
+            "tensor": {"achieved": tfs, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                       "frac": tfs / peaks["bf16_tflops_sustained"], "algorithmic_flops": acct["block_flops"],
+                       "peak_source": f"of {peak_src}"},
+        }
+        del cap
+    del mb
+    torch.cuda.empty_cache()
+    return {"workload": "int4 GPTQ-style experts (asymmetric, group 128, fp16 scales, 4-bit zero points), "
+                        "int8 shared expert; 1 and 512 tokens", "steps": steps, **out}
 
 
 def decode_side(args, dev, mb, block, peaks, peak_src) -> dict:
