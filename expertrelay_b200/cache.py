@@ -30,7 +30,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .store import FMT_INT8, RecordLayout
+from .store import FMT_INT4_ZP, FMT_INT8, RecordLayout
 
 Key = tuple[int, int]  # (layer, expert)
 
@@ -66,6 +66,44 @@ class DeviceInt8Matrix:
 
     q: torch.Tensor  # [out, in] int8
     scales: torch.Tensor  # [out] float32
+
+
+@dataclass
+class DeviceInt4Matrix:
+    """An int4 expert matrix as device views into its cache slot (the fields
+    of runtime/weights.py Int4Matrix: two codes per byte, the even column in
+    the low nibble, float16 scales per group of `group_size` inputs), plus
+    the 4-bit zero points of an asymmetric GPTQ record (None for the
+    store's symmetric records, whose zero point is 8)."""
+
+    packed: torch.Tensor  # [out, in / 2] uint8
+    scales: torch.Tensor  # [out, in / group_size] float16
+    group_size: int
+    zeros: torch.Tensor | None = None  # [out, in / group_size] uint8
+
+
+def record_views(layout: RecordLayout, rec: torch.Tensor) -> dict:
+    """The matrices of one store record held in the uint8 tensor `rec` (on
+    any device), as views: DeviceInt8Matrix or DeviceInt4Matrix per matrix
+    name, at the record layout's offsets (store/layout.py:53-115,
+    store/int4.py:165-244)."""
+    out = {}
+    for name, (rows, cols) in layout.matrices:
+        w0, s0 = layout.weight_offset(name), layout.scale_offset(name)
+        if layout.fmt == FMT_INT8:
+            q = rec[w0 : w0 + rows * cols].view(torch.int8).view(rows, cols)
+            s = rec[s0 : s0 + rows * 4].view(torch.float32)
+            out[name] = DeviceInt8Matrix(q, s)
+            continue
+        groups = cols // layout.group
+        packed = rec[w0 : w0 + rows * cols // 2].view(rows, cols // 2)
+        scales = rec[s0 : s0 + rows * groups * 2].view(torch.float16).view(rows, groups)
+        zeros = None
+        if layout.fmt == FMT_INT4_ZP:
+            z0 = layout.zero_offset(name)
+            zeros = rec[z0 : z0 + rows * groups].view(rows, groups)
+        out[name] = DeviceInt4Matrix(packed, scales, layout.group, zeros)
+    return out
 
 
 def slots_for(capacity_bytes: int, record_size: int) -> int:
@@ -234,24 +272,15 @@ class HbmExpertCache:
         )
         return out
 
-    def load(self, layer: int, expert: int, stream=None) -> dict[str, DeviceInt8Matrix]:
-        """ExpertSource.load (runtime/weights.py:199-207): the expert's int8
-        matrices as device views into its slot, held until end_layer."""
+    def load(self, layer: int, expert: int, stream=None) -> dict:
+        """ExpertSource.load (runtime/weights.py:199-207): the expert's
+        matrices as device views into its slot (DeviceInt8Matrix, or
+        DeviceInt4Matrix for int4 records), held until end_layer."""
         if self.dry:
             raise RuntimeError("a dry cache holds no records")
-        if self.layout.fmt != FMT_INT8:
-            raise ValueError("load() views int8 records; int4 records are used through MoeBlock")
         addr = int(self.acquire(layer, [expert], stream)[0])
         off = addr - self.arena.data_ptr()
-        rec = self.arena[off : off + self.layout.record_size]
-        lay = self.layout
-        out = {}
-        for name, (rows, cols) in lay.matrices:
-            q0, s0 = lay.weight_offset(name), lay.scale_offset(name)
-            q = rec[q0 : q0 + rows * cols].view(torch.int8).view(rows, cols)
-            s = rec[s0 : s0 + rows * 4].view(torch.float32)
-            out[name] = DeviceInt8Matrix(q, s)
-        return out
+        return record_views(self.layout, self.arena[off : off + self.layout.record_size])
 
     def prefetch(self, layer: int, experts, keep=(), max_new_reads: int | None = None) -> None:
         """Start copying `experts` of `layer` (cache/expert_cache.py:264-294)."""

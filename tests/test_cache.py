@@ -18,7 +18,7 @@ import json
 import numpy as np
 import pytest
 
-from expertrelay_b200.cache import CacheTooSmall, HbmExpertCache, HostRecords, slots_for
+from expertrelay_b200.cache import CacheTooSmall, HbmExpertCache, HostRecords, record_views, slots_for
 from expertrelay_b200.prefetch import IsotonicCalibrator, PrefetchPolicy, RankedIsotonicCalibrator, load_calibrator
 from expertrelay_b200.store import FMT_INT8, RecordLayout
 
@@ -247,3 +247,32 @@ def test_ranked_calibrator_maps_each_rank(tmp_path):
     assert isinstance(cal, IsotonicCalibrator) and prov["kind"] == "isotonic"
     with pytest.raises(ValueError):
         load_calibrator(path, kind="other")
+
+
+@pytest.mark.parametrize("fmt", ["int8", "int4", "gptq_asym"])
+def test_record_views_match_the_store_parser(fmt):
+    """What load() hands out for a cached record: views at the record
+    layout's offsets, the fields of the reference's Int8Matrix / Int4Matrix
+    (runtime/weights.py:51-80), equal to the store's own parse of the same
+    bytes; zero points only for asymmetric GPTQ records."""
+    import torch
+
+    from expertrelay_b200 import synth
+    from expertrelay_b200.store import parse_record
+
+    blk = synth.make_block(61, fmt=fmt, hidden=256, inter=128, shared_inter=384, num_experts=8, top_k=2)
+    rec = blk.records()[5]
+    views = record_views(blk.layout, torch.from_numpy(rec.copy()))
+    want = parse_record(blk.layout, rec)
+    assert set(views) == set(want)
+    for name, m in views.items():
+        if fmt == "int8":
+            assert np.array_equal(m.q.numpy(), want[name][0]) and np.array_equal(m.scales.numpy(), want[name][1])
+            continue
+        assert m.group_size == blk.layout.group and m.scales.dtype == torch.float16
+        assert np.array_equal(m.packed.numpy(), want[name][0])
+        assert np.array_equal(m.scales.numpy(), want[name][1])
+        if fmt == "gptq_asym":
+            assert np.array_equal(m.zeros.numpy(), want[name][2])
+        else:
+            assert m.zeros is None

@@ -89,6 +89,28 @@ def test_load_views_match_the_record(source, blocks):
     c.close()
 
 
+@pytest.mark.parametrize("fmt", ["int4", "gptq_asym"])
+def test_load_views_of_int4_records(cuda, fmt):
+    from expertrelay_b200.store import parse_record
+
+    blk = synth.make_block(61, fmt=fmt, **SHAPE)
+    src = HostRecords.from_blocks([blk])
+    c = HbmExpertCache(src, capacity_bytes=2 * src.layout.record_size)
+    w = c.load(0, 5)
+    torch.cuda.synchronize()
+    want = parse_record(src.layout, blk.records()[5])
+    for name, m in w.items():
+        assert m.packed.is_cuda and m.group_size == src.layout.group
+        assert np.array_equal(m.packed.cpu().numpy(), want[name][0])
+        assert np.array_equal(m.scales.cpu().numpy(), want[name][1])
+        if fmt == "gptq_asym":
+            assert np.array_equal(m.zeros.cpu().numpy(), want[name][2])
+        else:
+            assert m.zeros is None
+    c.end_layer(0)
+    c.close()
+
+
 def test_resize_moves_the_kept_records(source):
     rs = source.layout.record_size
     c = HbmExpertCache(source, capacity_bytes=6 * rs)
