@@ -35,6 +35,25 @@ def test_library_exports_every_declared_function():
     assert L.er_version() == 100
 
 
+def declared_arities() -> dict[str, int]:
+    out = {}
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for name, params in re.findall(r"^ER_API\s+[\w\s\*]+?\b(er_\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M):
+            params = " ".join(params.split())
+            out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_binding_arities_match_the_header():
+    """Each ctypes signature takes as many arguments as the header's
+    declaration: a parameter added on one side only fails here, not on a GPU."""
+    arities = declared_arities()
+    assert set(arities) == set(declared_functions())
+    for name, n in arities.items():
+        assert len(_lib.SIGNATURES[name][1]) == n, f"{name}: header {n} parameters, binding {len(_lib.SIGNATURES[name][1])}"
+
+
 @pytest.mark.parametrize(
     "lay",
     [RecordLayout(FMT_INT8, 2048, 1408), RecordLayout(FMT_INT4, 2048, 1408, 128),
