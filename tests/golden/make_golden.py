@@ -1,6 +1,8 @@
 """Generate the golden fixtures in tests/golden/ by running the reference.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path of the ExpertRelay checkout>
+
+(or set EXPERTRELAY_REFERENCE to that path instead of passing --reference)
 
 Imports ExpertRelay from <reference>/src (read only: no bytecode is written
 and numba's cache goes to a temporary directory) and records its outputs on
@@ -256,12 +258,62 @@ def full_fixtures() -> dict:
     blk, x = synth.make_workload("prefill4096_int8_zipf", seed=0)
     y, lg, sel = _run_moe(blk, x)
     out["prefill_sel"] = sel.astype(np.int8)
+    out["prefill_logits"] = lg.astype(np.float32)
     out["prefill_y_head"] = y[:32]
+    # every row of the output projected on PREFILL_SKETCH_COLS seeded
+    # directions: catches a wrong direction that the row norms cannot
+    out["prefill_y_sketch"] = y.astype(np.float64) @ prefill_sketch_matrix(y.shape[1])
     out["prefill_y_rownorm"] = np.linalg.norm(y.astype(np.float64), axis=1)
     out["prefill_y_sum"] = np.array([y.astype(np.float64).sum()])
     out["prefill_router_sha"] = np.frombuffer(sha(blk.router).encode(), dtype=np.uint8)
     out["prefill_zipf_realised"] = np.array(blk.meta["zipf"]["realised"])
     return out
+
+
+PREFILL_SKETCH_SEED, PREFILL_SKETCH_COLS = 7, 8
+
+
+def prefill_sketch_matrix(hidden: int) -> np.ndarray:
+    """[hidden, PREFILL_SKETCH_COLS] float64 directions (the GPU test rebuilds them)."""
+    return np.random.default_rng(PREFILL_SKETCH_SEED).standard_normal((hidden, PREFILL_SKETCH_COLS))
+
+
+def prefetch_fixtures() -> tuple[dict, dict]:
+    """The reference's prefetch policy (predictor/prefetch_policy.py:41-54)
+    and calibration maps (predictor/offline.py:87-200) on seeded router
+    logits: the experts each policy picks, the low-confidence skips, and
+    the calibrated probabilities; plus the maps' JSON form."""
+    from expertrelay.predictor.offline import IsotonicCalibrator, RankedIsotonicCalibrator
+    from expertrelay.predictor.prefetch_policy import PrefetchPolicy
+
+    rng = np.random.default_rng(21)
+    # fitted maps: scores with labels that grow more likely with the score
+    scores = rng.uniform(0, 1, 4000)
+    labels = (rng.uniform(0, 1, 4000) < scores ** 2).astype(np.float64)
+    single = IsotonicCalibrator(num_bins=40).fit(scores, labels)
+    probs = rng.dirichlet(np.full(16, 0.3), 600)
+    picked = np.zeros_like(probs)
+    np.put_along_axis(picked, np.argsort(-probs + rng.normal(0, 0.05, probs.shape), axis=1)[:, :4], 1.0, axis=1)
+    ranked = RankedIsotonicCalibrator(max_rank=6, num_bins=20).fit(probs, picked)
+    cases = []
+    for n, e, scale in ((1, 60, 2.0), (1, 16, 0.5), (7, 60, 1.5), (3, 16, 3.0), (32, 60, 1.0)):
+        cases.append(rng.normal(0, scale, (n, e)).astype(np.float32))
+    tie = np.zeros((2, 16), dtype=np.float32)
+    tie[0, [9, 4, 12]] = 2.0  # equal best scores: ascending id
+    cases.append(tie)
+    out = {}
+    policies = (("plain", None, 0.0), ("single", single, 0.3), ("ranked", ranked, 0.3), ("ranked_hi", ranked, 0.7))
+    for c, logits in enumerate(cases):
+        out[f"logits{c}"] = logits
+        for name, cal, pmin in policies:
+            for k in (1, 4, 8):
+                choice = PrefetchPolicy(top_k=k, min_probability=pmin, calibrator=cal).choose(logits)
+                out[f"experts{c}_{name}_k{k}"] = np.array(choice.experts, dtype=np.int64)
+                out[f"skipped{c}_{name}_k{k}"] = np.array([choice.skipped_low_confidence])
+        out[f"single_pred{c}"] = single.predict(logits.ravel())
+        out[f"ranked_pred{c}"] = ranked.predict(np.exp(logits) / np.exp(logits).sum(axis=-1, keepdims=True))
+    maps = {"calibrator": single.to_dict(), "rank_calibrator": ranked.to_dict(), "cases": len(cases)}
+    return out, maps
 
 
 # (num_layers, num_experts, top_k, prefill tokens) of the trace fixtures
@@ -413,12 +465,23 @@ def store_fixture(out_dir: Path) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EXPERTRELAY_REFERENCE"),
+                    help="the ExpertRelay checkout (default: $EXPERTRELAY_REFERENCE)")
     ap.add_argument("--skip-full", action="store_true")
-    ap.add_argument("--only", choices=("trace", "store", "model"), help="regenerate one fixture only")
+    ap.add_argument("--only", choices=("trace", "store", "model", "prefetch", "qwen"),
+                    help="regenerate one fixture only")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set EXPERTRELAY_REFERENCE")
     ref = Path(args.reference)
     _import_reference(ref)
+    if args.only == "qwen":
+        np.savez_compressed(HERE / "moe_qwen.npz", **full_fixtures())
+        return
+    if args.only in (None, "prefetch"):
+        arrays, maps = prefetch_fixtures()
+        np.savez_compressed(HERE / "prefetch.npz", **arrays)
+        (HERE / "prefetch_maps.json").write_text(json.dumps(maps, indent=1))
     if args.only in (None, "trace"):
         with tempfile.TemporaryDirectory() as tmp:
             np.savez_compressed(HERE / "trace.npz", **trace_fixtures(Path(tmp)))
