@@ -19,13 +19,13 @@ struct SchedSpec {
 
 constexpr int kNumSched = 2;
 
-// Routing plan in the workspace. `tally` and `cursor` are cleared (kPlanClear
-// ints from `tally`) before the top-k kernel counts into `tally`; the dispatch
-// kernel turns the counts into groups and schedules and claims expert-sorted
-// positions through `cursor`.
+// Routing plan in the workspace. `tally`, `cursor` and `error` are cleared
+// (kPlanClear ints from `tally`) before the top-k kernel counts into `tally`;
+// the dispatch kernel turns the counts into groups and schedules and claims
+// expert-sorted positions through `cursor`. Every kernel that reports a
+// problem sets its bit of `error` with atomicOr, so no report is lost.
 struct Plan {
   int n, E, k, nk;
-  int error;                           // nonzero: an expert id was out of range
   int num_active;                      // groups with at least one token (shared last)
   int counts[kMaxExperts + 1];         // tokens per group (counts[E] = n)
   int offsets[kMaxExperts + 1];        // first expert-sorted position of each routed group
@@ -34,8 +34,12 @@ struct Plan {
   SchedSpec sched[kNumSched];
   int tally[kMaxExperts];              // (token, slot) pairs routed to each expert
   int cursor[kMaxExperts];             // positions of each expert's range claimed so far
+  // bits: 1 an expert id out of range, 2 tallies and ids disagree (or do not
+  // add up to n * k), 4 a record outside the arena, 8 a tensor-core wait
+  // gave up; the combine writes NaN rows when any is set
+  int error;
 };
-constexpr int kPlanClear = 2 * kMaxExperts;  // tally and cursor, contiguous
+constexpr int kPlanClear = 2 * kMaxExperts + 1;  // tally, cursor and error, contiguous
 
 // Everything a grouped expert kernel needs to find a group's tokens and weights.
 struct GroupArgs {

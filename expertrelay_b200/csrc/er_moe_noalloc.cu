@@ -13,7 +13,8 @@
 //    held from the first call on that GPU until the process exits; a batch
 //    whose workspace (er_moe_workspace_bytes) exceeds it is rejected with
 //    ER_ENOSPACE before anything is launched (at Qwen1.5-MoE-A2.7B shapes:
-//    up to 96 tokens per call);
+//    up to 96 tokens per call on the GEMV / SIMT GEMM paths, 64 on the
+//    tensor-core path, whose int8 operand slices take room too);
 //  * the first call on a device looks up the array's device address (once
 //    per device, with that device current) and caches it; make that first
 //    call before any stream capture;

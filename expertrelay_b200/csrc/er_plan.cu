@@ -125,7 +125,7 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
     plan->E = E;
     plan->k = k;
     plan->nk = nk;
-    plan->error = bad;
+    if (bad) atomicOr(&plan->error, 2);
     plan->sched[0] = s0;
     plan->sched[1] = s1;
     plan->num_active = bad ? 0 : na;  // no work items on an inconsistent tally

@@ -155,7 +155,10 @@ ER_API size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path);
  * in the reference): same weights and io, no workspace argument. The scratch
  * is a fixed 8 MiB device array inside the library, held on each GPU from the
  * first call there until exit; batches needing more (er_moe_workspace_bytes)
- * fail with ER_ENOSPACE (96 tokens fit at Qwen1.5-MoE-A2.7B shapes). The
+ * fail with ER_ENOSPACE. At Qwen1.5-MoE-A2.7B shapes up to 96 tokens fit on
+ * the GEMV / SIMT GEMM paths and up to 64 on the tensor-core path (which
+ * ER_PATH_AUTO picks for int8 records in an arena: its int8 operand slices
+ * need room). The
  * first call on a device sets up the array's address: make it before any
  * stream capture. All calls share the array, so calls that overlap on the GPU
  * race and must be serialised by the caller. */

@@ -107,12 +107,25 @@ def test_moe_weights_validation_and_workspace_query():
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
+def _noalloc_limit(w, path: int) -> int:
+    L = _lib.lib()
+    n = 0
+    while L.er_moe_workspace_bytes(C.byref(w), n + 1, path) <= NOALLOC_SCRATCH_BYTES:
+        n += 1
+    return n
+
+
 def test_noalloc_token_limit_at_qwen_shapes():
     """er_moe_block_noalloc serves a batch when its er_moe_workspace_bytes
-    fits the fixed 8 MiB scratch: at Qwen1.5-MoE-A2.7B shapes (60 experts,
-    top-4, default path) that is up to 96 tokens, the limit its header states."""
-    L = _lib.lib()
+    fits the fixed 8 MiB scratch. At Qwen1.5-MoE-A2.7B shapes (60 experts,
+    top-4) the limits its header states: 96 tokens on the GEMV / SIMT GEMM
+    paths (the default without a record arena), 64 on the tensor-core path
+    (the default for int8 records in an arena)."""
     w = _lib.MoeWeights(hidden=2048, num_experts=60, top_k=4, inter=1408, shared_inter=5632, expert_fmt=0, group=0,
                         norm_topk_prob=0, router_w=16, shared_gate_w=16, expert_records=16, shared_record=256)
-    assert L.er_moe_workspace_bytes(C.byref(w), 96, _lib.PATH_AUTO) <= NOALLOC_SCRATCH_BYTES
-    assert L.er_moe_workspace_bytes(C.byref(w), 97, _lib.PATH_AUTO) > NOALLOC_SCRATCH_BYTES
+    assert _noalloc_limit(w, _lib.PATH_AUTO) == 96
+    assert _noalloc_limit(w, _lib.PATH_GEMV) == 96 and _noalloc_limit(w, _lib.PATH_GEMM) == 96
+    arena = _lib.MoeWeights.from_buffer_copy(w)
+    arena.record_arena, arena.arena_slots = 4096, 60
+    assert _noalloc_limit(arena, _lib.PATH_TC) == 64
+    assert _noalloc_limit(arena, _lib.PATH_AUTO) == 64
