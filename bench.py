@@ -194,6 +194,15 @@ class ClockSampler:
         }
 
 
+# the MoE layer of the expert-parallel prefill (32 sequences x 2048 tokens)
+EP_WORKLOAD = "ep_prefill65536_int8"
+
+
+def arm_workload(args, world: int) -> str:
+    """The workload the headline `value` measures at this GPU count."""
+    return args.workload
+
+
 def blas_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -248,62 +257,215 @@ def accounting(block, n: int, idx: np.ndarray, act_bytes: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
-# CPU side (oracle port of the reference's numpy path)
+# CPU side: the reference's own QwenMoe._moe (installed in baseline/_ref), and
+# the oracle port of it
 # ---------------------------------------------------------------------------
 
+REF_DIR = ROOT / "baseline" / "_ref"
 
-def cpu_baseline(block, x: np.ndarray, budget_s: float, max_tokens: int | None = None) -> dict:
-    from oracle import moe_oracle as O
-    from oracle.blocks import oracle_weights
 
-    w = oracle_weights(block)
-    n = x.shape[0] if max_tokens is None else min(x.shape[0], max_tokens)
-    xs = x[:n]
-    O.moe_block(xs[: min(n, 8)], w)  # warm BLAS / page in
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def pin_cpu_threads(cores: int) -> dict:
+    """Give the reference's BLAS and numba pools every host core, whatever
+    the launcher set (torchrun sets OMP_NUM_THREADS=1 on every rank); returns
+    the thread counts actually in effect."""
+    os.environ["NUMBA_NUM_THREADS"] = str(cores)
+    got = {"blas": None, "numba": None}
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        threadpool_limits(limits=cores)
+        blas = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        got["blas"] = int(max(blas)) if blas else None
+    except Exception as e:  # reported, not fatal
+        got["blas_error"] = f"{type(e).__name__}: {e}"[:120]
+    try:
+        import numba
+
+        numba.set_num_threads(min(cores, numba.config.NUMBA_NUM_THREADS))
+        got["numba"] = int(numba.get_num_threads())
+    except Exception as e:
+        got["numba_error"] = f"{type(e).__name__}: {e}"[:120]
+    return got
+
+
+class ReferenceBlock:
+    """The reference's QwenMoe._moe (runtime/qwen_moe.py:293-359) from the
+    unmodified package in baseline/_ref, driven in memory: the router, the
+    shared expert and its gate as ResidentWeights, the routed experts from
+    an ExpertSource that hands out Int8Matrix / Int4Matrix views of the
+    block's store encodings (runtime/weights.py:51-80, 196-235). `kernel`
+    is the reference's int8 kernel choice (runtime/int8_linear.py:78-93;
+    "fused" is its runtime default, runtime/generate.py:110)."""
+
+    def __init__(self, block, kernel: str = "fused"):
+        if not (REF_DIR / "expertrelay").is_dir():
+            raise ImportError(f"the reference is not installed in {REF_DIR}")
+        sys.dont_write_bytecode = True
+        import tempfile
+
+        os.environ.setdefault("NUMBA_CACHE_DIR", tempfile.mkdtemp(prefix="numba-ref-"))
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        from expertrelay.runtime import int8_linear as i8mod
+        from expertrelay.runtime.qwen_moe import ModelConfig, QwenMoe, StepTimings
+        from expertrelay.runtime.weights import ExpertSource, Int4Matrix, Int8Matrix, ResidentWeights, SourceStats
+
+        if block.fmt not in ("int8", "int4"):
+            raise ValueError(f"the reference's block path has no {block.fmt} experts (store/gptq.py:67-69)")
+        experts = []
+        for mats in block.experts:
+            if block.fmt == "int8":
+                experts.append({m: Int8Matrix(t[0], t[1]) for m, t in mats.items()})
+            else:
+                experts.append({m: Int4Matrix(t[0], t[1], t[0].shape[1] * 2 // t[1].shape[1]) for m, t in mats.items()})
+
+        class MemorySource(ExpertSource):
+            def __init__(self):
+                self.stats = SourceStats()
+
+            def load(self, layer, expert):
+                return experts[expert]
+
+        p = "model.layers.0.mlp."
+        resident = ResidentWeights({
+            p + "gate.weight": block.router,
+            p + "shared_expert_gate.weight": block.shared_gate,
+            **{p + f"shared_expert.{m}.weight": Int8Matrix(*block.shared[m]) for m in block.shared},
+        }, 0)
+        cfg = ModelConfig(151936, block.hidden, 1, 16, 16, block.num_experts, block.top_k, False, 1e-6, 1e6)
+        self.model = QwenMoe(cfg, resident, MemorySource())
+        self.kernel = kernel
+        self._i8 = i8mod
+        self._timings = StepTimings
+        i8mod.set_kernel(kernel)  # the fused kernel compiles here (numba)
+
+    def __call__(self, x: np.ndarray) -> np.ndarray:
+        self._i8.set_kernel(self.kernel)
+        return self.model._moe(0, np.ascontiguousarray(x, dtype=np.float32), self._timings(), None, None)
+
+
+def _time_calls(fn, x, budget_s: float, max_calls: int = 5) -> list[float]:
     times = []
     t_start = time.perf_counter()
     while True:
         t0 = time.perf_counter()
-        O.moe_block(xs, w)
+        fn(x)
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s or len(times) >= 5:
-            break
+        if time.perf_counter() - t_start > budget_s or len(times) >= max_calls:
+            return times
+
+
+def _sample_tokens(fn, x: np.ndarray, per_call_s: float) -> int:
+    """Tokens per call so that one call takes about per_call_s (at least
+    256, at most all of x), from a timed call on 256 tokens."""
+    n = x.shape[0]
+    probe = min(n, 256)
+    t0 = time.perf_counter()
+    fn(x[:probe])
+    dt = max(time.perf_counter() - t0, 1e-6)
+    return int(min(n, max(probe, probe * per_call_s / dt)))
+
+
+def cpu_baseline(block, x: np.ndarray, budget_s: float) -> dict:
+    """The reference's own block (both int8 kernels) and the oracle port,
+    timed on this host's cores on a bounded sample of the workload's tokens;
+    `value` is the reference with its default kernel."""
+    cores = host_cores()
+    threads = pin_cpu_threads(cores)
+    out = {"unit": "tokens/s", "cores": cores, "threads": threads, "host": cpu_model()}
+    kernels = {}
+    try:
+        for kernel in ("fused", "blocked"):
+            ref = ReferenceBlock(block, kernel)
+            n = _sample_tokens(ref, x, budget_s / 8)
+            times = _time_calls(ref, x[:n], budget_s / 3)
+            med = statistics.median(times)
+            kernels[kernel] = {"value": n / med, "tokens": n, "calls": len(times), "median_ms": med * 1e3}
+        out.update({"value": kernels["fused"]["value"], "kind": "reference", "kernels": kernels,
+                    "sample": (f"{kernels['fused']['calls']} x {kernels['fused']['tokens']} tokens of the same "
+                               f"workload through the reference's QwenMoe._moe (baseline/_ref, unmodified), int8 "
+                               f"kernel 'fused' (its runtime default); 'blocked' in kernels; {cores} host threads")})
+    except (ImportError, ValueError) as e:
+        out["reference_unavailable"] = f"{type(e).__name__}: {e}"[:200]
+    from oracle import moe_oracle as O
+    from oracle.blocks import oracle_weights
+
+    w = oracle_weights(block)
+
+    def port(xs):
+        return O.moe_block(xs, w)
+
+    n = _sample_tokens(port, x, budget_s / 8)
+    times = _time_calls(port, x[:n], budget_s / 3)
     med = statistics.median(times)
-    return {
-        "value": n / med,
-        "unit": "tokens/s",
-        "cores": blas_threads(),
-        "kind": "port",
-        "sample": f"{len(times)} x {n} tokens of the same workload (median {med * 1e3:.1f} ms), numpy/BLAS float32 "
-                  f"restatement of QwenMoe._moe, blocked int8 kernel; host {cpu_model()}",
-    }
+    out["port"] = {"value": n / med, "tokens": n, "calls": len(times), "median_ms": med * 1e3,
+                   "what": "oracle/moe_oracle.py: numpy/BLAS restatement of QwenMoe._moe, blocked int8 kernel"}
+    if "value" not in out:
+        out.update({"value": out["port"]["value"], "kind": "port",
+                    "sample": f"{len(times)} x {n} tokens through the oracle port; {cores} host threads"})
+    return out
 
 
 # ---------------------------------------------------------------------------
-# the GPU arm
+# the reference arm
 # ---------------------------------------------------------------------------
 
 
 def run_reference_arm(args) -> None:
+    """--impl reference: the reference's own QwenMoe._moe (baseline/_ref,
+    its default int8 kernel) on this host's cores, on the workload our arm
+    measures at this GPU count, each step a bounded sample of its tokens.
+    Under torchrun only rank 0 runs; the other ranks exit at once."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from expertrelay_b200 import synth
 
-    block, x = synth.make_workload(args.workload, seed=args.seed)
-    n = x.shape[0]
-    sample = n if args.steps + args.warmup <= 30 else min(n, 1024)
-    from oracle import moe_oracle as O
-    from oracle.blocks import oracle_weights
+    world = args.gpus
+    workload = arm_workload(args, world)
+    if workload == EP_WORKLOAD:
+        # the expert-parallel layer: the same block and near-uniform routing
+        # (the router without the Zipf scaling), tokens of that layer
+        import dataclasses
 
-    w = oracle_weights(block)
+        block, _ = synth.make_workload("prefill4096_int8_zipf", seed=args.seed)
+        block = dataclasses.replace(block, router=block.meta.get("router_base", block.router), meta={})
+        x = synth.make_tokens(args.seed * 1000 + 577, 4096, block.hidden)
+        tokens_total = args.ep_tokens
+    else:
+        block, x = synth.make_workload(workload, seed=args.seed)
+        tokens_total = x.shape[0]
+    cores = host_cores()
+    threads = pin_cpu_threads(cores)
+    try:
+        fn = ReferenceBlock(block, "fused")
+        kind, what = "reference", "the reference's QwenMoe._moe (baseline/_ref, unmodified), int8 kernel 'fused'"
+    except (ImportError, ValueError) as e:
+        from oracle import moe_oracle as O
+        from oracle.blocks import oracle_weights
+
+        w = oracle_weights(block)
+
+        def fn(xs):
+            return O.moe_block(xs, w)
+
+        kind, what = "port", f"the oracle port of QwenMoe._moe (reference unavailable: {e})"[:200]
+    # each step about 120 s / (steps + warm-up) of CPU work, so the run ends within a few minutes
+    sample = _sample_tokens(fn, x, 120.0 / max(args.steps + args.warmup, 1))
     xs = x[:sample]
     for _ in range(args.warmup):
-        O.moe_block(xs, w)
+        fn(xs)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.moe_block(xs, w)
+        fn(xs)
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = sample * args.steps / total
@@ -312,7 +474,7 @@ def run_reference_arm(args) -> None:
         "metric": "MoE-block tokens/s",
         "value": value,
         "unit": "tokens/s",
-        "n_gpus": args.gpus,
+        "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": total / args.steps * 1e3,
@@ -321,10 +483,12 @@ def run_reference_arm(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded N(0,0.02) weights in store encodings, N(0,1) activations",
-        "config": {"workload": args.workload, "tokens": n, "tokens_per_step": sample},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
-                         "sample": f"{sample} of {n} tokens per step; numpy/BLAS restatement of QwenMoe._moe "
-                                   f"(blocked int8 kernel) on {cpu_model()}"},
+        "config": {"workload": workload, "tokens": tokens_total, "tokens_per_step": sample,
+                   "hidden": block.hidden, "experts": block.num_experts, "top_k": block.top_k,
+                   "expert_format": block.fmt},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind, "threads": threads,
+                         "sample": f"{sample} of the workload's tokens per step through {what}; {cores} host "
+                                   f"threads on {cpu_model()}"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

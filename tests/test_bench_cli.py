@@ -29,7 +29,9 @@ def test_reference_arm_prints_one_contract_line():
                 "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in line, key
     assert line["impl"] == "reference" and line["value"] > 0 and line["higher_is_better"] is True
-    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    # the reference itself when its package is installed beside the bench, else the oracle port
+    want = "reference" if (ROOT / "baseline" / "_ref" / "expertrelay").is_dir() else "port"
+    assert line["cpu_baseline"]["kind"] == want and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
     assert line["config"]["workload"] == "decode8_int8"
 
@@ -38,3 +40,14 @@ def test_reference_arm_other_ranks_exit_quietly():
     p = _run({"RANK": "1"})
     assert p.returncode == 0, p.stderr[-2000:]
     assert p.stdout.strip() == ""
+
+
+def test_reference_arm_uses_every_core_under_a_launcher_limit():
+    """torchrun sets OMP_NUM_THREADS=1 on every rank; the reference arm still
+    gives BLAS and numba all of this host's cores and says so."""
+    p = _run({"RANK": "0", "OMP_NUM_THREADS": "1"})
+    assert p.returncode == 0, p.stderr[-2000:]
+    line = json.loads(p.stdout.strip().splitlines()[-1])
+    cores = line["cpu_baseline"]["cores"]
+    assert cores == len(os.sched_getaffinity(0))
+    assert line["cpu_baseline"]["threads"]["blas"] == cores
