@@ -98,18 +98,19 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def traffic_from_profiles(workload: str, stage: str) -> float | None:
+def traffic_from_profiles(workload: str, stage: str) -> tuple[float | None, str | None]:
     """DRAM bytes per launch recorded from an ncu capture in profiles/*.md, as a
-    line `traffic_per_launch_bytes[<workload>/<stage>] = <bytes>`."""
+    line `traffic_per_launch_bytes[<workload>/<stage>] = <bytes>`, and the file
+    it came from. The figure is from that capture, not from this run."""
     key = f"traffic_per_launch_bytes[{workload}/{stage}]"
     for f in sorted((ROOT / "profiles").glob("*.md")):
         for line in f.read_text().splitlines():
             if key in line and "=" in line:
                 try:
-                    return float(line.split("=", 1)[1].strip().strip("`").split()[0])
+                    return float(line.split("=", 1)[1].strip().strip("`").split()[0]), f"profiles/{f.name}"
                 except ValueError:
-                    return None
-    return None
+                    return None, None
+    return None, None
 
 
 class ClockSampler:
@@ -625,17 +626,23 @@ def main() -> None:
     dom = max(("gate_up", "down"), key=lambda s: stage_avg[s])
     tensor_bound = n >= 256
     if tensor_bound:
+        # the timed region is a few ms of short steps: the burst GEMM peak is
+        # the denominator; the sustained (power-capped) one rides beside it
         work = acct["gate_up_flops"] if dom == "gate_up" else acct["down_flops"]
         achieved = work / (stage_avg[dom] / 1e3) / 1e12
-        peak = peaks["bf16_tflops_sustained"]
-        roof = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dom, "algorithmic_flops_per_launch": work}
+        peak = peaks["bf16_tflops"]
+        roof = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dom, "algorithmic_flops_per_launch": work,
+                "peak_kind": "burst bf16 GEMM", "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"]}
     else:
         work = acct["gate_up_bytes"] if dom == "gate_up" else acct["down_bytes"]
         achieved = work / (stage_avg[dom] / 1e3) / 1e9
         peak = peaks["hbm_gbs"]
-        roof = {"bound": "hbm", "unit": "GB/s", "kernel": dom, "algorithmic_bytes_per_launch": work}
+        roof = {"bound": "hbm", "unit": "GB/s", "kernel": dom, "algorithmic_bytes_per_launch": work,
+                "peak_kind": "copy bandwidth"}
+    traffic, traffic_src = traffic_from_profiles(args.workload, dom)
     roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak, "peak_source": f"of {peak_src}",
-                 "traffic": traffic_from_profiles(args.workload, dom)})
+                 "traffic": traffic,
+                 "traffic_source": f"ncu capture summarised in {traffic_src}, not this run" if traffic_src else None})
 
     line = {
         "metric": "MoE-block tokens/s",
@@ -702,7 +709,36 @@ def main() -> None:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
+        line["summary"] = summary_of(line)  # last, so a tail of the output keeps it
         print(json.dumps(line), flush=True)
+
+
+def summary_of(line: dict) -> dict:
+    """The side measurements' key figures in a few short keys."""
+
+    def pick(d, *keys):
+        for k in keys:
+            if not isinstance(d, dict) or k not in d:
+                return None
+            d = d[k]
+        return round(d, 4) if isinstance(d, float) else d
+
+    out = {"value": pick(line, "value"), "frac": pick(line, "roofline", "frac"),
+           "e2e": pick(line, "e2e", "value"), "cpu": pick(line, "cpu_baseline", "value")}
+    if "decode" in line:
+        out["decode8"] = {"path": pick(line, "decode", "best_path"), "ms": pick(line, "decode", "ms_per_block"),
+                          "gate_up_hbm_frac": pick(line, "decode", "roofline", "frac"),
+                          "block_GBps": pick(line, "decode", "block_weight_GBps")}
+    if "gptq" in line:
+        for k in ("decode1", "prefill512"):
+            out[f"gptq_{k}"] = {"path": pick(line, "gptq", k, "path"), "ms": pick(line, "gptq", k, "ms_per_block"),
+                                "hbm_frac": pick(line, "gptq", k, "hbm", "frac"),
+                                "tensor_frac": pick(line, "gptq", k, "tensor", "frac")}
+    if "expert_parallel" in line:
+        out["ep"] = {"value": pick(line, "expert_parallel", "value"), "ms": pick(line, "expert_parallel", "ms_per_step")}
+    if "full_model" in line:
+        out["full_model_tok_s"] = pick(line, "full_model", "decode_tokens_per_s")
+    return out
 
 
 def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict:
@@ -901,8 +937,9 @@ def gptq_side(args, dev, peaks, peak_src) -> dict:
             "unique_experts": acct["unique_experts"],
             "hbm": {"achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
                     "algorithmic_bytes": acct["block_weight_bytes"], "peak_source": f"of {peak_src}"},
-            "tensor": {"achieved": tfs, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                       "frac": tfs / peaks["bf16_tflops_sustained"], "algorithmic_flops": acct["block_flops"],
+            "tensor": {"achieved": tfs, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                       "frac": tfs / peaks["bf16_tflops"], "algorithmic_flops": acct["block_flops"],
+                       "peak_kind": "burst bf16 GEMM",
                        "peak_source": f"of {peak_src}"},
         }
         del cap
@@ -970,7 +1007,8 @@ def decode_side(args, dev, mb, block, peaks, peak_src) -> dict:
             "roofline": {"bound": "hbm", "kernel": "gate_up", "achieved": gu_gbs, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": gu_gbs / peaks["hbm_gbs"], "peak_source": f"of {peak_src}",
                          "algorithmic_bytes_per_launch": acct["gate_up_bytes"],
-                         "traffic": traffic_from_profiles("decode8_int8", "gate_up") if name == "tc" else None},
+                         "traffic": traffic_from_profiles("decode8_int8", "gate_up")[0] if name == "tc" else None,
+                         "traffic_source": "ncu capture summarised in profiles/, not this run" if name == "tc" else None},
             "stages_ms": stage,
         }
     if base_router is not None:
