@@ -383,10 +383,13 @@ def cpu_baseline(block, x: np.ndarray, budget_s: float) -> dict:
     out = {"unit": "tokens/s", "cores": cores, "threads": threads, "host": cpu_model()}
     kernels = {}
     try:
-        for kernel in ("fused", "blocked"):
+        # one sample size for both kernels (per-token cost depends on rows per expert)
+        n = None
+        for kernel in ("blocked", "fused"):
             ref = ReferenceBlock(block, kernel)
-            n = _sample_tokens(ref, x, budget_s / 8)
-            times = _time_calls(ref, x[:n], budget_s / 3)
+            if n is None:
+                n = _sample_tokens(ref, x, budget_s / 5)
+            times = _time_calls(ref, x[:n], budget_s / 3, max_calls=3)
             med = statistics.median(times)
             kernels[kernel] = {"value": n / med, "tokens": n, "calls": len(times), "median_ms": med * 1e3}
         out.update({"value": kernels["fused"]["value"], "kind": "reference", "kernels": kernels,
@@ -403,8 +406,8 @@ def cpu_baseline(block, x: np.ndarray, budget_s: float) -> dict:
     def port(xs):
         return O.moe_block(xs, w)
 
-    n = _sample_tokens(port, x, budget_s / 8)
-    times = _time_calls(port, x[:n], budget_s / 3)
+    n = _sample_tokens(port, x, budget_s / 5)
+    times = _time_calls(port, x[:n], budget_s / 3, max_calls=3)
     med = statistics.median(times)
     out["port"] = {"value": n / med, "tokens": n, "calls": len(times), "median_ms": med * 1e3,
                    "what": "oracle/moe_oracle.py: numpy/BLAS restatement of QwenMoe._moe, blocked int8 kernel"}
@@ -458,7 +461,8 @@ def run_reference_arm(args) -> None:
             return O.moe_block(xs, w)
 
         kind, what = "port", f"the oracle port of QwenMoe._moe (reference unavailable: {e})"[:200]
-    # each step about 120 s / (steps + warm-up) of CPU work, so the run ends within a few minutes
+    # each step at most about 120 s / (steps + warm-up) of CPU work (the whole
+    # batch when that fits), so the run ends within a few minutes
     sample = _sample_tokens(fn, x, 120.0 / max(args.steps + args.warmup, 1))
     xs = x[:sample]
     for _ in range(args.warmup):

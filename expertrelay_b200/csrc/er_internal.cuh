@@ -179,6 +179,9 @@ struct TcLaunch {
   float *out_r, *out_s;        // mode 1: out_s holds shared_parts partial [n, H] outputs
   int shared_parts;            // mode 1: K parts of the shared expert's down items (the schedule's ks)
   long long items_bound;
+  int fmt, group;              // routed record format and int4 group size (the shared expert is int8)
+  unsigned long long wait_ns;  // mbarrier wait bound (0: the default)
+  int stall_last;              // test hook (er_tc_test_stall): withhold the last item's accumulator
 };
 int launch_tc_grouped(const TcLaunch& L, cudaStream_t st);
 // two int8 slices and a scale per row of a [rows, K] fp32 / bf16 matrix

@@ -1,0 +1,414 @@
+// er_tc.cuh -- pieces shared by the tcgen05 grouped expert GEMMs (er_tc.cu:
+// int8 records; er_tcg.cu: group-scaled int4 records): PTX wrappers for
+// mbarriers, TMA, tcgen05 MMA / TMEM, the launch arguments, the work-item
+// lookup over the routing plan, and tensor-map encoding.
+#pragma once
+
+#include <cuda.h>
+#include <string.h>
+
+#include "er_internal.cuh"
+
+namespace er {
+
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;  // 2 s: bound of every mbarrier wait
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with `parity` to complete. Returns false (and
+// raises the CTA's abort flag) after limit_ns, or at once if another role
+// already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long limit_ns) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > limit_ns) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+// One lane polls, the whole warp learns the outcome; the warp then syncs so
+// every lane's later accesses are ordered after the acquire.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int lane,
+                                          unsigned long long limit_ns) {
+  bool w = true;
+  if (lane == 0) w = mbar_wait(bar, parity, abort_flag, limit_ns);
+  w = __shfl_sync(0xffffffffu, (int)w, 0) != 0;
+  __syncwarp();
+  return w;
+}
+// Bounded wait used while draining after an abort (no abort check).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned long long ns) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_test(bar, parity) && globaltimer() - t0 < ns) {
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+// Pair forms: the tile lands in this CTA's shared memory and completes on the
+// barrier at shared::cluster address `bar` (CTA 0's full barrier). Plain
+// loads of this GPU's memory; no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+template <int CG>
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int x, int y) {
+  if constexpr (CG == 1)
+    tma_load_2d(dst, map, bar, x, y);
+  else
+    tma_load_2d_pair(dst, map, bar_c, x, y);
+}
+template <int CG>
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int x, int y,
+                                       int z) {
+  if constexpr (CG == 1)
+    tma_load_3d(dst, map, bar, x, y, z);
+  else
+    tma_load_3d_pair(dst, map, bar_c, x, y, z);
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), LBO unused (1), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::i8: D s32, A and B signed int8, both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+template <int CG>
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  if constexpr (CG == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+// Pair kernels arrive on the barrier at the same offset in both CTAs.
+template <int CG>
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  if constexpr (CG == 1)
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+  else
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+template <int CG>
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+  if constexpr (CG == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  } else {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+}
+template <int CG>
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t cols) {
+  if constexpr (CG == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+  else
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+}
+
+// ---- clusters (SM pairs)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the variable at shared::cta address `a` in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// Orders this thread's earlier generic-proxy shared-memory writes before later
+// async-proxy reads of them (operands written by threads, read by tcgen05.mma).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// launch arguments and the work-item lookup
+// ---------------------------------------------------------------------------
+
+struct TcMaps {
+  CUtensorMap a_routed[2];  // mode 0: gate, up (64-row boxes) over the arena; mode 1: down in [0]
+  CUtensorMap a_shared[2];  // the same for the shared-expert record (2-D)
+  CUtensorMap b_routed[2];  // activation slices 0 / 1 of the routed rows (mode 0: all nk + n rows)
+  CUtensorMap b_shared[2];  // mode 1: activation slices of the shared rows
+};
+
+struct TcArgs {
+  GroupArgs g;
+  const uint8_t* arena;      // base of the routed-record arena
+  int arena_slots;
+  size_t record_bytes;
+  int sched;
+  const float* xscale_r;     // per-row slice scale of the B rows (routed / all rows in mode 0)
+  const float* xscale_s;     // mode 1: shared rows
+  float* out_r;              // mode 0: act routed [nk, I]; mode 1: y routed [nk, H]
+  float* out_s;              // mode 0: act shared [n, Is]; mode 1: shared_parts partial y shared [n, H]
+  int shared_parts;          // mode 1: K parts of each shared-expert tile (1: no split)
+  Plan* plan_rw;             // error bits
+  unsigned long long wait_ns;  // bound of every mbarrier wait (kDefaultWaitNs unless a test shortens it)
+  int stall_last;            // test hook: nonzero -> the MMA issuer never completes the accumulator of the
+                             // launch's last item, so its epilogue wait runs out (that item is its CTA's
+                             // last: no copy is in flight when the wait gives up)
+};
+
+// The plan's schedule, copied into shared memory once per CTA so that the
+// per-item lookups of every role (a binary search over the item prefix,
+// then the group's rows and record) cost no global-memory round trips.
+// Entries are indexed by active position a, not by group id.
+struct TcPlanCache {
+  int total;       // work items of this schedule
+  int num_active;  // active groups (routed, then the shared expert)
+  int nk;
+  int item_start[kMaxExperts + 2];
+  int group[kMaxExperts + 1];   // group id (E = shared expert)
+  int rows[kMaxExperts + 1];    // tokens of the group
+  int offset[kMaxExperts + 1];  // first expert-sorted position (routed groups)
+  int slot[kMaxExperts + 1];    // arena slot of the group's record; -1 outside the arena
+};
+
+struct TcItem {
+  int g, shared, valid;
+  int unit0;   // first unit of the tile (mode 0: intermediate column; mode 1: hidden row)
+  int tok0;    // first token of the tile within the group
+  int nvalid;  // tokens in the tile
+  int npad;    // tokens rounded up to 16
+  int brow0;   // first B row in the operand matrix
+  int slot;    // arena slot of the routed record
+  int units;
+  int kb0, nkb;  // the item's k-blocks: [kb0, kb0 + nkb)
+  int part;      // mode 1 shared items: which K part (partial output) the item computes
+};
+
+// Copies the schedule `t.sched` of the plan into `pc` (all threads take part;
+// a __syncthreads must follow before any lookup).
+__device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) {
+  const Plan* P = t.g.plan;
+  const int na = min(P->num_active, kMaxExperts + 1);
+  for (int a = threadIdx.x; a <= na; a += blockDim.x) {
+    pc->item_start[a] = P->item_start[t.sched][a];
+    if (a == na) continue;
+    const int g = P->active[a];
+    pc->group[a] = g;
+    pc->rows[a] = P->counts[g];
+    const bool shared = g == t.g.E;
+    pc->offset[a] = shared ? 0 : P->offsets[g];
+    int slot = 0;
+    if (!shared) {
+      const uint64_t addr = t.g.expert_records[g];
+      const uint64_t base = (uint64_t)t.arena;
+      slot = -1;  // record outside the arena: reported, never loaded
+      if (addr >= base && (addr - base) % t.record_bytes == 0 && (addr - base) / t.record_bytes < (uint64_t)t.arena_slots)
+        slot = (int)((addr - base) / t.record_bytes);
+    }
+    pc->slot[a] = slot;
+  }
+  if (threadIdx.x == 0) {
+    pc->num_active = na;
+    pc->total = P->item_start[t.sched][na];
+    pc->nk = P->nk;
+  }
+}
+
+// Locate work item `item`: the group (binary search over the item prefix),
+// its token tile and output-unit tile, and the item's k-blocks of KBLK K
+// elements (the shared expert's down tiles in `t.shared_parts` K parts).
+// UNITS = output units per item. Returns false past the last item.
+template <int MODE, int KBLK, int UNITS, int TT>
+__device__ __forceinline__ bool tc_item_at(const TcArgs& t, const TcPlanCache* pc, int item, TcItem& it) {
+  const int na = pc->num_active;
+  if (item >= pc->total || na <= 0) return false;
+  int lo = 0, hi = na - 1;  // largest a with item_start[a] <= item
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pc->item_start[mid] <= item)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  const int local = item - pc->item_start[lo];
+  const int g = pc->group[lo];
+  it.g = g;
+  it.shared = (g == t.g.E);
+  const int inter = it.shared ? t.g.Is : t.g.I;
+  it.units = MODE == 0 ? inter : t.g.H;
+  const int K = MODE == 0 ? t.g.H : inter;
+  const int blocks = (K + KBLK - 1) / KBLK;
+  const int ntiles = (it.units + UNITS - 1) / UNITS;
+  int tile = local;
+  it.kb0 = 0;
+  it.nkb = blocks;
+  it.part = 0;
+  if (MODE == 1 && it.shared && t.shared_parts > 1) {
+    // the K parts of one tile are adjacent items (different CTAs); part p
+    // covers k-blocks [p span, min(blocks, (p + 1) span)), none empty
+    const int span = (blocks + t.shared_parts - 1) / t.shared_parts;
+    tile = local / t.shared_parts;
+    it.part = local % t.shared_parts;
+    it.kb0 = it.part * span;
+    it.nkb = min(blocks - it.kb0, span);
+  }
+  it.tok0 = (tile / ntiles) * TT;
+  it.unit0 = (tile % ntiles) * UNITS;
+  it.nvalid = min(TT, pc->rows[lo] - it.tok0);
+  it.npad = (it.nvalid + 15) & ~15;
+  if (MODE == 0)
+    it.brow0 = (it.shared ? pc->nk : pc->offset[lo]) + it.tok0;
+  else
+    it.brow0 = pc->offset[lo] + it.tok0;
+  it.slot = it.shared ? 0 : pc->slot[lo];
+  it.valid = it.slot >= 0;
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// uint8 tensor map, K innermost (contiguous), box box_k x box_rows [x 1]:
+// 128-byte swizzle for MMA operand tiles (box_k = 128), none for staged tiles.
+inline int make_map(CUtensorMap* m, const void* base, int rank, uint64_t k, uint64_t rows, uint64_t slots,
+                    uint64_t row_stride, uint64_t slot_stride, uint32_t box_rows, const char* what,
+                    uint32_t box_k = 128, bool swizzle = true) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ER_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (((uintptr_t)base & 15) || (row_stride & 15) || (rank == 3 && (slot_stride & 15)))
+    return fail(ER_EINVAL, "tensor map %s: base and strides must be 16-byte aligned", what);
+  if (box_k % 16 || (swizzle && box_k != 128))
+    return fail(ER_EINVAL, "tensor map %s: box width %u bytes", what, box_k);
+  const cuuint64_t dims[3] = {k, rows, slots};
+  const cuuint64_t strides[2] = {row_stride, slot_stride};
+  const cuuint32_t box[3] = {box_k, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ER_ECUDA, "cuTensorMapEncodeTiled(%s) failed (%d)", what, (int)r);
+  return ER_OK;
+}
+
+}  // namespace er
