@@ -123,6 +123,7 @@ SIGNATURES: dict[str, tuple] = {
     "er_moe_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_block": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp, C.c_size_t, _vp]),
     "er_moe_block_noalloc": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp]),
+    "er_tc_test_stall": (_i, [C.c_ulonglong, _i]),
     "er_moe_rows_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_rows": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeRowsIO), _vp, C.c_size_t, _vp]),
     "er_moe_shared_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),

@@ -184,6 +184,8 @@ struct TcLaunch {
   int stall_last;              // test hook (er_tc_test_stall): withhold the last item's accumulator
 };
 int launch_tc_grouped(const TcLaunch& L, cudaStream_t st);
+// the same for int4 routed records (group-scaled; er_tcg.cu); the shared expert stays int8
+int launch_tcg_grouped(const TcLaunch& L, cudaStream_t st);
 // two int8 slices and a scale per row of a [rows, K] fp32 / bf16 matrix
 int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, int8_t* s1, float* scale,
                       cudaStream_t st);
@@ -197,7 +199,14 @@ struct SliceSet {
 // two such sets in one launch (K up to 8192 each)
 int launch_slice_sets(const SliceSet& a, const SliceSet& b, cudaStream_t st);
 // tokens per tcgen05 work item: 16 when every group fits (n <= 16), else 128
-inline int tc_tok_tile(int n) { return n <= 16 ? 16 : 128; }
+// for int8 records (SM pairs) and 64 for int4 records (single SMs)
+inline int tc_tok_tile(int n, int fmt = ER_FMT_INT8) { return n <= 16 ? 16 : (fmt == ER_FMT_INT8 ? 128 : 64); }
+// whether the int4 tensor-core path takes these shapes (groups in whole
+// 32-input MMA steps, rows in whole 16-byte TMA strides)
+inline bool tcg_shapes_ok(int H, int I, int Is, int group) {
+  return group > 0 && group % 32 == 0 && H % group == 0 && I % group == 0 && H % 128 == 0 && I % 32 == 0 &&
+         Is % 128 == 0;
+}
 constexpr int kTcKBlock = 256;  // K elements per tcgen05 pipeline stage
 // Decode tiles split the shared expert's down product (K = Is, Is / I times a
 // routed expert's) into parts of about a routed expert's K, so its items take

@@ -16,6 +16,12 @@ namespace er {
 
 enum RunMode { kBlock = 0, kRows = 1, kShared = 2 };
 
+// Test hooks of the tensor-core path (er_tc_test_stall): the bound of every
+// mbarrier wait (0: the kernels' default) and which int8 launch withholds
+// its last item's accumulator (0 none, 1 gate/up, 2 down).
+static unsigned long long g_tc_test_wait_ns = 0;
+static int g_tc_test_stall = 0;
+
 struct Run {
   int mode;
   const void* h;  // tokens (kRows: the rows)
@@ -39,7 +45,7 @@ static bool run_shared(int mode) { return mode != kRows; }
 
 // partial outputs of the shared expert's down product (K parts of its tiles)
 static int shared_parts(const er_moe_weights* w, int n, int path) {
-  return path == ER_PATH_TC ? tc_shared_parts(tc_tok_tile(n), w->inter, w->shared_inter) : 1;
+  return path == ER_PATH_TC ? tc_shared_parts(tc_tok_tile(n, w->expert_fmt), w->inter, w->shared_inter) : 1;
 }
 
 struct WsLayout {
@@ -117,11 +123,18 @@ static int validate(const er_moe_weights* w, int mode) {
   return ER_OK;
 }
 
-// AUTO: the tensor-core path when it can run (int8 records in an arena),
-// else the weight-streaming GEMV for decode batches and the SIMT GEMM beyond.
+// whether the tensor-core path takes this block's records: int8, or int4
+// whose groups and rows fit its tiles
+static bool tc_format_ok(const er_moe_weights* w) {
+  return w->expert_fmt == ER_FMT_INT8 || tcg_shapes_ok(w->hidden, w->inter, w->shared_inter, w->group);
+}
+
+// AUTO: the tensor-core path when it can run (records in an arena, a format
+// it takes), else the weight-streaming GEMV for decode batches and the SIMT
+// GEMM beyond.
 static int pick_path(const er_moe_weights* w, int path, int n) {
   if (path != ER_PATH_AUTO) return path;
-  if (w->expert_fmt == ER_FMT_INT8 && w->record_arena && w->arena_slots > 0) return ER_PATH_TC;
+  if (tc_format_ok(w) && w->record_arena && w->arena_slots > 0) return ER_PATH_TC;
   return n <= kGemvMaxTok ? ER_PATH_GEMV : ER_PATH_GEMM;
 }
 
@@ -142,8 +155,11 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
   if (path != ER_PATH_GEMV && path != ER_PATH_GEMM && path != ER_PATH_TC)
     return fail(ER_EINVAL, "er_moe: unknown path %d", r.path);
   if (path == ER_PATH_TC) {
-    if (w->expert_fmt != ER_FMT_INT8)
-      return fail(ER_EINVAL, "er_moe: the tensor-core path takes int8 expert records");
+    if (!tc_format_ok(w))
+      return fail(ER_EINVAL,
+                  "er_moe: the tensor-core path takes int8 records, or int4 records whose group (%d) is a multiple "
+                  "of 32 dividing hidden and inter, with hidden and shared inter multiples of 128",
+                  w->group);
     if (mode != kShared && (!w->record_arena || w->arena_slots < 1 || ((uintptr_t)w->record_arena & 15)))
       return fail(ER_EINVAL, "er_moe: the tensor-core path needs the record arena (record_arena, arena_slots)");
   }
@@ -244,8 +260,9 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     specs[0] = SchedSpec{0, kGemvUnitsGU, 0};
     specs[1] = SchedSpec{0, kGemvUnitsDN, 1};
   } else if (path == ER_PATH_TC) {
-    specs[0] = SchedSpec{tc_tok_tile(n), tc_units_gu(tc_tok_tile(n)), 0};
-    specs[1] = SchedSpec{tc_tok_tile(n), tc_units_dn(tc_tok_tile(n)), 1, shared_parts(w, n, path)};
+    const int tt = tc_tok_tile(n, w->expert_fmt);
+    specs[0] = SchedSpec{tt, tc_units_gu(tt), 0};
+    specs[1] = SchedSpec{tt, tc_units_dn(tt), 1, shared_parts(w, n, path)};
   } else {
     specs[0] = SchedSpec{kSimtBM, kSimtBN, 0};
     specs[1] = SchedSpec{kSimtBM, kSimtBN, 1};
@@ -296,11 +313,15 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     tl.g = ga;
     tl.arena = w->record_arena;
     tl.arena_slots = w->arena_slots;
-    tl.record_bytes = er_record_bytes(ER_FMT_INT8, H, w->inter, 0);
+    tl.fmt = w->expert_fmt;
+    tl.group = w->expert_fmt == ER_FMT_INT8 ? 1 : w->group;
+    tl.record_bytes = er_record_bytes(w->expert_fmt, H, w->inter, w->group);
     tl.nk = (int)nk;
     tl.n = shared ? n : 0;
     tl.has_shared = shared;
-    tl.tok_tile = tc_tok_tile(n);
+    tl.tok_tile = tc_tok_tile(n, w->expert_fmt);
+    tl.wait_ns = g_tc_test_wait_ns;
+    tl.stall_last = 0;
     tl.mode = 0;
     tl.sched = 0;
     tl.b0_r = xs0;
@@ -309,7 +330,8 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     tl.out_r = act_r;
     tl.out_s = act_s;
     tl.items_bound = b0;
-    if (int rc = launch_tc_grouped(tl, st)) return rc;
+    tl.stall_last = g_tc_test_stall == 1;
+    if (int rc = (tl.fmt == ER_FMT_INT8 ? launch_tc_grouped : launch_tcg_grouped)(tl, st)) return rc;
     if (int rc = mark(3)) return rc;
     if (nk > 0 || shared) {
       const SliceSet routed{act_r, (int)nk, w->inter, as0_r, as1_r, ascale_r};
@@ -329,7 +351,8 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     tl.out_s = y_s;
     tl.shared_parts = specs[1].ks;
     tl.items_bound = b1;
-    if (int rc = launch_tc_grouped(tl, st)) return rc;
+    tl.stall_last = g_tc_test_stall == 2;
+    if (int rc = (tl.fmt == ER_FMT_INT8 ? launch_tc_grouped : launch_tcg_grouped)(tl, st)) return rc;
   } else if (path == ER_PATH_GEMV) {
     if (int rc = launch_gemv_grouped(ga, 0, 0, r.h, r.h_dtype, act_r, act_s, nullptr, nullptr, b0, st)) return rc;
     if (int rc = mark(3)) return rc;
@@ -353,6 +376,13 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
 }  // namespace er
 
 using namespace er;
+
+extern "C" int er_tc_test_stall(unsigned long long wait_ns, int stall) {
+  if (stall < 0 || stall > 2) return fail(ER_EINVAL, "er_tc_test_stall: stall %d (0 none, 1 gate/up, 2 down)", stall);
+  g_tc_test_wait_ns = wait_ns;
+  g_tc_test_stall = stall;
+  return ER_OK;
+}
 
 extern "C" size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path) {
   if (validate(w, kBlock) != ER_OK || n < 0) return 0;

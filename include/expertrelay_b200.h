@@ -65,10 +65,13 @@ extern "C" {
 #define ER_FMT_INT4_ZP 2   /* ER_FMT_INT4 + [gate z u8][up z][down z] after the scales, value = nibble - z */
 
 /* ---- expert-matrix execution paths ------------------------------------- */
-#define ER_PATH_AUTO 0     /* stream weights (GEMV) for small n, tiled GEMM otherwise */
+#define ER_PATH_AUTO 0     /* the tensor-core path for records in an arena of a format it takes; else
+                              stream weights (GEMV) for small n, tiled GEMM otherwise */
 #define ER_PATH_GEMV 1     /* weight-streaming grouped GEMV, any n (slow for large n) */
 #define ER_PATH_GEMM 2     /* tiled grouped GEMM, fp32 FMA (exact-fp32 path) */
-#define ER_PATH_TC 3       /* tcgen05 grouped GEMM: int8 weights x two int8 activation slices, int32 accumulate */
+#define ER_PATH_TC 3       /* tcgen05 grouped GEMM: int8 weights (int4 records: codes q - z, unpacked in
+                              shared memory) x two int8 activation slices, int32 accumulate (int4: per
+                              scale group, the group scale applied to each partial sum) */
 
 /* library identity / diagnostics */
 ER_API int er_version(void);                 /* e.g. 100 = 0.1.0 */
@@ -163,6 +166,15 @@ ER_API size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path);
  * stream capture. All calls share the array, so calls that overlap on the GPU
  * race and must be serialised by the caller. */
 ER_API int er_moe_block_noalloc(const er_moe_weights* w, const er_moe_io* io, void* stream);
+/* Test hook of the tensor-core path (no counterpart in the reference, whose
+ * CPU path has no device waits): every later er_moe_block call bounds each
+ * mbarrier wait of its tensor-core kernels by wait_ns (0: the default, 2 s)
+ * and, with stall = 1 (gate/up) or 2 (down), the int8 kernel of that step
+ * never completes its last work item's accumulator, so that item's epilogue
+ * wait runs out: the kernel returns, the plan's error bit 8 is set and the
+ * block writes NaN rows. (0, 0) restores normal operation. Process-wide,
+ * not thread-safe; for tests of the bounded-wait error path only. */
+ER_API int er_tc_test_stall(unsigned long long wait_ns, int stall);
 ER_API int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
                  void* stream);
 

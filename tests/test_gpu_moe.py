@@ -34,6 +34,8 @@ PATHS = {"gemv": _lib.PATH_GEMV, "gemm": _lib.PATH_GEMM}
 # the tensor-core path (int8 records only): int8 weights x two int8 activation slices
 PATHS_INT8 = {**PATHS, "tc": _lib.PATH_TC}
 TOL = {"gemv": FP32_FMA_TOL, "gemm": FP32_FMA_TOL, "tc": FP32_TOL}
+# int4 records: the tensor-core path unpacks the codes in shared memory
+PATHS_INT4 = PATHS_INT8
 
 
 def _run(block: MoeBlock, x: np.ndarray, path: int, logits: np.ndarray | None = None, dtype=torch.float32):
@@ -186,18 +188,53 @@ def gptq_block(cuda):
     return blk, MoeBlock.from_host_block(blk, device=cuda), gptq_oracle_weights(blk)
 
 
-@pytest.mark.parametrize(("n", "path"), [(1, "gemv"), (1, "gemm"), (8, "gemv"), (64, "gemm"), (512, "gemm")])
+GPTQ_CASES = [(1, "gemv"), (1, "gemm"), (8, "gemv"), (64, "gemm"), (512, "gemm"),
+              (1, "tc"), (8, "tc"), (17, "tc"), (64, "tc"), (130, "tc"), (512, "tc")]
+
+
+@pytest.mark.parametrize(("n", "path"), GPTQ_CASES)
 def test_gptq_asym_block_against_gptq_formula(gptq_block, n, path):
     """Asymmetric GPTQ experts: the oracle uses weights dequantized from the
-    raw GPTQ v1 tensors (qweight/qzeros/scales/g_idx), in float64."""
+    raw GPTQ v1 tensors (qweight/qzeros/scales/g_idx), in float64. The
+    tensor-core path (codes q - z unpacked in shared memory, exact int32 sums
+    per group of 128 inputs times the group's fp16 scale) is held to the fp32
+    tolerance; the fp32-FMA paths also to the tighter one."""
     blk, dev, ow = gptq_block
     x = synth.make_tokens(200 + n, n)
-    y, lg, idx, _ = _run(dev, x, PATHS[path])
+    y, lg, idx, _ = _run(dev, x, PATHS_INT4[path])
     exact = O.moe_block_f64(x, ow, logits=lg)
     ref32 = O.moe_block(x, ow, logits=lg)
     np.testing.assert_array_equal(idx, ref32.selected)
     assert O.rel_l2(y, exact) < FP32_TOL
-    assert O.rel_l2(y, ref32.y) < FP32_FMA_TOL
+    if path != "tc":
+        assert O.rel_l2(y, ref32.y) < FP32_FMA_TOL
+
+
+def test_gptq_asym_tc_is_the_default_and_repeats(gptq_block):
+    """With the records in an arena the default path is the tensor-core one,
+    and its output does not change from call to call."""
+    _, dev, _ = gptq_block
+    h = torch.from_numpy(synth.make_tokens(9, 40)).to(dev.device)
+    y_auto = dev.forward(h, path=_lib.PATH_AUTO)
+    y_tc = dev.forward(h, path=_lib.PATH_TC)
+    y_again = dev.forward(h, path=_lib.PATH_TC)
+    torch.cuda.synchronize()
+    assert torch.equal(y_auto, y_tc) and torch.equal(y_tc, y_again)
+
+
+@pytest.mark.parametrize(("group", "n"), [(128, 3), (64, 24), (32, 70)])
+def test_int4_store_block_tc_groups(cuda, group, n):
+    """Symmetric int4 store records (value = nibble - 8) on the tensor-core
+    path at several group sizes (1, 2 and 4 groups per 128-input block) and
+    token counts over one and several token tiles."""
+    blk = synth.make_block(40 + group, fmt="int4", group=group, num_experts=16)
+    dev = MoeBlock.from_host_block(blk, device=cuda)
+    x = synth.make_tokens(group + n, n)
+    y, lg, idx, _ = _run(dev, x, _lib.PATH_TC)
+    ow = oracle_weights(blk)
+    ref = O.moe_block(x, ow, logits=lg)
+    np.testing.assert_array_equal(idx, ref.selected)
+    assert O.rel_l2(y, ref.y) < FP32_TOL
 
 
 def test_int4_store_block(cuda):
@@ -205,11 +242,11 @@ def test_int4_store_block(cuda):
     blk = synth.make_block(4, fmt="int4", group=128, num_experts=16)
     dev = MoeBlock.from_host_block(blk, device=cuda)
     x = synth.make_tokens(4, 6)
-    for path in PATHS.values():
+    for name, path in PATHS_INT4.items():
         y, lg, idx, _ = _run(dev, x, path)
         ref = O.moe_block(x, oracle_weights(blk), logits=lg)
         np.testing.assert_array_equal(idx, ref.selected)
-        assert O.rel_l2(y, ref.y) < FP32_FMA_TOL
+        assert O.rel_l2(y, ref.y) < TOL[name]
 
 
 @pytest.fixture(scope="module")
