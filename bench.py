@@ -737,7 +737,10 @@ def summary_of(line: dict) -> dict:
         for k in ("decode1", "prefill512"):
             out[f"gptq_{k}"] = {"path": pick(line, "gptq", k, "path"), "ms": pick(line, "gptq", k, "ms_per_block"),
                                 "hbm_frac": pick(line, "gptq", k, "hbm", "frac"),
-                                "tensor_frac": pick(line, "gptq", k, "tensor", "frac")}
+                                "tensor_frac": pick(line, "gptq", k, "tensor", "frac"),
+                                "gate_up_hbm_frac": pick(line, "gptq", k, "expert_kernels", "gate_up", "hbm_frac"),
+                                "gate_up_tensor_frac": pick(line, "gptq", k, "expert_kernels", "gate_up",
+                                                            "tensor_frac")}
     if "expert_parallel" in line:
         out["ep"] = {"value": pick(line, "expert_parallel", "value"), "ms": pick(line, "expert_parallel", "ms_per_step")}
     if "full_model" in line:
@@ -900,11 +903,13 @@ def full_model_side(args, dev) -> dict:
 def gptq_side(args, dev, peaks, peak_src) -> dict:
     """The MoE block with int4 GPTQ-style routed experts (asymmetric 4-bit,
     group 128 along the input, fp16 scales, 4-bit zero points; the shared
-    expert int8), at 1 decode token (exact-fp32 weight-streaming GEMV) and at
-    512 tokens (exact-fp32 SIMT GEMM). Each step replays the captured forward
-    after an L2 flush. Both report the block's algorithmic weight bytes
-    against HBM and its FLOPs against dense bf16 (512 tokens sits near the
-    ridge between the two)."""
+    expert int8), at 1 decode token and at 512 tokens, on the tcgen05 path
+    (the default for these records) and, for comparison, on the exact-fp32
+    weight-streaming GEMV (1 token) / SIMT GEMM (512 tokens). Each step
+    replays the captured forward after an L2 flush. Both report the block's
+    algorithmic weight bytes against HBM and its FLOPs against dense bf16
+    (512 tokens sits near the ridge between the two); the gate/up and down
+    kernels are also timed alone (stage events in a second capture)."""
     import torch
 
     from expertrelay_b200 import _lib, synth
@@ -914,39 +919,72 @@ def gptq_side(args, dev, peaks, peak_src) -> dict:
     mb = MoeBlock.from_host_block(block, device=dev)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(_lib.MOE_STAGES) + 1)]
+    for e in ev:
+        e.record()
     steps = max(args.steps, 20)
     out = {}
-    for name, n, path, pname in (("decode1", 1, _lib.PATH_GEMV, "gemv"), ("prefill512", 512, _lib.PATH_GEMM, "gemm")):
+    cases = (("decode1", 1, (("tc", _lib.PATH_TC), ("gemv", _lib.PATH_GEMV))),
+             ("prefill512", 512, (("tc", _lib.PATH_TC), ("gemm", _lib.PATH_GEMM))))
+    for name, n, paths in cases:
         h = torch.from_numpy(synth.make_tokens(args.seed, n, block.hidden)).to(dev)
-        _, _, idx, _ = mb.forward(h, path=path, return_routing=True)
+        _, _, idx, _ = mb.forward(h, path=_lib.PATH_TC, return_routing=True)
         acct = accounting(block, n, idx.cpu().numpy(), 4)
-        cap = mb.capture(n, path=path)
-        cap.h.copy_(h)
-        for _ in range(max(args.warmup, 3)):
-            cap.replay()
-        torch.cuda.synchronize()
-        tot = 0.0
-        for _ in range(steps):
-            flush.zero_()
-            t0.record()
-            cap.replay()
-            t1.record()
-            t1.synchronize()
-            tot += t0.elapsed_time(t1)
-        sec = tot / steps / 1e3
-        gbs = acct["block_weight_bytes"] / sec / 1e9
-        tfs = acct["block_flops"] / sec / 1e12
-        out[name] = {
-            "tokens": n, "path": pname, "ms_per_block": sec * 1e3, "tokens_per_s": n / sec,
-            "unique_experts": acct["unique_experts"],
-            "hbm": {"achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
-                    "algorithmic_bytes": acct["block_weight_bytes"], "peak_source": f"of {peak_src}"},
-            "tensor": {"achieved": tfs, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                       "frac": tfs / peaks["bf16_tflops"], "algorithmic_flops": acct["block_flops"],
-                       "peak_kind": "burst bf16 GEMM",
-                       "peak_source": f"of {peak_src}"},
-        }
-        del cap
+        res = {}
+        for pname, path in paths:
+            cap = mb.capture(n, path=path)
+            cap_st = mb.capture(n, path=path, stage_events=ev)
+            cap.h.copy_(h)
+            cap_st.h.copy_(h)
+            for _ in range(max(args.warmup, 3)):
+                cap.replay()
+                cap_st.replay()
+            torch.cuda.synchronize()
+            tot = 0.0
+            stage = {s: 0.0 for s in _lib.MOE_STAGES}
+            for _ in range(steps):
+                flush.zero_()
+                t0.record()
+                cap.replay()
+                t1.record()
+                t1.synchronize()
+                tot += t0.elapsed_time(t1)
+                flush.zero_()
+                cap_st.replay()
+                ev[-1].synchronize()
+                for j, s in enumerate(_lib.MOE_STAGES):
+                    stage[s] += ev[j].elapsed_time(ev[j + 1])
+            sec = tot / steps / 1e3
+            stage = {s: v / steps for s, v in stage.items()}
+            gbs = acct["block_weight_bytes"] / sec / 1e9
+            tfs = acct["block_flops"] / sec / 1e12
+            kern = {
+                "gate_up": {"ms": stage["gate_up"],
+                            "GBps": acct["gate_up_bytes"] / (stage["gate_up"] / 1e3) / 1e9,
+                            "TFLOPs": acct["gate_up_flops"] / (stage["gate_up"] / 1e3) / 1e12},
+                "down": {"ms": stage["down"],
+                         "GBps": acct["down_bytes"] / (stage["down"] / 1e3) / 1e9,
+                         "TFLOPs": acct["down_flops"] / (stage["down"] / 1e3) / 1e12},
+            }
+            for k in kern.values():
+                k["hbm_frac"] = k["GBps"] / peaks["hbm_gbs"]
+                k["tensor_frac"] = k["TFLOPs"] / peaks["bf16_tflops"]
+            res[pname] = {
+                "tokens": n, "path": pname, "ms_per_block": sec * 1e3, "tokens_per_s": n / sec,
+                "unique_experts": acct["unique_experts"],
+                "hbm": {"achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+                        "algorithmic_bytes": acct["block_weight_bytes"], "peak_source": f"of {peak_src}"},
+                "tensor": {"achieved": tfs, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                           "frac": tfs / peaks["bf16_tflops"], "algorithmic_flops": acct["block_flops"],
+                           "peak_kind": "burst bf16 GEMM", "peak_source": f"of {peak_src}"},
+                "stages_ms": stage,
+                "expert_kernels": kern,
+            }
+            del cap, cap_st
+        best = min(res, key=lambda k: res[k]["ms_per_block"])
+        out[name] = {**res[best], "best_path": best,
+                     "other_paths": {k: {"ms_per_block": v["ms_per_block"], "hbm_frac": v["hbm"]["frac"],
+                                         "tensor_frac": v["tensor"]["frac"]} for k, v in res.items() if k != best}}
     del mb
     torch.cuda.empty_cache()
     return {"workload": "int4 GPTQ-style experts (asymmetric, group 128, fp16 scales, 4-bit zero points), "

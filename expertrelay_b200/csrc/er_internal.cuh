@@ -205,7 +205,7 @@ inline int tc_tok_tile(int n, int fmt = ER_FMT_INT8) { return n <= 16 ? 16 : (fm
 // 32-input MMA steps, rows in whole 16-byte TMA strides)
 inline bool tcg_shapes_ok(int H, int I, int Is, int group) {
   return group > 0 && group % 32 == 0 && H % group == 0 && I % group == 0 && H % 128 == 0 && I % 32 == 0 &&
-         Is % 128 == 0;
+         Is % 128 == 0 && H / group <= 64 && I / group <= 64;
 }
 constexpr int kTcKBlock = 256;  // K elements per tcgen05 pipeline stage
 // Decode tiles split the shared expert's down product (K = Is, Is / I times a

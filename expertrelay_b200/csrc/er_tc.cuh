@@ -44,21 +44,34 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend hint: the thread sleeps until the phase completes
+// (it is woken then) or hint_ns pass, instead of spinning on the barrier and
+// taking issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase with `parity` to complete. Returns false (and
-// raises the CTA's abort flag) after limit_ns, or at once if another role
-// already aborted.
+// raises the CTA's abort flag) after limit_ns, or as soon as it sees that
+// another role already aborted (within one suspend hint, <= 100 us).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned long long limit_ns) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > limit_ns) {
-        *abort_flag = 1;
-        return false;
-      }
+  const uint32_t hint = (uint32_t)(limit_ns / 16 < 100000ull ? limit_ns / 16 + 1 : 100000ull);
+  for (;;) {
+    if (mbar_test_sleep(bar, parity, hint)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > limit_ns) {
+      *abort_flag = 1;
+      return false;
     }
   }
 }

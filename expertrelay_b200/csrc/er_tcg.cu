@@ -59,7 +59,10 @@ struct TcgGeom {
   static constexpr int kUnits = MODE == 0 ? 64 : 128;  // intermediate columns / hidden rows per item
   static constexpr int kChunks = (TT + 31) / 32;       // 16-token chunks per epilogue warp
   static constexpr size_t kXchBytes = MODE == 0 ? 4 * 2 * 16 * 32 * 4 : 0;
-  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + kXchBytes + 2048 + sizeof(TcPlanCache);
+  static constexpr int kMaxGroups = 64;               // scale groups per weight row (K / G) the kernel takes
+  static constexpr size_t kZeroBytes = 128 * kMaxGroups;  // one item's zero points, [row][group]
+  static constexpr size_t kSmem =
+      1024 + (size_t)kStages * kStageBytes + kXchBytes + 2048 + sizeof(TcPlanCache) + kZeroBytes;
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment (128-byte swizzle)");
   static_assert(kSlots >= 2, "at least two accumulators");
 };
@@ -121,6 +124,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   TcPlanCache* pc = reinterpret_cast<TcPlanCache*>(tail + Geo::kXchBytes + 2048);
+  uint8_t* zsm = reinterpret_cast<uint8_t*>(pc + 1);  // the transform's zero points of the current item
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -227,23 +231,50 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
       const RecordGeom rg{t.g.fmt, t.g.H, t.g.I, t.g.group};
       const int kfull = MODE == 0 ? t.g.H : t.g.I;  // inputs per row of the routed matrix
       const int gpr = kfull / t.g.group;              // scale groups per row
+      const bool zp = !it.shared && t.g.fmt == ER_FMT_INT4_ZP;
+      if (zp) {
+        // the item's zero points, [row][group], staged once per item. A warp
+        // reads only the rows it transforms (8 w + 0..7, + 32 q), so it stages
+        // just those and needs no barrier beyond its own (none that could
+        // outlast an abort of the other warps).
+        // All of a batch's loads are issued before any store, so the batch
+        // costs one memory latency (a load-then-store loop would pay one per
+        // iteration).
+        __syncwarp();  // the previous item's values are no longer read
+        constexpr int kZB = 16;  // bytes per lane per batch
+        for (int base = 0; base < 32 * gpr; base += 32 * kZB) {
+          uint8_t zb[kZB];
+#pragma unroll
+          for (int u = 0; u < kZB; ++u) {
+            const int i = base + u * 32 + lane;
+            zb[u] = 0;
+            if (i < 32 * gpr) {
+              const int j = i / gpr, gi = i - j * gpr;
+              const int r = 8 * (warp & 3) + (j & 7) + 32 * (j >> 3);
+              const int which = MODE == 0 ? (r < 64 ? 0 : 1) : 2;
+              const int mrow = min(it.unit0 + (MODE == 0 ? (r & 63) : r), rg.rows(which) - 1);
+              zb[u] = __ldg(rec + rg.zero_offset(which) + (size_t)mrow * gpr + gi);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kZB; ++u) {
+            const int i = base + u * 32 + lane;
+            if (i < 32 * gpr) {
+              const int j = i / gpr, gi = i - j * gpr;
+              zsm[(8 * (warp & 3) + (j & 7) + 32 * (j >> 3)) * gpr + gi] = zb[u];
+            }
+          }
+        }
+        __syncwarp();
+      }
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
         uint32_t zz[4] = {0x08080808u, 0x08080808u, 0x08080808u, 0x08080808u};
-        if (!it.shared && t.g.fmt == ER_FMT_INT4_ZP) {
-          // zero points of this thread's rows for the group of its chunk,
-          // fetched before the wait so their latency hides behind it
+        if (zp) {
           const int grp = min(((it.kb0 + kb) * 128 + 32 * c) / t.g.group, gpr - 1);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int r = r0 + 32 * q;
-            int which = MODE == 0 ? (r < 64 ? 0 : 1) : 2;
-            int mrow = it.unit0 + (MODE == 0 ? (r & 63) : r);
-            mrow = min(mrow, rg.rows(which) - 1);  // rows past the matrix multiply zero tokens only
-            const uint32_t z = __ldg(rec + rg.zero_offset(which) + (size_t)mrow * gpr + grp);
-            zz[q] = z * 0x01010101u;
-          }
+          for (int q = 0; q < 4; ++q) zz[q] = (uint32_t)zsm[(r0 + 32 * q) * gpr + grp] * 0x01010101u;
         }
         bool w = true;
         if (lane == 0) w = mbar_wait(&full[s], ph, abort_flag, wait_ns);
@@ -288,44 +319,46 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
       int gpos = 0;      // K elements of the current group issued so far
       uint32_t d = 0;    // its accumulator
       int slot = 0;
-      for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
+      // The whole warp runs the loop in step (waits polled by lane 0 and
+      // broadcast); only the MMAs and commits are issued by lane 0. A
+      // lane-0-only loop body with waits inside it cost over a thousand
+      // cycles per stage in branch and reconvergence overhead.
+      for (int kb = 0; ok && kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
-        bool w = true;
-        if (lane == 0) {
-          w = mbar_wait(&ready[s], ph, abort_flag, wait_ns);
-          if (w) {
-            tc_fence_after();
-            const uint32_t st = smem_u32(smem + (size_t)s * Geo::kStageBytes);
-            const uint32_t sa = st, sb = st + Geo::kABytes;
-#pragma unroll 1
-            for (int ks = 0; ks < 4; ++ks) {
-              const int k = (it.kb0 + kb) * 128 + ks * 32;
-              if (k >= sp.kend) break;
-              if (gpos == 0) {
-                slot = (int)(gc % NS);
-                if (!mbar_wait(&acc_empty[slot], ((gc / NS) & 1) ^ 1, abort_flag, wait_ns)) {
-                  w = false;
-                  break;
-                }
-                tc_fence_after();
-                d = tmem_base + slot * Geo::kSlotCols;
-              }
-              mma_i8<1>(d, umma_desc_sw128(sa + ks * 32), umma_desc_sw128(sb + ks * 32), idesc, gpos > 0 ? 1u : 0u);
-              gpos += 32;
-              if (gpos == sp.gk || k + 32 >= sp.kend) {
-                umma_commit<1>(&acc_full[slot]);  // this group's partial sums are ready
-                ++gc;
-                gpos = 0;
-              }
-            }
-            umma_commit<1>(&empty[s]);  // the stage is free once these MMAs have read it
-          }
-        }
-        if (!__shfl_sync(0xffffffffu, (int)w, 0)) {
+        if (!warp_wait(&ready[s], ph, abort_flag, lane, wait_ns)) {
           ok = false;
           break;
         }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + (size_t)s * Geo::kStageBytes);
+        const uint32_t sa = st, sb = st + Geo::kABytes;
+        const int k0 = (it.kb0 + kb) * 128;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const int k = k0 + ks * 32;
+          if (k < sp.kend) {
+            if (gpos == 0) {
+              slot = (int)(gc % NS);
+              if (!warp_wait(&acc_empty[slot], ((gc / NS) & 1) ^ 1, abort_flag, lane, wait_ns)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              d = tmem_base + slot * Geo::kSlotCols;
+            }
+            if (lane == 0)
+              mma_i8<1>(d, umma_desc_sw128(sa + ks * 32), umma_desc_sw128(sb + ks * 32), idesc, gpos > 0 ? 1u : 0u);
+            gpos += 32;
+            if (gpos == sp.gk || k + 32 >= sp.kend) {
+              if (lane == 0) umma_commit<1>(&acc_full[slot]);  // this group's partial sums are ready
+              ++gc;
+              gpos = 0;
+            }
+          }
+        }
+        if (lane == 0) umma_commit<1>(&empty[s]);  // the stage is free once these MMAs have read it
+        __syncwarp();
       }
     }
     if (lane == 0) {
@@ -390,35 +423,42 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
       for (int i = 0; i < Geo::kChunks; ++i)
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
-      float s_cur = sp.ngroups > 0 ? group_scale(0) : 0.f;
+      // group scales in batches of kGB, all of a batch fetched before its
+      // first accumulator wait (one latency per batch, not per group)
+      constexpr int kGB = 16;
 #pragma unroll 1
-      for (int g = 0; g < sp.ngroups; ++g) {
-        const float s_nxt = g + 1 < sp.ngroups ? group_scale(g + 1) : 0.f;  // fetched ahead of the wait
-        const int slot = (int)(gc % NS);
-        if (!warp_wait(&acc_full[slot], (gc / NS) & 1, abort_flag, lane, wait_ns)) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t tb = tmem_base + slot * Geo::kSlotCols + ((uint32_t)(quad * 32) << 16);
+      for (int g0 = 0; alive && g0 < sp.ngroups; g0 += kGB) {
+        float sc[kGB];
 #pragma unroll
-        for (int ci = 0; ci < Geo::kChunks; ++ci) {
-          const int c0 = half * 16 + 32 * ci;
-          if (c0 < it.npad) {  // the same for the whole warp
-            uint32_t v0[16], v1[16];
-            tmem_ld16(tb + c0, v0);
-            tmem_ld16(tb + TT + c0, v1);
-            tmem_ld_wait();
+        for (int i = 0; i < kGB; ++i) sc[i] = g0 + i < sp.ngroups ? group_scale(g0 + i) : 0.f;
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              acc[ci][j] = fmaf(s_cur, fmaf((float)(int)v1[j], 1.f / 256.f, (float)(int)v0[j]), acc[ci][j]);
+        for (int i = 0; i < kGB; ++i) {
+          if (g0 + i >= sp.ngroups) break;
+          const int slot = (int)(gc % NS);
+          if (!warp_wait(&acc_full[slot], (gc / NS) & 1, abort_flag, lane, wait_ns)) {
+            alive = false;
+            break;
           }
+          tc_fence_after();
+          const uint32_t tb = tmem_base + slot * Geo::kSlotCols + ((uint32_t)(quad * 32) << 16);
+#pragma unroll
+          for (int ci = 0; ci < Geo::kChunks; ++ci) {
+            const int c0 = half * 16 + 32 * ci;
+            if (c0 < it.npad) {  // the same for the whole warp
+              uint32_t v0[16], v1[16];
+              tmem_ld16(tb + c0, v0);
+              tmem_ld16(tb + TT + c0, v1);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                acc[ci][j] = fmaf(sc[i], fmaf((float)(int)v1[j], 1.f / 256.f, (float)(int)v0[j]), acc[ci][j]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[slot]);
+          ++gc;
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[slot]);
-        ++gc;
-        s_cur = s_nxt;
       }
       if (!alive) break;
       const int ld_out = MODE == 0 ? (it.shared ? t.g.Is : t.g.I) : t.g.H;
@@ -517,6 +557,8 @@ int launch_tcg_grouped(const TcLaunch& L, cudaStream_t st) {
   if (L.group <= 0 || L.group % 32 || a.H % L.group || a.I % L.group)
     return fail(ER_EINVAL, "int4 tensor-core path: group %d must be a multiple of 32 dividing %d and %d", L.group, a.H,
                 a.I);
+  if (a.H / L.group > TcgGeom<0, 16>::kMaxGroups || a.I / L.group > TcgGeom<0, 16>::kMaxGroups)
+    return fail(ER_EINVAL, "int4 tensor-core path: more than %d groups per row", TcgGeom<0, 16>::kMaxGroups);
   if (a.H % 128 || a.I % 32 || a.Is % 128)
     return fail(ER_EINVAL, "int4 tensor-core path: hidden %d (x128), inter %d (x32), shared inter %d (x128)", a.H, a.I,
                 a.Is);
