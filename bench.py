@@ -27,7 +27,9 @@ experts (asymmetric, group 128) at 1 and 512 tokens (--no-gptq skips it).
 On every N the line carries `expert_parallel`: the MoE layer of the
 expert-parallel prefill (32 x 2048 tokens split over the N ranks, the 60
 experts spread over the GPUs, NCCL all-to-all of rows and results), timed
-as max over ranks (--no-ep skips it).
+as max over ranks (--no-ep skips it). On N > 1 GPUs that layer is the
+headline `value` (strong scaling) and the independent per-GPU replicas of
+the block move to `replicas`.
 
 --impl reference times the CPU implementation of the path (the oracle, a
 restatement of the reference's numpy/BLAS code) on this host's cores on the
@@ -200,8 +202,9 @@ EP_WORKLOAD = "ep_prefill65536_int8"
 
 
 def arm_workload(args, world: int) -> str:
-    """The workload the headline `value` measures at this GPU count."""
-    return args.workload
+    """The workload the headline `value` measures at this GPU count: the
+    block of --workload on one GPU, the expert-parallel layer on several."""
+    return EP_WORKLOAD if world > 1 and not args.no_ep else args.workload
 
 
 def blas_threads() -> int:
@@ -701,7 +704,27 @@ def main() -> None:
         except (RuntimeError, ValueError, MemoryError) as e:  # reported, the main line still prints
             line["gptq"] = {"error": f"{type(e).__name__}: {e}"[:400]}
     if not args.no_ep:
-        line["expert_parallel"] = expert_parallel_side(args, dev, block, world, rank, flush)
+        ep_line = expert_parallel_side(args, dev, block, world, rank, flush)
+        line["expert_parallel"] = ep_line
+        if world > 1 and "error" not in ep_line:
+            # several GPUs: the headline is the sharded layer; the independent
+            # replicas of the block stay beside it
+            line["replicas"] = {"value": line["value"], "ms_per_step": line["ms_per_step"], "e2e": line["e2e"],
+                                "workload": f"{args.workload} on every GPU independently (no collective)"}
+            line["metric"] = "MoE-layer tokens/s (expert-parallel)"
+            line["value"] = ep_line["value"]
+            line["ms_per_step"] = ep_line["ms_per_step"]
+            line["steps"] = ep_line["steps"]
+            line["scaling"] = "strong"
+            line["e2e"] = {k: ep_line["e2e"][k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")}
+            line["gpu_launches"] = ep_line["gpu_launches_per_step"] * ep_line["steps"]
+            line["dtype"] = "i8"
+            line["config"] = {"workload": EP_WORKLOAD, "tokens": args.ep_tokens, "hidden": block.hidden,
+                              "experts": block.num_experts, "top_k": block.top_k, "expert_format": block.fmt,
+                              "activations": "bf16", "results": "bf16", "path": "tc",
+                              "parallelism": f"ep{world}", "microbatch": args.ep_microbatch,
+                              "l2": "flushed before every timed step (256 MiB write)"}
+            line["clocks"] = ep_line["clocks"]
     if rank == 0 and world == 1 and not args.no_full_model:
         del mb
         torch.cuda.empty_cache()
@@ -742,7 +765,9 @@ def summary_of(line: dict) -> dict:
                                 "gate_up_tensor_frac": pick(line, "gptq", k, "expert_kernels", "gate_up",
                                                             "tensor_frac")}
     if "expert_parallel" in line:
-        out["ep"] = {"value": pick(line, "expert_parallel", "value"), "ms": pick(line, "expert_parallel", "ms_per_step")}
+        out["ep"] = {"value": pick(line, "expert_parallel", "value"), "ms": pick(line, "expert_parallel", "ms_per_step"),
+                     "nvlink_GBps": pick(line, "expert_parallel", "nvlink", "GBps"),
+                     "phases_ms": {k: round(v, 3) for k, v in (line["expert_parallel"].get("phases_ms") or {}).items()}}
     if "full_model" in line:
         out["full_model_tok_s"] = pick(line, "full_model", "decode_tokens_per_s")
     return out
@@ -754,14 +779,20 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
     is fixed: strong scaling), bf16 activations, the block's router without
     the Zipf scaling (a random-init model routes near-uniformly). The 60
     experts are spread contiguously over the ranks (30/30, 15 x 4,
-    8,8,8,8,7,7,7,7) and each rank runs ExpertParallelMoe on the tensor-core
-    path: all-to-all of counts, of the rows (bf16) with their expert ids and
-    weights, the owner's experts, all-to-all of the results (fp32) back, the
-    gated shared expert and the ordered combine. A rank processes its tokens
-    in microbatches of --ep-microbatch (ExpertParallelMoe.forward_many: all
-    microbatches routed and counted, then one read-back of the counts). Every rank takes the same collective
-    steps; a failure while building is agreed on first, so that no rank
-    waits in a collective for one that gave up."""
+    8,8,8,8,7,7,7,7); each rank runs ExpertParallelMoe on the tensor-core
+    path in microbatches of --ep-microbatch: one exchange of counts, then the
+    rows (bf16) with their expert ids and weights out and the results (bf16)
+    back, asynchronously so that the transfers overlap the expert GEMMs, the
+    gated shared expert on a side stream, and the ordered combine. On one GPU
+    there is nothing to exchange and the layer runs as the block.
+
+    Timed: `value` from CUDA events around each step (max over ranks);
+    `e2e` the same steps with each rank's tokens copied in from pinned host
+    memory and its output copied back inside the timed region; `phases`
+    one extra step with the steps run one after another and timed apart
+    (max over ranks). Every rank takes the same collective steps; a failure
+    while building is agreed on first, so that no rank waits in a collective
+    for one that gave up."""
     import dataclasses
 
     import torch
@@ -778,7 +809,8 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
         if per % mbatch:
             raise ValueError(f"{per} tokens per rank are not a multiple of the {mbatch}-token microbatch")
         ep_block = dataclasses.replace(block, router=block.meta.get("router_base", block.router), meta={})
-        ep = ExpertParallelMoe(EpCudaOps(ep_block, rank, world, dev, _lib.PATH_TC))
+        ops = EpCudaOps(ep_block, rank, world, dev, _lib.PATH_TC, return_bf16=True)
+        ep = ExpertParallelMoe(ops)
         gen = torch.Generator(device=dev)
         gen.manual_seed(args.seed * 1000 + 577 + rank)
         h = torch.randn((per, block.hidden), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
@@ -793,48 +825,95 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
     parts = [h[c * mbatch:(c + 1) * mbatch] for c in range(chunks)]
 
     def step(stats=None):
-        ep.forward_many(parts)
+        out = ep.forward_many(parts)
         if stats is not None:
             send, recv = ep.last_counts
             stats[0] += sum(v for r, v in enumerate(send) if r != rank)
-            stats[1] += sum(recv)
+            stats[1] += sum(v for r, v in enumerate(recv) if r != rank)
+            stats[2] += sum(recv)
+        return out
 
     for _ in range(max(args.warmup, 3)):
         step()
     steps = max(3, min(args.steps, args.ep_steps))
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    stats = [0, 0]  # rows this rank sent to other ranks, rows it computed
+    stats = [0, 0, 0]  # rows this rank sent to other ranks, got from them, computed
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(dev) as clocks:
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record()
+            step(stats if i == 0 else None)
+            ends[i].record()
+        torch.cuda.synchronize()
+    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+
+    # end to end: this rank's tokens in from pinned host memory, its output back
+    h_host = h.cpu().pin_memory()
+    y_host = torch.empty((per, block.hidden), dtype=torch.float32).pin_memory()
+
+    def step_e2e():
+        h.copy_(h_host, non_blocking=True)
+        out = step()
+        for c, y in enumerate(out):
+            y_host[c * mbatch:(c + 1) * mbatch].copy_(y, non_blocking=True)
+
+    step_e2e()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     for i in range(steps):
         flush.zero_()
         starts[i].record()
-        step(stats if i == 0 else None)
+        step_e2e()
         ends[i].record()
     torch.cuda.synchronize()
-    t = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(starts, ends)), stats[1]], dtype=torch.float64,
-                     device=dev)
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+
+    # one more step with its steps timed apart
+    phases: dict = {}
+    if world > 1:
+        dist.barrier()
+    ep.forward_many(parts, phases=phases)
+    torch.cuda.synchronize()
+    keys = ["route", "counts", "shared", "pack", "dispatch", "rows", "return", "combine"]
+    t = torch.tensor([step_ms, e2e_ms, stats[2], stats[0], stats[1]] + [phases.get(k, 0.0) for k in keys],
+                     dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0].item()) / steps
+    ms, e2e_max, rows_max, sent_max, got_max = (float(v) for v in t[:5].tolist())
     row_out = block.hidden * 2 + 8  # bf16 row + expert id + weight
+    row_back = block.hidden * 2  # bf16 result
+    link_bytes = sent_max * row_out + got_max * row_back  # bytes one rank pushes out over NVLink per step (max)
+    # kernels per step: router, top-k, count, pack, rows (dispatch, gate/up, slices, down, combine, plus its
+    # tally), shared expert (gate logit, sigmoid, dispatch, gate/up, slices, down, combine), combine
+    launches = chunks * (2 + 1 + 1 + 6 + 7 + 1) if world > 1 else chunks * 7
     return {
         "workload": (f"MoE layer of the expert-parallel prefill: {total} tokens (32 x 2048) over {world} GPU(s), "
-                     f"{per} per rank in {chunks} microbatch(es) of {mbatch}; int8 experts, bf16 activations, "
-                     f"near-uniform routing"),
+                     f"{per} per rank in {chunks} microbatch(es) of {mbatch}; int8 experts, bf16 activations and "
+                     f"results, near-uniform routing"),
         "value": total / (ms / 1e3),
         "unit": "tokens/s",
         "ms_per_step": ms,
         "steps": steps,
         "scaling": "strong",
+        "e2e": {"value": total / (e2e_max / 1e3), "unit": "tokens/s", "ms_per_step": e2e_max,
+                "h2d_bytes_per_step": int(per * block.hidden * 2), "d2h_bytes_per_step": int(per * block.hidden * 4)},
+        "phases_ms": {k: float(v) for k, v in zip(keys, t[5:].tolist())},
+        "phases_timing": "one step with its steps run one after another (not overlapped), max over ranks",
         "experts_per_rank": [hi - lo for lo, hi in expert_partition(block.num_experts, world)],
-        "rows_computed_max_rank": int(t[1].item()),
-        "rank0_bytes_sent_per_step": int(stats[0] * row_out),
-        "rank0_bytes_returned_per_step": int(stats[0] * block.hidden * 4),
-        "collectives": "NCCL all_to_all_single: counts, rows + ids + weights, results" if world > 1 else "none",
+        "rows_computed_max_rank": int(rows_max),
+        "nvlink": {"bytes_out_per_step_max_rank": int(link_bytes),
+                   "GBps": link_bytes / (ms / 1e3) / 1e9 if world > 1 else 0.0,
+                   "peak_GBps": 770.0, "peak_source": "measured peer copy per direction on this pool"},
+        "gpu_launches_per_step": launches,
+        "collectives": ("NCCL all_to_all_single: counts, rows, ids + weights (one int32 buffer), results; "
+                        "asynchronous, overlapping the expert GEMMs") if world > 1 else "none (the block)",
         "timing": "CUDA events around each step (host waits for the counts included), max over ranks, L2 flushed",
+        "clocks": clocks.summary(),
     }
 
 

@@ -74,6 +74,7 @@ class MoeRowsIO(C.Structure):
         ("y", _vp),
         ("path", _i),
         ("launch_count", C.POINTER(_i)),
+        ("y_dtype", _i),
     ]
 
 
@@ -128,9 +129,9 @@ SIGNATURES: dict[str, tuple] = {
     "er_moe_rows": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeRowsIO), _vp, C.c_size_t, _vp]),
     "er_moe_shared_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_shared": (_i, [C.POINTER(MoeWeights), _vp, _i, _i, _vp, _i, _vp, C.c_size_t, _vp]),
-    "er_moe_combine": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "er_moe_combine": (_i, [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "er_ep_count": (_i, [_vp, _i, _i, _vp, _i, _i, _vp, _vp]),
-    "er_ep_pack": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "er_ep_pack": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "er_cache_create": (_i, [_i, C.c_size_t, _i, _vp, _i, C.POINTER(_vp)]),
     "er_cache_destroy": (_i, [_vp]),
     "er_cache_info": (_i, [_vp, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_size_t), C.POINTER(_vp)]),

@@ -33,7 +33,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const XT* __restrict__ h, 
                                                       const int32_t* __restrict__ offsets,
                                                       int32_t* __restrict__ cursor, XT* __restrict__ x_send,
                                                       int32_t* __restrict__ expert_send,
-                                                      float* __restrict__ weight_send, int32_t* __restrict__ pos_of) {
+                                                      float* __restrict__ weight_send, int meta_stride,
+                                                      int32_t* __restrict__ pos_of) {
   chain_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -44,8 +45,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const XT* __restrict__ h, 
     const int r = (e >= 0 && e < E) ? owner[e] : -1;
     if (r >= 0 && r < ranks) {
       p = offsets[r] + atomicAdd(&cursor[r], 1);
-      expert_send[p] = local[e];
-      weight_send[p] = w[(size_t)t * k + lane];
+      expert_send[(size_t)p * meta_stride] = local[e];
+      weight_send[(size_t)p * meta_stride] = w[(size_t)t * k + lane];
     }
     pos_of[(size_t)t * k + lane] = p;
   }
@@ -80,11 +81,12 @@ extern "C" int er_ep_count(const int32_t* idx, int n, int k, const int32_t* owne
 extern "C" int er_ep_pack(const void* h, int h_dtype, int hidden, const int32_t* idx, const float* w, int n, int k,
                           const int32_t* owner, const int32_t* local, int num_experts, int ranks,
                           const int32_t* offsets, int32_t* cursor, void* x_send, int32_t* expert_send,
-                          float* weight_send, int32_t* pos_of, void* stream) {
+                          float* weight_send, int meta_stride, int32_t* pos_of, void* stream) {
   if (n < 0 || k < 1 || k > kMaxTopK || num_experts < 1 || ranks < 1 || hidden <= 0)
     return fail(ER_EINVAL, "er_ep_pack: bad sizes (n %d, k %d, experts %d, ranks %d, hidden %d)", n, k, num_experts,
                 ranks, hidden);
   if (h_dtype != ER_DTYPE_F32 && h_dtype != ER_DTYPE_BF16) return fail(ER_EINVAL, "er_ep_pack: dtype %d", h_dtype);
+  if (meta_stride < 1) return fail(ER_EINVAL, "er_ep_pack: meta stride %d", meta_stride);
   const int vec = h_dtype == ER_DTYPE_F32 ? 4 : 8;
   if (hidden % vec || ((uintptr_t)h | (uintptr_t)x_send) & 15)
     return fail(ER_EINVAL, "er_ep_pack: rows must be 16-byte aligned and a multiple of 16 bytes");
@@ -98,8 +100,8 @@ extern "C" int er_ep_pack(const void* h, int h_dtype, int hidden, const int32_t*
   if (h_dtype == ER_DTYPE_BF16)
     return launch_chained(ep_pack_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, "ep_pack_kernel",
                           (const __nv_bfloat16*)h, hidden, idx, w, n, k, owner, local, num_experts, ranks, offsets,
-                          cursor, (__nv_bfloat16*)x_send, expert_send, weight_send, pos_of);
+                          cursor, (__nv_bfloat16*)x_send, expert_send, weight_send, meta_stride, pos_of);
   return launch_chained(ep_pack_kernel<float>, dim3(blocks), dim3(256), 0, st, "ep_pack_kernel", (const float*)h,
                         hidden, idx, w, n, k, owner, local, num_experts, ranks, offsets, cursor, (float*)x_send,
-                        expert_send, weight_send, pos_of);
+                        expert_send, weight_send, meta_stride, pos_of);
 }

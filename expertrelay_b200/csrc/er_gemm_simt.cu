@@ -185,13 +185,26 @@ int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void
 constexpr int kCombineThreads = 128;
 constexpr int kCombineMaxParts = 8;
 
-template <int KMAX, int PMAX>
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ y_r,
+// RT / OT: the row results' and the output's element type (float or bf16; the
+// sums are fp32 either way).
+__device__ __forceinline__ float4 load_f4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 load_f4(const __nv_bfloat16* p) { return load4(p); }
+__device__ __forceinline__ void store_f4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void store_f4(__nv_bfloat16* p, float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+template <int KMAX, int PMAX, typename RT, typename OT>
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const RT* __restrict__ y_r,
                                                                   const float* __restrict__ y_s, int parts,
                                                                   const int32_t* __restrict__ pos_of,
                                                                   const int32_t* __restrict__ idx, int n, int k,
                                                                   int H, const int* __restrict__ error,
-                                                                  float* __restrict__ out) {
+                                                                  OT* __restrict__ out) {
   __shared__ int pos_sorted[KMAX];
   chain_wait();
   const int t = blockIdx.x;
@@ -218,15 +231,15 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
   }
   const int step = gridDim.y * kCombineThreads * 4;
   for (int c = (blockIdx.y * kCombineThreads + threadIdx.x) * 4; c < H; c += step) {
-    float4* dst = reinterpret_cast<float4*>(out + (size_t)t * H + c);
+    OT* dst = out + (size_t)t * H + c;
     if (failed || missing) {
-      *dst = make_float4(nan, nan, nan, nan);
+      store_f4(dst, make_float4(nan, nan, nan, nan));
       continue;
     }
     float4 v[KMAX], sv[PMAX];
 #pragma unroll
     for (int s = 0; s < KMAX; ++s)
-      if (s < k) v[s] = *reinterpret_cast<const float4*>(y_r + (size_t)pos[s] * H + c);
+      if (s < k) v[s] = load_f4(y_r + (size_t)pos[s] * H + c);
     if (y_s) {
 #pragma unroll
       for (int q = 0; q < PMAX; ++q)
@@ -258,25 +271,26 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
       acc.z += sh.z;
       acc.w += sh.w;
     }
-    *dst = acc;
+    store_f4(dst, acc);
   }
 }
 
-template <int KMAX>
-static int launch_combine_k(const float* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx,
-                            int n, int k, int H, const int* error, float* out, dim3 grid, cudaStream_t st) {
+template <int KMAX, typename RT, typename OT>
+static int launch_combine_k(const RT* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx,
+                            int n, int k, int H, const int* error, OT* out, dim3 grid, cudaStream_t st) {
   if (parts <= 1)
-    return launch_chained(combine_kernel<KMAX, 1>, grid, dim3(kCombineThreads), 0, st, "combine_kernel", y_r, y_s,
-                          parts, pos_of, idx, n, k, H, error, out);
+    return launch_chained(combine_kernel<KMAX, 1, RT, OT>, grid, dim3(kCombineThreads), 0, st, "combine_kernel", y_r,
+                          y_s, parts, pos_of, idx, n, k, H, error, out);
   if (parts <= 4)
-    return launch_chained(combine_kernel<KMAX, 4>, grid, dim3(kCombineThreads), 0, st, "combine_kernel", y_r, y_s,
-                          parts, pos_of, idx, n, k, H, error, out);
-  return launch_chained(combine_kernel<KMAX, kCombineMaxParts>, grid, dim3(kCombineThreads), 0, st, "combine_kernel",
-                        y_r, y_s, parts, pos_of, idx, n, k, H, error, out);
+    return launch_chained(combine_kernel<KMAX, 4, RT, OT>, grid, dim3(kCombineThreads), 0, st, "combine_kernel", y_r,
+                          y_s, parts, pos_of, idx, n, k, H, error, out);
+  return launch_chained(combine_kernel<KMAX, kCombineMaxParts, RT, OT>, grid, dim3(kCombineThreads), 0, st,
+                        "combine_kernel", y_r, y_s, parts, pos_of, idx, n, k, H, error, out);
 }
 
-int launch_combine(const float* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx, int n,
-                   int k, int H, const int* error, float* out, cudaStream_t st) {
+template <typename RT, typename OT>
+static int launch_combine_t(const RT* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx,
+                            int n, int k, int H, const int* error, OT* out, cudaStream_t st) {
   if (n <= 0) return ER_OK;
   if (parts < 1 || parts > kCombineMaxParts) return fail(ER_EINVAL, "combine: %d shared parts", parts);
   // a few tokens: their columns spread over CTAs; many: one CTA per token row
@@ -284,6 +298,24 @@ int launch_combine(const float* y_r, const float* y_s, int parts, const int32_t*
   const dim3 grid(n, n >= 2 * 148 ? 1 : col_blocks);
   if (k <= 4) return launch_combine_k<4>(y_r, y_s, parts, pos_of, idx, n, k, H, error, out, grid, st);
   return launch_combine_k<kMaxTopK>(y_r, y_s, parts, pos_of, idx, n, k, H, error, out, grid, st);
+}
+
+int launch_combine(const float* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx, int n,
+                   int k, int H, const int* error, float* out, cudaStream_t st) {
+  return launch_combine_t(y_r, y_s, parts, pos_of, idx, n, k, H, error, out, st);
+}
+
+int launch_combine_dt(const void* y_r, int r_dtype, const float* y_s, int parts, const int32_t* pos_of,
+                      const int32_t* idx, int n, int k, int H, const int* error, void* out, int o_dtype,
+                      cudaStream_t st) {
+  const bool rb = r_dtype == ER_DTYPE_BF16, ob = o_dtype == ER_DTYPE_BF16;
+  if (!rb && !ob)
+    return launch_combine_t((const float*)y_r, y_s, parts, pos_of, idx, n, k, H, error, (float*)out, st);
+  if (rb && !ob)
+    return launch_combine_t((const __nv_bfloat16*)y_r, y_s, parts, pos_of, idx, n, k, H, error, (float*)out, st);
+  if (!rb && ob)
+    return launch_combine_t((const float*)y_r, y_s, parts, pos_of, idx, n, k, H, error, (__nv_bfloat16*)out, st);
+  return fail(ER_EINVAL, "combine: bf16 rows into a bf16 output is not provided");
 }
 
 }  // namespace er

@@ -157,6 +157,10 @@ int launch_gemm_simt_grouped(const GroupArgs& a, int sched, int mode, const void
 // NULL); rows of NaN when *error is nonzero
 int launch_combine(const float* y_r, const float* y_s, int parts, const int32_t* pos_of, const int32_t* idx, int n,
                    int k, int H, const int* error, float* out, cudaStream_t st);
+// the same with the row results and the output in ER_DTYPE_F32 or ER_DTYPE_BF16
+int launch_combine_dt(const void* y_r, int r_dtype, const float* y_s, int parts, const int32_t* pos_of,
+                      const int32_t* idx, int n, int k, int H, const int* error, void* out, int o_dtype,
+                      cudaStream_t st);
 // per-expert counts of ids[0..m) into tally[E] (nclear ints from tally cleared
 // first); out-of-range ids are not counted
 int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaStream_t st);

@@ -28,7 +28,8 @@ struct Run {
   int h_dtype;
   int n;
   const float* logits_in;
-  float* y;
+  void* y;
+  int y_dtype;    // ER_DTYPE_F32, or (kRows) ER_DTYPE_BF16
   float* logits_out;
   int64_t* topk_idx_out;
   float* topk_w_out;
@@ -151,6 +152,8 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
     return fail(ER_EINVAL, "er_moe: inputs and outputs must be 16-byte aligned");
   if (mode == kRows && (!r.row_expert || !r.row_weight))
     return fail(ER_EINVAL, "er_moe_rows: null expert ids or weights");
+  if (r.y_dtype != ER_DTYPE_F32 && !(mode == kRows && r.y_dtype == ER_DTYPE_BF16))
+    return fail(ER_EINVAL, "er_moe: output dtype %d (fp32; bf16 for er_moe_rows)", r.y_dtype);
   const int path = pick_path(w, r.path, n);
   if (path != ER_PATH_GEMV && path != ER_PATH_GEMM && path != ER_PATH_TC)
     return fail(ER_EINVAL, "er_moe: unknown path %d", r.path);
@@ -367,7 +370,9 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
   launches += 2 * per_stage;
   if (int rc = mark(4)) return rc;
   // K4
-  if (int rc = launch_combine(y_r, y_s, specs[1].ks, pos_of, idx32, n, k, H, &plan->error, r.y, st)) return rc;
+  if (int rc = launch_combine_dt(y_r, ER_DTYPE_F32, y_s, specs[1].ks, pos_of, idx32, n, k, H, &plan->error, r.y,
+                                 r.y_dtype, st))
+    return rc;
   launches += 1;
   if (r.launch_count) *r.launch_count += launches;
   return mark(5);
@@ -424,6 +429,7 @@ extern "C" int er_moe_rows(const er_moe_weights* w, const er_moe_rows_io* io, vo
   r.y = io->y;
   r.row_expert = io->expert;
   r.row_weight = io->weight;
+  r.y_dtype = io->y_dtype;
   r.path = io->path;
   r.launch_count = io->launch_count;
   return run_moe(w, r, workspace, workspace_bytes, (cudaStream_t)stream);
@@ -446,13 +452,16 @@ extern "C" int er_moe_shared(const er_moe_weights* w, const void* h, int h_dtype
   return run_moe(w, r, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
-extern "C" int er_moe_combine(const float* y_rows, const int32_t* pos_of, const int32_t* idx, const float* y_shared,
-                              int n, int k, int hidden, float* y, void* stream) {
+extern "C" int er_moe_combine(const void* y_rows, int rows_dtype, const int32_t* pos_of, const int32_t* idx,
+                              const float* y_shared, int n, int k, int hidden, float* y, void* stream) {
   if (n < 0 || k < 0 || k > kMaxTopK || hidden <= 0 || hidden % 4)
     return fail(ER_EINVAL, "er_moe_combine: n %d, k %d (<= %d), hidden %d (a multiple of 4)", n, k, kMaxTopK, hidden);
+  if (rows_dtype != ER_DTYPE_F32 && rows_dtype != ER_DTYPE_BF16)
+    return fail(ER_EINVAL, "er_moe_combine: rows dtype %d", rows_dtype);
   if (n == 0) return ER_OK;
   if (!y || (k > 0 && (!y_rows || !pos_of || !idx))) return fail(ER_EINVAL, "er_moe_combine: null argument");
-  if (((uintptr_t)y_rows | (uintptr_t)y_shared | (uintptr_t)y) & 15)
-    return fail(ER_EINVAL, "er_moe_combine: rows must be 16-byte aligned");
-  return launch_combine(y_rows, y_shared, 1, pos_of, idx, n, k, hidden, nullptr, y, (cudaStream_t)stream);
+  if ((((uintptr_t)y_shared | (uintptr_t)y) & 15) || ((uintptr_t)y_rows & (rows_dtype == ER_DTYPE_BF16 ? 7 : 15)))
+    return fail(ER_EINVAL, "er_moe_combine: rows must be aligned (16 bytes; 8 for bf16 rows)");
+  return launch_combine_dt(y_rows, rows_dtype, y_shared, 1, pos_of, idx, n, k, hidden, nullptr, y, ER_DTYPE_F32,
+                           (cudaStream_t)stream);
 }

@@ -189,9 +189,11 @@ typedef struct er_moe_rows_io {
   int m;
   const int32_t* expert;       /* [m] expert of each row: 0 .. num_experts-1 of `w` (this rank's experts) */
   const float* weight;         /* [m] routing weight of each row */
-  float* y;                    /* [m, H] = weight * down(silu(gate x) * up x) (qwen_moe.py:345-349) */
+  void* y;                     /* [m, H] = weight * down(silu(gate x) * up x) (qwen_moe.py:345-349), dtype y_dtype */
   int path;                    /* ER_PATH_* */
   int* launch_count;           /* optional */
+  int y_dtype;                 /* ER_DTYPE_F32 (0, the default) or ER_DTYPE_BF16: results rounded to bf16 halve
+                                  the bytes sent back to the tokens' ranks */
 } er_moe_rows_io;
 /* routed experts on pre-routed rows (w->router_w and the shared weights unused) */
 ER_API size_t er_moe_rows_workspace_bytes(const er_moe_weights* w, int m, int path);
@@ -204,9 +206,10 @@ ER_API int er_moe_shared(const er_moe_weights* w, const void* h, int h_dtype, in
                          void* workspace, size_t workspace_bytes, void* stream);
 /* y[t] = sum over t's k slots in ascending expert id (idx [n, k]) of
  * y_rows[pos_of[t * k + j]] (+ y_shared[t] when not NULL): the reference's
- * np.add.at order (qwen_moe.py:340-349) and its final sum (:359) */
-ER_API int er_moe_combine(const float* y_rows, const int32_t* pos_of, const int32_t* idx, const float* y_shared,
-                          int n, int k, int hidden, float* y, void* stream);
+ * np.add.at order (qwen_moe.py:340-349) and its final sum (:359), in fp32;
+ * y_rows in rows_dtype (ER_DTYPE_F32 or ER_DTYPE_BF16) */
+ER_API int er_moe_combine(const void* y_rows, int rows_dtype, const int32_t* pos_of, const int32_t* idx,
+                          const float* y_shared, int n, int k, int hidden, float* y, void* stream);
 
 /* ---- expert-parallel exchange buffers -------------------------------------
  * owner[e] = rank holding global expert e, local[e] = its index there. */
@@ -216,13 +219,16 @@ ER_API int er_ep_count(const int32_t* idx, int n, int k, const int32_t* owner, i
 /* Packs the send buffers, destination rank by destination rank: rank r's
  * rows occupy [offsets[r], offsets[r] + counts[r]) (offsets: device, the
  * exclusive prefix of er_ep_count's counts). For pair (t, j) at position p:
- * x_send[p] = h[t] (dtype h_dtype), expert_send[p] = local[idx[t, j]],
- * weight_send[p] = w[t, j], pos_of[t * k + j] = p. cursor: device scratch of
- * `ranks` ints. Rows of one destination are in no particular order. */
+ * x_send[p] = h[t] (dtype h_dtype), expert_send[p * meta_stride] =
+ * local[idx[t, j]], weight_send[p * meta_stride] = w[t, j], pos_of[t * k + j]
+ * = p (meta_stride 2 with weight_send = expert_send + 1 interleaves the id
+ * and the weight's bits, so both travel in one exchange). cursor: device
+ * scratch of `ranks` ints. Rows of one destination are in no particular
+ * order. */
 ER_API int er_ep_pack(const void* h, int h_dtype, int hidden, const int32_t* idx, const float* w, int n, int k,
                       const int32_t* owner, const int32_t* local, int num_experts, int ranks, const int32_t* offsets,
-                      int32_t* cursor, void* x_send, int32_t* expert_send, float* weight_send, int32_t* pos_of,
-                      void* stream);
+                      int32_t* cursor, void* x_send, int32_t* expert_send, float* weight_send, int meta_stride,
+                      int32_t* pos_of, void* stream);
 
 /* ------------------------------------------------------------------------
  * HBM expert cache: replaces CachedExpertSource (cache/expert_cache.py:92-402).

@@ -62,8 +62,9 @@ class HostOps:
     def pack(self, h, idx, w, offsets, total):
         n, k = idx.shape
         x = np.empty((total, h.shape[1]), np.float32)
-        e_send = np.empty(total, np.int32)
-        w_send = np.empty(total, np.float32)
+        meta = np.empty((total, 2), np.int32)  # (local expert id, weight bits)
+        w_send = meta[:, 1].view(np.float32)
+        e_send = meta[:, 0]
         pos_of = np.empty((n, k), np.int32)
         cursor = offsets.numpy().copy()
         # destination by destination, pairs in reverse order: any order is allowed
@@ -74,10 +75,11 @@ class HostOps:
                 p = cursor[d]
                 cursor[d] += 1
                 x[p], e_send[p], w_send[p], pos_of[t, j] = h[t].numpy(), self.local[e], w[t, j], p
-        return torch.from_numpy(x), torch.from_numpy(e_send), torch.from_numpy(w_send), torch.from_numpy(pos_of)
+        return torch.from_numpy(x), torch.from_numpy(meta), torch.from_numpy(pos_of)
 
-    def rows(self, x, expert, weight):
-        x, expert, weight = x.numpy(), expert.numpy(), weight.numpy()
+    def rows(self, x, meta):
+        x, meta = x.numpy(), np.ascontiguousarray(meta.numpy())
+        expert, weight = meta[:, 0].copy(), meta[:, 1].copy().view(np.float32)
         y = np.zeros_like(x)
         for e in np.unique(expert):
             r = np.nonzero(expert == e)[0]
@@ -128,6 +130,9 @@ def _rank_main(rank: int, world: int, port: int, results):
         err_many = max(O.rel_l2(y_j.numpy(), O.moe_block(p.numpy(), oracle_weights(block)).y)
                        for y_j, p in zip(many, parts) if p.shape[0])
         assert all(y_j.shape == p.shape for y_j, p in zip(many, parts))
+        # the timed, one-step-after-another variant gives the same outputs
+        timed = ep.forward_many(parts, phases={})
+        assert all(torch.equal(a, b) for a, b in zip(many, timed))
         assert sum(ep.last_counts[0]) == sum(p.shape[0] for p in parts) * SHAPE["top_k"]
         results[rank] = (max(O.rel_l2(y, ref), err_many), counts)
     finally:

@@ -34,6 +34,8 @@ def _expected(block, h, path, device):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("path", list(PATHS))
 def test_one_rank_equals_the_block(cuda, path, dtype):
+    """One rank: the layer is the block; the exchange path (taken when the
+    steps are timed) gives the same bits."""
     block = synth.make_block(4, num_experts=16)
     ep = ExpertParallelMoe(EpCudaOps(block, 0, 1, cuda, PATHS[path]))
     hs = []
@@ -44,11 +46,35 @@ def test_one_rank_equals_the_block(cuda, path, dtype):
         torch.cuda.synchronize()
         assert torch.equal(y, ref), f"n={n}"
         hs.append(h)
-    # the same batches as microbatches of one call (one count read-back)
-    for h, y in zip(hs, ep.forward_many(hs)):
+    # the same batches as microbatches of one call (one count read-back), and
+    # through pack / rows / combine with the steps timed
+    phases = {}
+    for h, y, y2 in zip(hs, ep.forward_many(hs), ep.forward_many(hs, phases=phases)):
         ref = _expected(block, h, PATHS[path], cuda)
         torch.cuda.synchronize()
         assert torch.equal(y, ref), f"forward_many, n={h.shape[0]}"
+        assert torch.equal(y2, ref), f"forward_many through the exchange steps, n={h.shape[0]}"
+    assert {"route", "counts", "shared", "pack", "dispatch", "rows", "return", "combine"} <= set(phases)
+
+
+def test_bf16_results_within_the_bf16_tolerance(cuda):
+    """Routed results sent back in bf16: each rank's output within the bf16
+    tolerance (rel-L2 1e-2) of the oracle on the same bf16 tokens and
+    logits, and close to the fp32-return output."""
+    from helpers import oracle_weights
+
+    from oracle import moe_oracle as O
+
+    block = synth.make_block(5, num_experts=16)
+    h = torch.from_numpy(synth.make_tokens(77, 200)).to(cuda).to(torch.bfloat16)
+    ep32 = ExpertParallelMoe(EpCudaOps(block, 0, 1, cuda, _lib.PATH_TC))
+    ep16 = ExpertParallelMoe(EpCudaOps(block, 0, 1, cuda, _lib.PATH_TC, return_bf16=True))
+    y32 = ep32.forward_many([h], phases={})[0]
+    y16 = ep16.forward_many([h], phases={})[0]
+    logits = ep32.ops.full.router_logits(h)
+    ref = O.moe_block(h.float().cpu().numpy(), oracle_weights(block), logits=logits.cpu().numpy())
+    assert O.rel_l2(y16.cpu().numpy(), ref.y) < 1e-2
+    assert O.rel_l2(y16.cpu().numpy(), y32.cpu().numpy()) < 5e-3
 
 
 def _free_port() -> int:
@@ -67,6 +93,14 @@ def _rank_main(rank: int, world: int, port: int):
         for path, dtype in ((_lib.PATH_TC, torch.float32), (_lib.PATH_GEMV, torch.float32),
                             (_lib.PATH_TC, torch.bfloat16)):
             ep = ExpertParallelMoe(EpCudaOps(block, rank, world, dev, path))
+            if dtype == torch.bfloat16:  # results back in bf16: within the bf16 rounding of the fp32 ones
+                ep16 = ExpertParallelMoe(EpCudaOps(block, rank, world, dev, path, return_bf16=True))
+                h = torch.from_numpy(synth.make_tokens(50 + rank, 64 + 16 * rank)).to(dev).to(dtype)
+                y16, y32 = ep16(h), ep(h)
+                torch.cuda.synchronize()
+                rel = ((y16 - y32).norm() / y32.norm()).item()
+                if not rel < 5e-3:
+                    raise AssertionError(f"rank {rank}: bf16 results differ from fp32 by rel-L2 {rel:.2e}")
             for n in (8, 96 + 32 * rank):  # ragged across ranks
                 h = torch.from_numpy(synth.make_tokens(70 + 10 * rank + n, n)).to(dev).to(dtype)
                 y = ep(h)
