@@ -125,11 +125,14 @@ SIGNATURES: dict[str, tuple] = {
     "er_moe_block": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp, C.c_size_t, _vp]),
     "er_moe_block_noalloc": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeIO), _vp]),
     "er_tc_test_stall": (_i, [C.c_ulonglong, _i]),
+    "er_moe_error_bits": (_i, [C.POINTER(MoeWeights), _i, _i, _vp, C.POINTER(_i), _vp]),
     "er_moe_rows_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_rows": (_i, [C.POINTER(MoeWeights), C.POINTER(MoeRowsIO), _vp, C.c_size_t, _vp]),
     "er_moe_shared_workspace_bytes": (C.c_size_t, [C.POINTER(MoeWeights), _i, _i]),
     "er_moe_shared": (_i, [C.POINTER(MoeWeights), _vp, _i, _i, _vp, _i, _vp, C.c_size_t, _vp]),
     "er_moe_combine": (_i, [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "er_route_scratch_bytes": (C.c_size_t, [_i, _i]),
+    "er_route": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _i, _vp, C.c_size_t, _vp, _vp, _vp, _vp]),
     "er_ep_count": (_i, [_vp, _i, _i, _vp, _i, _i, _vp, _vp]),
     "er_ep_pack": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "er_cache_create": (_i, [_i, C.c_size_t, _i, _vp, _i, C.POINTER(_vp)]),

@@ -112,6 +112,10 @@ __device__ __forceinline__ float abs_max4(float4 v) {
 // Router logits; large batches write kRouterKSplit partial sums (K slices)
 // into logits / gate_logit (each n*E / n apart), *nparts says how many.
 constexpr int kRouterKSplit = 4;
+// partial logits the router writes for a batch of n tokens and `rows` weight
+// rows (E, plus one for the shared gate): K slices for the tiled kernel
+// (more than 64 tokens, at most 64 rows), one set otherwise
+inline int router_parts(int n, int rows) { return (n <= 64 || rows > 64) ? 1 : kRouterKSplit; }
 // `tally` (optional, `ntally` ints) is cleared for the top-k kernel's counts.
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
                          float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st);

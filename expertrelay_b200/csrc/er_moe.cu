@@ -67,8 +67,11 @@ static WsLayout ws_layout(const er_moe_weights* w, int n, int path, int mode) {
   const size_t nk = (size_t)n * run_k(w, mode);
   const size_t ns = run_shared(mode) ? (size_t)n : 0;  // rows through the shared expert
   const size_t nl = mode == kBlock ? (size_t)n : 0;    // rows with router logits
-  L.logits = take((size_t)kRouterKSplit * nl * w->num_experts * 4);  // partial sums of K slices
-  L.gate_logit = take((size_t)kRouterKSplit * ns * 4);
+  // partial sums of K slices: the router rows with the shared gate (block), or
+  // the shared gate alone (given router logits, or the shared expert), which
+  // is split whenever a batch is
+  L.logits = take((size_t)router_parts(n, w->num_experts + 1) * nl * w->num_experts * 4);
+  L.gate_logit = take((size_t)router_parts(n, 1) * ns * 4);
   L.gate_sig = take(ns * 4);
   L.idx32 = take(mode == kBlock ? nk * 4 : 0);
   L.topw = take(mode == kBlock ? nk * 4 : 0);
@@ -387,6 +390,22 @@ extern "C" int er_tc_test_stall(unsigned long long wait_ns, int stall) {
   g_tc_test_wait_ns = wait_ns;
   g_tc_test_stall = stall;
   return ER_OK;
+}
+
+extern "C" int er_moe_error_bits(const er_moe_weights* w, int n, int path, const void* workspace, int* bits,
+                                 void* stream) {
+  if (!bits) return fail(ER_EINVAL, "er_moe_error_bits: null output");
+  *bits = 0;
+  if (int rc = validate(w, kBlock)) return rc;
+  if (n <= 0) return ER_OK;
+  if (!workspace) return fail(ER_EINVAL, "er_moe_error_bits: null workspace");
+  const WsLayout L = ws_layout(w, n, pick_path(w, path, n), kBlock);
+  const Plan* plan = reinterpret_cast<const Plan*>(static_cast<const char*>(workspace) + L.plan);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int rc = cuda_check(cudaMemcpyAsync(bits, &plan->error, sizeof(int), cudaMemcpyDeviceToHost, st),
+                          "er_moe_error_bits: copy"))
+    return rc;
+  return cuda_check(cudaStreamSynchronize(st), "er_moe_error_bits: sync");
 }
 
 extern "C" size_t er_moe_workspace_bytes(const er_moe_weights* w, int n, int path) {

@@ -111,6 +111,7 @@ class EpCudaOps:
             self.full.use_arena(self.records.data_ptr(), n_local)
             self.full.set_expert_table(self.table)
         self.return_dtype = torch.bfloat16 if return_bf16 else torch.float32
+        self._route_scratch: torch.Tensor | None = None
         self.cursor = torch.zeros(ranks, dtype=torch.int32, device=self.device)
         self._ws: torch.Tensor | None = None  # the routed rows' workspace
         # the shared expert runs on a side stream, beside the exchange and the
@@ -133,9 +134,17 @@ class EpCudaOps:
         w = torch.empty((n, self.top_k), dtype=torch.float32, device=self.device)
         if n == 0:  # an empty microbatch still takes part in the exchange
             return torch.empty((0, self.num_experts), dtype=torch.float32, device=self.device), idx, w
-        logits = self.full.router_logits(h)
-        _lib.check(_lib.lib().er_router_topk(logits.data_ptr(), n, self.num_experts, self.top_k, None,
-                                             idx.data_ptr(), w.data_ptr(), self._stream()), "er_router_topk")
+        logits = torch.empty((n, self.num_experts), dtype=torch.float32, device=self.device)
+        L = _lib.lib()
+        nbytes = L.er_route_scratch_bytes(n, self.num_experts)
+        if self._route_scratch is None or self._route_scratch.numel() < nbytes:
+            self._route_scratch = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        sc = self._route_scratch
+        dtype = _lib.DTYPE_BF16 if h.dtype == torch.bfloat16 else _lib.DTYPE_F32
+        h = h.contiguous()
+        _lib.check(L.er_route(h.data_ptr(), dtype, n, self.hidden, self.full.router.data_ptr(), self.num_experts,
+                              self.top_k, 0, sc.data_ptr(), sc.numel(), logits.data_ptr(), idx.data_ptr(),
+                              w.data_ptr(), self._stream()), "er_route")
         return logits, idx, w
 
     def count(self, idx: torch.Tensor) -> torch.Tensor:

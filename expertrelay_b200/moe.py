@@ -158,6 +158,18 @@ class MoeBlock:
         else:
             self.expert_table.copy_(addresses.to(self.device, torch.int64), non_blocking=True)
 
+    def error_bits(self, n: int, path: int = _lib.PATH_AUTO, workspace: torch.Tensor | None = None) -> int:
+        """The plan's error bits after the last forward of n tokens on this
+        path (0: clean; see er_moe_error_bits). Synchronises the stream."""
+        ws = workspace if workspace is not None else self._ws
+        if ws is None:
+            return 0
+        bits = C.c_int(0)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(_lib.lib().er_moe_error_bits(C.byref(self._w), int(n), int(path), ws.data_ptr(), C.byref(bits),
+                                                stream), "er_moe_error_bits")
+        return int(bits.value)
+
     def workspace_bytes(self, n: int, path: int = _lib.PATH_AUTO) -> int:
         return int(_lib.lib().er_moe_workspace_bytes(C.byref(self._w), int(n), int(path)))
 

@@ -112,6 +112,16 @@ ER_API int er_dequant_int4(const uint8_t* packed, const uint16_t* scales_f16, co
  * and their softmax probabilities (no renormalisation). idx64 or idx32 may be NULL. */
 ER_API int er_router_topk(const float* logits, int n, int num_experts, int k, int64_t* idx64, int32_t* idx32,
                    float* probs_out, void* stream);
+/* Routing straight from the tokens (runtime/qwen_moe.py:303-308): the router
+ * logits h @ router_w^T in fp32 FMA (h fp32 or bf16, [n, hidden]; router_w
+ * fp32 [num_experts, hidden]), then softmax + top-k as er_router_topk;
+ * logits_out [n, E] optional. scratch: device memory of
+ * er_route_scratch_bytes(n, num_experts) bytes for the K-slice partial
+ * logits. */
+ER_API size_t er_route_scratch_bytes(int n, int num_experts);
+ER_API int er_route(const void* h, int h_dtype, int n, int hidden, const float* router_w, int num_experts, int k,
+                    int norm_topk_prob, float* scratch, size_t scratch_bytes, float* logits_out, int32_t* idx32,
+                    float* w_out, void* stream);
 
 /* ---- the MoE block (runtime/qwen_moe.py:293-359) ------------------------- */
 typedef struct er_moe_weights {
@@ -175,6 +185,14 @@ ER_API int er_moe_block_noalloc(const er_moe_weights* w, const er_moe_io* io, vo
  * block writes NaN rows. (0, 0) restores normal operation. Process-wide,
  * not thread-safe; for tests of the bounded-wait error path only. */
 ER_API int er_tc_test_stall(unsigned long long wait_ns, int stall);
+/* The error bits the last er_moe_block call on this workspace (same w, n and
+ * path) left in its plan, read after the stream's work: 0 when it ran clean;
+ * 1 an expert id out of range, 2 inconsistent routing counts, 4 a record
+ * outside the arena, 8 a tensor-core wait gave up. Any of them made the
+ * block write NaN rows. Synchronises the stream. No counterpart in the
+ * reference (its CPU path raises instead). */
+ER_API int er_moe_error_bits(const er_moe_weights* w, int n, int path, const void* workspace, int* bits,
+                             void* stream);
 ER_API int er_moe_block(const er_moe_weights* w, const er_moe_io* io, void* workspace, size_t workspace_bytes,
                  void* stream);
 

@@ -26,9 +26,11 @@ pytestmark = pytest.mark.gpu
 PATHS = {"auto": _lib.PATH_AUTO, "gemv": _lib.PATH_GEMV, "gemm": _lib.PATH_GEMM, "tc": _lib.PATH_TC}
 
 
-def _expected(block, h, path, device):
+def _expected(block, h, path, device, ep):
+    """The single-GPU block on the router logits the expert-parallel layer
+    routes from (the same top-k kernel then picks the same experts)."""
     mb = MoeBlock.from_host_block(block, device=device)
-    return mb.forward(h, logits=mb.router_logits(h), path=path)
+    return mb.forward(h, logits=ep.ops.route(h)[0], path=path)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
@@ -42,7 +44,7 @@ def test_one_rank_equals_the_block(cuda, path, dtype):
     for n in (3, 40, 300):
         h = torch.from_numpy(synth.make_tokens(60 + n, n)).to(cuda).to(dtype)
         y = ep(h)
-        ref = _expected(block, h, PATHS[path], cuda)
+        ref = _expected(block, h, PATHS[path], cuda, ep)
         torch.cuda.synchronize()
         assert torch.equal(y, ref), f"n={n}"
         hs.append(h)
@@ -50,7 +52,7 @@ def test_one_rank_equals_the_block(cuda, path, dtype):
     # through pack / rows / combine with the steps timed
     phases = {}
     for h, y, y2 in zip(hs, ep.forward_many(hs), ep.forward_many(hs, phases=phases)):
-        ref = _expected(block, h, PATHS[path], cuda)
+        ref = _expected(block, h, PATHS[path], cuda, ep)
         torch.cuda.synchronize()
         assert torch.equal(y, ref), f"forward_many, n={h.shape[0]}"
         assert torch.equal(y2, ref), f"forward_many through the exchange steps, n={h.shape[0]}"
@@ -71,7 +73,7 @@ def test_bf16_results_within_the_bf16_tolerance(cuda):
     ep16 = ExpertParallelMoe(EpCudaOps(block, 0, 1, cuda, _lib.PATH_TC, return_bf16=True))
     y32 = ep32.forward_many([h], phases={})[0]
     y16 = ep16.forward_many([h], phases={})[0]
-    logits = ep32.ops.full.router_logits(h)
+    logits = ep32.ops.route(h)[0]
     ref = O.moe_block(h.float().cpu().numpy(), oracle_weights(block), logits=logits.cpu().numpy())
     assert O.rel_l2(y16.cpu().numpy(), ref.y) < 1e-2
     assert O.rel_l2(y16.cpu().numpy(), y32.cpu().numpy()) < 5e-3
@@ -104,7 +106,7 @@ def _rank_main(rank: int, world: int, port: int):
             for n in (8, 96 + 32 * rank):  # ragged across ranks
                 h = torch.from_numpy(synth.make_tokens(70 + 10 * rank + n, n)).to(dev).to(dtype)
                 y = ep(h)
-                ref = _expected(block, h, path, dev)
+                ref = _expected(block, h, path, dev, ep)
                 torch.cuda.synchronize()
                 if not torch.equal(y, ref):
                     diff = (y - ref).abs().max().item()
@@ -116,7 +118,7 @@ def _rank_main(rank: int, world: int, port: int):
                     if y.shape != h.shape:
                         raise AssertionError(f"rank {rank}: empty microbatch gave {tuple(y.shape)}")
                     continue
-                ref = _expected(block, h, path, dev)
+                ref = _expected(block, h, path, dev, ep)
                 torch.cuda.synchronize()
                 if not torch.equal(y, ref):
                     raise AssertionError(f"rank {rank} path {path} {dtype} forward_many microbatch {j} differs")
