@@ -229,8 +229,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
         bool w = true;
-        if (lane == 0) w = mbar_wait(&empty[s], ph ^ 1, abort_flag, t.wait_ns);
-        if (!__shfl_sync(0xffffffffu, (int)w, 0)) {
+        w = warp_wait(&empty[s], ph ^ 1, abort_flag, lane, t.wait_ns);
+        if (!w) {
           ok = false;
           break;
         }
@@ -302,16 +302,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       const int ab = ic & 1;
       const uint32_t aph = (ic >> 1) & 1;
       bool w = true;
-      if (lane == 0) w = mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag, t.wait_ns);
-      if (!__shfl_sync(0xffffffffu, (int)w, 0)) break;
+      w = warp_wait(&acc_empty[ab], aph ^ 1, abort_flag, lane, t.wait_ns);
+      if (!w) break;
       tc_fence_after();
       const uint32_t d = tmem_base + ab * kTcAccCols;
       const uint32_t idesc = CG == 1 ? idesc_i8(128, TT + it.npad) : idesc_i8(256, 2 * TT);
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
-        if (lane == 0) w = mbar_wait(&full[s], ph, abort_flag, t.wait_ns);
-        if (!__shfl_sync(0xffffffffu, (int)w, 0)) {
+        w = warp_wait(&full[s], ph, abort_flag, lane, t.wait_ns);
+        if (!w) {
           ok = false;
           break;
         }

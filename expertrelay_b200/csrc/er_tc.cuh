@@ -58,12 +58,11 @@ __device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity, 
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with `parity` to complete. Returns false (and
-// raises the CTA's abort flag) after limit_ns, or as soon as it sees that
-// another role already aborted (within one suspend hint, <= 100 us).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned long long limit_ns) {
-  if (mbar_test(bar, parity)) return true;
+// The waiting part of mbar_wait, out of line: inlined, its loop made every
+// call cost over a hundred cycles more even when the phase had already
+// completed (measured), and the pipelines make several such calls per stage.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                            unsigned long long limit_ns) {
   const unsigned long long t0 = globaltimer();
   const uint32_t hint = (uint32_t)(limit_ns / 16 < 100000ull ? limit_ns / 16 + 1 : 100000ull);
   for (;;) {
@@ -75,12 +74,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
   }
 }
-// One lane polls, the whole warp learns the outcome; the warp then syncs so
+// Bounded wait for the phase with `parity` to complete. Returns false (and
+// raises the CTA's abort flag) after limit_ns, or as soon as it sees that
+// another role already aborted (within one suspend hint, <= 100 us).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long limit_ns) {
+  if (mbar_test(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, limit_ns);
+}
+// The whole warp waits (every lane tests the barrier, so the warp's control
+// flow stays uniform: a lane-0 wait inside a divergent branch cost several
+// times more per call), then agrees on lane 0's outcome; the warp syncs so
 // every lane's later accesses are ordered after the acquire.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int lane,
                                           unsigned long long limit_ns) {
-  bool w = true;
-  if (lane == 0) w = mbar_wait(bar, parity, abort_flag, limit_ns);
+  (void)lane;
+  bool w = mbar_wait(bar, parity, abort_flag, limit_ns);
   w = __shfl_sync(0xffffffffu, (int)w, 0) != 0;
   __syncwarp();
   return w;

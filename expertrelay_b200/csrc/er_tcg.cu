@@ -168,8 +168,8 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
         bool w = true;
-        if (lane == 0) w = mbar_wait(&empty[s], ph ^ 1, abort_flag, wait_ns);
-        if (!__shfl_sync(0xffffffffu, (int)w, 0)) {
+        w = warp_wait(&empty[s], ph ^ 1, abort_flag, lane, wait_ns);
+        if (!w) {
           ok = false;
           break;
         }
@@ -277,8 +277,8 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
           for (int q = 0; q < 4; ++q) zz[q] = (uint32_t)zsm[(r0 + 32 * q) * gpr + grp] * 0x01010101u;
         }
         bool w = true;
-        if (lane == 0) w = mbar_wait(&full[s], ph, abort_flag, wait_ns);
-        if (!__shfl_sync(0xffffffffu, (int)w, 0)) {
+        w = warp_wait(&full[s], ph, abort_flag, lane, wait_ns);
+        if (!w) {
           ok = false;
           break;
         }
