@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (warp == kTcTmaWarp && lane == 0) prefetch_maps(maps, t.maps_used);
   // everything above touched only this CTA's shared memory; the plan and the
   // operands come from the kernels before this one
   chain_wait();
@@ -721,6 +722,7 @@ int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
   t.plan_rw = const_cast<Plan*>(a.plan);
   t.wait_ns = L.wait_ns ? L.wait_ns : kDefaultWaitNs;
   t.stall_last = L.stall_last;
+  t.maps_used = maps_used_bits(maps);
   // 16-token tiles on single SMs, 128-token tiles on SM pairs (tc_cta_group)
   if (L.mode == 0)
     return TT == 16 ? launch_tc_mode<0, 16, 1>(maps, t, L.items_bound, st)

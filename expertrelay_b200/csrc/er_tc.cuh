@@ -276,6 +276,8 @@ struct TcArgs {
   int shared_parts;          // mode 1: K parts of each shared-expert tile (1: no split)
   Plan* plan_rw;             // error bits
   unsigned long long wait_ns;  // bound of every mbarrier wait (kDefaultWaitNs unless a test shortens it)
+  uint32_t maps_used;        // bit i: map i of TcMaps (a_routed 0-1, a_shared 2-3, b_routed 4-5, b_shared 6-7)
+                             // is encoded (prefetched at the kernel's start)
   int stall_last;            // test hook: nonzero -> the MMA issuer never completes the accumulator of the
                              // launch's last item, so its epilogue wait runs out (that item is its CTA's
                              // last: no copy is in flight when the wait gives up)
@@ -388,6 +390,29 @@ __device__ __forceinline__ bool tc_item_at(const TcArgs& t, const TcPlanCache* p
   it.slot = it.shared ? 0 : pc->slot[lo];
   it.valid = it.slot >= 0;
   return true;
+}
+
+// Prefetch the encoded tensor maps into the TMA unit's descriptor cache (one
+// lane), so the first copies do not wait for the descriptor fetch; the maps
+// are kernel parameters, so this may run before the kernel waits for the
+// one before it.
+__device__ __forceinline__ void prefetch_maps(const TcMaps& maps, uint32_t used) {
+  const CUtensorMap* m = &maps.a_routed[0];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (used & (1u << i)) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m + i)) : "memory");
+}
+
+// bits of TcArgs::maps_used for the maps a launch encoded
+inline uint32_t maps_used_bits(const TcMaps& maps) {
+  uint32_t bits = 0;
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(&maps);
+  for (int i = 0; i < 8; ++i) {
+    bool any = false;
+    for (size_t b = 0; b < sizeof(CUtensorMap) && !any; ++b) any = p[i * sizeof(CUtensorMap) + b] != 0;
+    if (any) bits |= 1u << i;
+  }
+  return bits;
 }
 
 // ---------------------------------------------------------------------------

@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (warp == kGTmaWarp && lane == 0) prefetch_maps(maps, t.maps_used);
   chain_wait();
   tc_cache_plan(t, pc);
   if (warp == kGMmaWarp) tmem_alloc<1>(tmem_slot, 512);
@@ -625,6 +626,7 @@ int launch_tcg_grouped(const TcLaunch& L, cudaStream_t st) {
   t.plan_rw = const_cast<Plan*>(a.plan);
   t.wait_ns = L.wait_ns ? L.wait_ns : kDefaultWaitNs;
   t.stall_last = 0;
+  t.maps_used = maps_used_bits(maps);
   if (L.mode == 0)
     return TT == 16 ? launch_tcg_mode<0, 16>(maps, t, L.items_bound, st) : launch_tcg_mode<0, 64>(maps, t, L.items_bound, st);
   return TT == 16 ? launch_tcg_mode<1, 16>(maps, t, L.items_bound, st) : launch_tcg_mode<1, 64>(maps, t, L.items_bound, st);
