@@ -26,6 +26,12 @@ inline int launch_check(const char* what) { return cuda_check(cudaGetLastError()
 // the stream uses. In a kernel launched without the attribute it returns at
 // once.
 __device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the chain launch (its CTAs start as resources
+// allow and run their prologue up to chain_wait) before this one completes;
+// it changes nothing about what the next kernel's chain_wait waits for.
+// Called first thing by the short kernels ahead of a tensor-core GEMM, so
+// the GEMM's barrier set-up and tensor-map prefetch overlap them.
+__device__ __forceinline__ void chain_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <typename... KArgs, typename... Args>
 inline int launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,

@@ -26,10 +26,10 @@ constexpr int kNumSched = 2;
 // problem sets its bit of `error` with atomicOr, so no report is lost.
 struct Plan {
   int n, E, k, nk;
-  int num_active;                      // groups with at least one token (shared last)
+  int num_active;                      // groups with at least one token (shared first)
   int counts[kMaxExperts + 1];         // tokens per group (counts[E] = n)
   int offsets[kMaxExperts + 1];        // first expert-sorted position of each routed group
-  int active[kMaxExperts + 1];         // active group ids, ascending, shared last
+  int active[kMaxExperts + 1];         // active group ids: the shared expert first, then routed ascending
   int item_start[kNumSched][kMaxExperts + 2];  // prefix of items over active groups
   SchedSpec sched[kNumSched];
   int tally[kMaxExperts];              // (token, slot) pairs routed to each expert
@@ -138,7 +138,7 @@ int launch_router_topk(const TopkArgs& a, int n, int E, int k, cudaStream_t st);
 // Batches of at most this many tokens run the top-k inside the dispatch kernel.
 constexpr int kFusedTopkMaxTok = 16;
 // The plan (groups, ranges, work-item schedules; the shared expert, all n
-// tokens, is the last group when `shared` is nonzero) from plan->tally, and
+// tokens, is the first group when `shared` is nonzero) from plan->tally, and
 // the scatter of the (token, slot) pairs to expert-sorted positions
 // (perm_token, perm_w, pos_of). With s0 non-null also slices each token's h
 // row once and writes the slices to its k routed positions and, when
@@ -171,6 +171,14 @@ int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaS
 // gate_sig[t] = sigmoid(sum of the nparts partial shared-gate logits of token t)
 int launch_gate_sigmoid(const float* gate_logit, int nparts, int n, float* gate_sig, cudaStream_t st);
 
+// rows [0, rows) of a [rows, K] fp32 matrix to slice (the same outputs as launch_slice_rows)
+struct SliceSet {
+  const float* src;
+  int rows, K;
+  int8_t *s0, *s1;
+  float* scale;
+};
+
 // tcgen05 grouped GEMM (er_tc.cu)
 struct TcLaunch {
   GroupArgs g;
@@ -197,13 +205,6 @@ int launch_tcg_grouped(const TcLaunch& L, cudaStream_t st);
 // two int8 slices and a scale per row of a [rows, K] fp32 / bf16 matrix
 int launch_slice_rows(const void* src, int dtype, int rows, int K, int8_t* s0, int8_t* s1, float* scale,
                       cudaStream_t st);
-// rows [0, rows) of a [rows, K] fp32 matrix to slice (the same outputs as launch_slice_rows)
-struct SliceSet {
-  const float* src;
-  int rows, K;
-  int8_t *s0, *s1;
-  float* scale;
-};
 // two such sets in one launch (K up to 8192 each)
 int launch_slice_sets(const SliceSet& a, const SliceSet& b, cudaStream_t st);
 // tokens per tcgen05 work item: 16 when every group fits (n <= 16), else 128

@@ -64,8 +64,12 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
     if (e < E) hist[e] = cnt[j];
   }
   int total, na_routed;
+  // the shared expert, when it runs, is the first active group: its work
+  // items come first in every schedule (decode launches prefetch its weights
+  // before the routing is known)
+  const int first = (shared && n > 0) ? 1 : 0;
   int off = cta_excl_scan(cnt[0] + cnt[1], tmp, &total);
-  int pos = cta_excl_scan(on[0] + on[1], tmp, &na_routed);
+  int pos = cta_excl_scan(on[0] + on[1], tmp, &na_routed) + first;
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int e = 2 * tid + j;
@@ -86,9 +90,9 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
     __syncthreads();
     return;
   }
-  const int na = na_routed + (shared && n > 0 ? 1 : 0);
+  const int na = na_routed + first;
   if (tid == 0) {
-    if (shared && n > 0) act[na_routed] = E;
+    if (first) act[0] = E;
     plan->counts[E] = n;
     plan->offsets[E] = 0;
   }
@@ -260,6 +264,7 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
   __shared__ float w_s[kFusedTopkMaxTok * kMaxTopK];
   __shared__ int bad;
   __shared__ int scan_tmp[16];
+  chain_trigger();  // the gate/up GEMM's CTAs may start their prologue meanwhile
   chain_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int me = blockIdx.x;  // this CTA's token

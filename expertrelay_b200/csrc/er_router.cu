@@ -17,6 +17,7 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const XT* __restrict__
                                                           int E, float* __restrict__ logits,
                                                           float* __restrict__ gate_logit, int* __restrict__ tally,
                                                           int ntally) {
+  chain_trigger();  // the dispatch kernel, and through it the gate/up GEMM, may start meanwhile
   chain_wait();
   constexpr int kTok = kRouterTok;
   if (blockIdx.x == 0 && tally)  // cleared for the top-k kernel's per-expert counts

@@ -20,7 +20,7 @@
 //    expert) and prefill use the same kernel.
 //  * One persistent CTA per SM, warp-specialised: one warp issues TMA, one
 //    allocates TMEM and issues MMAs, eight run the epilogue out of TMEM.
-//    A shared-memory ring and double-buffered accumulators overlap loads,
+//    A shared-memory ring and a ring of TMEM accumulators overlap loads,
 //    MMAs and epilogue. Every mbarrier wait is bounded: after the launch's
 //    wait bound (2 s unless a test shortens it) the
 //    kernel sets an abort flag and an error bit in the plan, drains what it
@@ -53,7 +53,8 @@ constexpr int kTcEpiWarp0 = 4;
 constexpr int kTcMmaWarp = 2;
 constexpr int kTcTmaWarp = 3;
 constexpr int kTcThreads = (kTcEpiWarp0 + kTcEpiWarps) * 32;
-constexpr int kTcAccCols = 256;  // TMEM columns per accumulator set (x2 buffers = 512)
+static_assert(kTcThreads >= kMaxExperts + 2, "tc_cache_plan reads one plan entry per thread");
+constexpr int kTcTmemCols = 512;  // TMEM columns allocated: a ring of accumulators
 
 // ---------------------------------------------------------------------------
 // activation slicing
@@ -142,13 +143,25 @@ struct TcGeom {
   static constexpr int kBBytes = kKC * kBChunkBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTxBytes = CG * kStageBytes;  // bytes completing on the (CTA 0) full barrier per stage
-  static constexpr int kStages = (TT >= 128 ? 196608 : 184320) / kStageBytes;
+  // 3 stages of 64 KB on pairs; 5 of 40 KB for 16-token tiles, whose
+  // throughput is set by copies in flight (a stage's turn-around is a
+  // DRAM round trip plus its MMAs)
+  static constexpr int kStages = (TT >= 128 ? 196608 : 204800) / kStageBytes;
   static constexpr int kCtaUnits = MODE == 0 ? 64 : 128;  // this CTA's intermediate columns / hidden rows
   static constexpr int kUnits = CG * kCtaUnits;           // per item
   static constexpr size_t kRingBytes = (size_t)kStages * kStageBytes;
   static constexpr size_t kXchBytes = MODE == 0 ? 4 * 2 * 16 * 32 * 4 : 0;  // gate/up exchange
   static constexpr int kChunks = (TT + 31) / 32;  // 16-token TMEM chunks per epilogue warp
-  static constexpr size_t kSmem = kRingBytes + kXchBytes + 2048 + sizeof(struct TcPlanCache);
+  // Accumulators: 2 TT columns each (both slices; on a pair, one slice per
+  // CTA). 128-token tiles double-buffer 256 columns; 16-token tiles keep a
+  // ring of 16, so the MMAs run up to 15 items ahead of the epilogue (whose
+  // first item, with every cache cold, takes several items' time).
+  static constexpr int kAccCols = 2 * TT;
+  static constexpr int kAccBufs = kTcTmemCols / kAccCols;
+  static_assert(kAccBufs >= 2 && kAccBufs <= 16, "accumulator ring");
+  // + 1024: the kernel rounds the dynamic shared memory base up to 1024 bytes
+  static constexpr size_t kSmem = 1024 + kRingBytes + kXchBytes + 2048 + sizeof(struct TcPlanCache);
+  static_assert(kSmem <= 232448, "shared memory per CTA");
 };
 
 template <int MODE, int TT, int CG>
@@ -167,8 +180,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Geo::kRingBytes + Geo::kXchBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain_bar = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + Geo::kAccBufs;
+  uint64_t* drain_bar = acc_empty + Geo::kAccBufs;
   uint64_t* xfull = drain_bar + 1;   // [pair*2 + half][buffer]: u values written
   uint64_t* xempty = xfull + 8;      // [pair*2 + half][buffer]: u values consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 8);
@@ -186,7 +199,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Geo::kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], CG * kTcEpiWarps);  // one arrival per epilogue warp of each CTA
     }
@@ -210,7 +223,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     cluster_sync();
   }
   // one warp of each CTA allocates TMEM (on a pair, the two warps collectively)
-  if (warp == kTcMmaWarp) tmem_alloc<CG>(tmem_slot, 2 * kTcAccCols);
+  if (warp == kTcMmaWarp) tmem_alloc<CG>(tmem_slot, kTcTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -243,7 +256,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           if (leader) mbar_expect_tx(&full[s], Geo::kTxBytes);
           const uint32_t fc = CG == 2 ? mapa_shared(smem_u32(&full[s]), 0) : 0u;
           const CUtensorMap* b = (MODE == 1 && it.shared) ? maps.b_shared : maps.b_routed;
-#pragma unroll
+#pragma unroll(TT == 16 ? 1 : Geo::kKC)
           for (int c = 0; c < Geo::kKC; ++c) {
             // chunks past K read as zeros (out-of-bounds fill) and add nothing
             const int x = ((it.kb0 + kb) * Geo::kKC + c) * 128;
@@ -300,13 +313,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       TcItem it;
       if (!tc_item<MODE, TT, CG>(t, pc, item, it)) break;
       if (!it.valid) continue;
-      const int ab = ic & 1;
-      const uint32_t aph = (ic >> 1) & 1;
+      const int ab = ic % Geo::kAccBufs;
+      const uint32_t aph = (ic / Geo::kAccBufs) & 1;
       bool w = true;
       w = warp_wait(&acc_empty[ab], aph ^ 1, abort_flag, lane, t.wait_ns);
       if (!w) break;
       tc_fence_after();
-      const uint32_t d = tmem_base + ab * kTcAccCols;
+      const uint32_t d = tmem_base + ab * Geo::kAccCols;
       const uint32_t idesc = CG == 1 ? idesc_i8(128, TT + it.npad) : idesc_i8(256, 2 * TT);
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
@@ -319,13 +332,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         tc_fence_after();
         if (lane == 0) {
           const uint32_t st = smem_u32(smem + s * Geo::kStageBytes);
-#pragma unroll
-          for (int c = 0; c < Geo::kKC; ++c) {
-            const uint32_t sa = st + c * Geo::kAChunkBytes, sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
+          if constexpr (TT == 16) {
+            // one MMA per iteration: short code for a launch that runs it cold
+#pragma unroll 1
+            for (int q = 0; q < 4 * Geo::kKC; ++q) {
+              const int c = q >> 2, ks = q & 3;
+              const uint32_t sa = st + c * Geo::kAChunkBytes, sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
               mma_i8<CG>(d, umma_desc_sw128(sa + ks * 32), umma_desc_sw128(sb + ks * 32), idesc,
-                         (kb > 0 || c > 0 || ks > 0) ? 1u : 0u);
+                         (kb > 0 || q > 0) ? 1u : 0u);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < Geo::kKC; ++c) {
+              const uint32_t sa = st + c * Geo::kAChunkBytes, sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                mma_i8<CG>(d, umma_desc_sw128(sa + ks * 32), umma_desc_sw128(sb + ks * 32), idesc,
+                           (kb > 0 || c > 0 || ks > 0) ? 1u : 0u);
+            }
           }
           umma_commit<CG>(&empty[s]);  // frees the stage (in both CTAs of a pair) once these MMAs have read it
         }
@@ -384,14 +408,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         xs_r[i] = ok ? __ldg(xsc + it.brow0 + tk) : 0.f;
         tw_r[i] = (MODE == 1 && ok) ? __ldg(tokw + it.brow0 + tk) : 0.f;
       }
-      const int ab = ic & 1;
-      const uint32_t aph = (ic >> 1) & 1;
+      const int ab = ic % Geo::kAccBufs;
+      const uint32_t aph = (ic / Geo::kAccBufs) & 1;
       if (!warp_wait(&acc_full[ab], aph, abort_flag, lane, t.wait_ns)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + ab * kTcAccCols + ((uint32_t)(quad * 32) << 16);
+      const uint32_t tbase = tmem_base + ab * Geo::kAccCols + ((uint32_t)(quad * 32) << 16);
       const int ld_out = MODE == 0 ? (it.shared ? t.g.Is : t.g.I) : t.g.H;
       float* out_base = it.shared ? t.out_s + (size_t)it.part * t.g.n * t.g.H : t.out_r;
       const int orow0 = (MODE == 0 && it.shared) ? it.tok0 : it.brow0;
+      if constexpr (TT == 16) {
+        // 16-token tiles run a few items per launch, so their epilogue code
+        // mostly runs cold, fetched from memory (the first item's took ~20 us
+        // unrolled): loops that are not unrolled, one TMEM column per load,
+        // keep it short. Warps of half h take tokens 8h .. 8h + 7; gate warps
+        // park their values in the exchange buffer's upper rows until the up
+        // values arrive.
+        const int b = chunk & 1;
+        const uint32_t use_ph = (chunk >> 1) & 1;
+        float* xb = xch + (xpb + b) * (16 * 32);
+        if (MODE == 0 && up_warp && !warp_wait(&xempty[xpb + b], use_ph ^ 1, abort_flag, lane, t.wait_ns)) break;
+#pragma unroll 1
+        for (int j = 0; j < 8; ++j) {
+          const int tk = half * 8 + j;
+          const uint32_t v0 = tmem_ld1(tbase + tk), v1 = tmem_ld1(tbase + TT + tk);
+          const float xs = __shfl_sync(0xffffffffu, xs_r[0], tk);
+          const float tw = MODE == 1 ? __shfl_sync(0xffffffffu, tw_r[0], tk) : 0.f;
+          tmem_ld_wait();
+          const float val = fmaf((float)(int)v1, 1.f / 256.f, (float)(int)v0) * (xs * sw);
+          if (MODE == 0)
+            xb[(up_warp ? j : 8 + j) * 32 + lane] = val;
+          else if (row_ok && tk < it.nvalid)
+            out_base[(size_t)(orow0 + tk) * ld_out + col] = val * tw;
+        }
+        if (MODE == 0) {
+          __syncwarp();
+          if (up_warp) {
+            if (lane == 0) mbar_arrive(&xfull[xpb + b]);
+          } else {
+            if (!warp_wait(&xfull[xpb + b], use_ph, abort_flag, lane, t.wait_ns)) break;
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+              const int tk = half * 8 + j;
+              const float g = xb[(8 + j) * 32 + lane], u = xb[j * 32 + lane];
+              if (row_ok && tk < it.nvalid)
+                out_base[(size_t)(orow0 + tk) * ld_out + col] = __fdividef(g, 1.f + __expf(-g)) * u;  // silu(g) * u
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xempty[xpb + b]);
+          }
+        }
+        ++chunk;
+      } else {
 #pragma unroll 1
       for (int ci = 0; ci < Geo::kChunks; ++ci) {
         const int c0 = half * 16 + 32 * ci;  // tokens c0 .. c0 + 15: lanes half*16 .. +15 of xs_r[ci]
@@ -462,6 +529,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         }
         ++chunk;
       }
+      }
       if (!alive) break;
       tc_fence_before();
       __syncwarp();
@@ -482,7 +550,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
   if (*abort_flag && threadIdx.x == 0) atomicOr(&t.plan_rw->error, 8);
-  if (warp == kTcMmaWarp) tmem_dealloc<CG>(tmem_base, 2 * kTcAccCols);
+  if (warp == kTcMmaWarp) tmem_dealloc<CG>(tmem_base, kTcTmemCols);
 }
 
 // ---------------------------------------------------------------------------
@@ -625,6 +693,7 @@ __device__ __forceinline__ void slice_set(const SliceSet& s, int b) {
 }
 
 __global__ void __launch_bounds__(256) slice_sets_kernel(SliceSet a, int a_blocks, SliceSet b) {
+  chain_trigger();  // the down GEMM's CTAs may start their prologue as SMs free up
   chain_wait();
   if ((int)blockIdx.x < a_blocks)
     slice_set(a, blockIdx.x);

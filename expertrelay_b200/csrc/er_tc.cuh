@@ -115,6 +115,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// Untiled bulk copy of `bytes` from global memory into this CTA's shared
+// memory, completing on `bar` (src, dst and bytes multiples of 16). A plain
+// load of this GPU's memory; no multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 // Pair forms: the tile lands in this CTA's shared memory and completes on the
 // barrier at shared::cluster address `bar` (CTA 0's full barrier). Plain
 // loads of this GPU's memory; no multicast.
@@ -247,6 +256,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// Eight consecutive TMEM columns per lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+// One TMEM column (32-bit) per lane.
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  return r;
+}
 // Orders this thread's earlier generic-proxy shared-memory writes before later
 // async-proxy reads of them (operands written by threads, read by tcgen05.mma).
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -289,7 +310,7 @@ struct TcArgs {
 // Entries are indexed by active position a, not by group id.
 struct TcPlanCache {
   int total;       // work items of this schedule
-  int num_active;  // active groups (routed, then the shared expert)
+  int num_active;  // active groups (the shared expert, then the routed experts)
   int nk;
   int item_start[kMaxExperts + 2];
   int group[kMaxExperts + 1];   // group id (E = shared expert)
@@ -311,22 +332,33 @@ struct TcItem {
   int part;      // mode 1 shared items: which K part (partial output) the item computes
 };
 
-// Copies the schedule `t.sched` of the plan into `pc` (all threads take part;
-// a __syncthreads must follow before any lookup).
+// Copies the schedule `t.sched` of the plan into `pc` (every thread takes
+// part; at least kMaxExperts + 2 threads; a __syncthreads must follow before
+// any lookup). Two dependent rounds of loads: every entry that can be active
+// is read together with num_active (entries past it are read and dropped),
+// then each active group's rows, range and record. Group ids are clamped to
+// 0..E, so every load stays inside its array.
 __device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) {
   const Plan* P = t.g.plan;
+  const int E = t.g.E;
+  const int a = threadIdx.x;
   const int na = min(P->num_active, kMaxExperts + 1);
-  for (int a = threadIdx.x; a <= na; a += blockDim.x) {
-    pc->item_start[a] = P->item_start[t.sched][a];
-    if (a == na) continue;
-    const int g = P->active[a];
+  const int start = a < kMaxExperts + 2 ? P->item_start[t.sched][a] : 0;
+  const int g_raw = a < kMaxExperts + 1 ? P->active[a] : E;
+  const int g = g_raw < 0 ? 0 : (g_raw > E ? E : g_raw);
+  const bool shared = g == E;
+  const bool live = a < na;
+  const int rows = live ? P->counts[g] : 0;
+  const int offset = (live && !shared) ? P->offsets[g] : 0;
+  const uint64_t addr = (live && !shared) ? t.g.expert_records[g] : 0;
+  if (a <= na) pc->item_start[a] = start;
+  if (a == na) pc->total = start;
+  if (live) {
     pc->group[a] = g;
-    pc->rows[a] = P->counts[g];
-    const bool shared = g == t.g.E;
-    pc->offset[a] = shared ? 0 : P->offsets[g];
+    pc->rows[a] = rows;
+    pc->offset[a] = offset;
     int slot = 0;
     if (!shared) {
-      const uint64_t addr = t.g.expert_records[g];
       const uint64_t base = (uint64_t)t.arena;
       slot = -1;  // record outside the arena: reported, never loaded
       if (addr >= base && (addr - base) % t.record_bytes == 0 && (addr - base) / t.record_bytes < (uint64_t)t.arena_slots)
@@ -334,9 +366,8 @@ __device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) 
     }
     pc->slot[a] = slot;
   }
-  if (threadIdx.x == 0) {
+  if (a == 0) {
     pc->num_active = na;
-    pc->total = P->item_start[t.sched][na];
     pc->nk = P->nk;
   }
 }

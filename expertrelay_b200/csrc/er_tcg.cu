@@ -45,6 +45,7 @@ constexpr int kGTmaWarp = 5;
 constexpr int kGEpiWarp0 = 6;
 constexpr int kGEpiWarps = 8;
 constexpr int kGThreads = (kGEpiWarp0 + kGEpiWarps) * 32;
+static_assert(kGThreads >= kMaxExperts + 2, "tc_cache_plan reads one plan entry per thread");
 
 template <int MODE, int TT>
 struct TcgGeom {
@@ -61,8 +62,9 @@ struct TcgGeom {
   static constexpr size_t kXchBytes = MODE == 0 ? 4 * 2 * 16 * 32 * 4 : 0;
   static constexpr int kMaxGroups = 64;               // scale groups per weight row (K / G) the kernel takes
   static constexpr size_t kZeroBytes = 128 * kMaxGroups;  // one item's zero points, [row][group]
+  // two item buffers of zero points (bulk-copied with the item's first stage)
   static constexpr size_t kSmem =
-      1024 + (size_t)kStages * kStageBytes + kXchBytes + 2048 + sizeof(TcPlanCache) + kZeroBytes;
+      1024 + (size_t)kStages * kStageBytes + 2 * kZeroBytes + kXchBytes + 2048 + sizeof(TcPlanCache);
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment (128-byte swizzle)");
   static_assert(kSlots >= 2, "at least two accumulators");
 };
@@ -111,7 +113,8 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
   constexpr int NS = Geo::kSlots;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* tail = smem + (size_t)S * Geo::kStageBytes;
+  uint8_t* zbuf = smem + (size_t)S * Geo::kStageBytes;  // [2][128 rows][groups]: zero points of an item
+  uint8_t* tail = zbuf + 2 * Geo::kZeroBytes;
   float* xch = reinterpret_cast<float*>(tail);
   uint64_t* full = reinterpret_cast<uint64_t*>(tail + Geo::kXchBytes);
   uint64_t* ready = full + S;
@@ -121,10 +124,10 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
   uint64_t* drain_bar = acc_empty + NS;
   uint64_t* xfull = drain_bar + 1;  // [pair*2 + half][buffer]: up values written
   uint64_t* xempty = xfull + 8;     // [pair*2 + half][buffer]: up values consumed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 8);
+  uint64_t* zempty = xempty + 8;    // [buffer]: the transform is done with the item's zero points
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(zempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   TcPlanCache* pc = reinterpret_cast<TcPlanCache*>(tail + Geo::kXchBytes + 2048);
-  uint8_t* zsm = reinterpret_cast<uint8_t*>(pc + 1);  // the transform's zero points of the current item
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -142,6 +145,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
       mbar_init(&xfull[i], 1);
       mbar_init(&xempty[i], 1);
     }
+    for (int i = 0; i < 2; ++i) mbar_init(&zempty[i], kGXfmWarps);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -159,12 +163,18 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
 
   if (warp == kGTmaWarp) {
     // ---------------- TMA producer ----------------
-    uint32_t kc = 0;
+    uint32_t kc = 0, zi = 0;  // k-blocks issued; items with zero points issued
     bool ok = true;
     for (int item = first_item; ok && item < total; item += item_stride) {
       TcItem it;
       if (!tc_item_at<MODE, 128, Geo::kUnits, TT>(t, pc, item, it)) break;
       if (!it.valid) continue;
+      // asymmetric records: the item's zero points ([rows][groups], contiguous
+      // in the record) ride on its first stage into a buffer the transform
+      // releases when it is done with the item
+      const bool zp = !it.shared && t.g.fmt == ER_FMT_INT4_ZP;
+      uint8_t* zdst = zbuf + (zi & 1) * Geo::kZeroBytes;
+      if (zp && !warp_wait(&zempty[zi & 1], ((zi >> 1) & 1) ^ 1, abort_flag, lane, wait_ns)) break;
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
@@ -190,12 +200,23 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
             }
           } else {
             // packed nibbles: 64 bytes per row per k-block, x / 2 a multiple of 64
-            mbar_expect_tx(&full[s], Geo::kPackBytes + Geo::kBBytes);
+            const RecordGeom rg{t.g.fmt, t.g.H, t.g.I, t.g.group};
+            const int gpr = rg.cols(MODE == 0 ? 0 : 2) / t.g.group;  // groups per row
+            // rows of the item inside its matrix (multiples of 16: so are the copies)
+            const int nr = MODE == 0 ? min(64, t.g.I - it.unit0) : min(128, t.g.H - it.unit0);
+            const uint32_t zbytes = (zp && kb == 0) ? (MODE == 0 ? 2u : 1u) * (uint32_t)(nr * gpr) : 0u;
+            mbar_expect_tx(&full[s], Geo::kPackBytes + Geo::kBBytes + zbytes);
+            const uint8_t* rec = t.arena + (size_t)it.slot * t.record_bytes;
             if (MODE == 0) {
               tma_load_3d(sp, &maps.a_routed[0], &full[s], x / 2, it.unit0, it.slot);
               tma_load_3d(sp + 4096, &maps.a_routed[1], &full[s], x / 2, it.unit0, it.slot);
+              if (zbytes) {  // gate rows' zero points to buffer rows 0..63, up rows' to 64..127
+                bulk_load(zdst, rec + rg.zero_offset(0) + (size_t)it.unit0 * gpr, nr * gpr, &full[s]);
+                bulk_load(zdst + 64 * gpr, rec + rg.zero_offset(1) + (size_t)it.unit0 * gpr, nr * gpr, &full[s]);
+              }
             } else {
               tma_load_3d(sp, &maps.a_routed[0], &full[s], x / 2, it.unit0, it.slot);
+              if (zbytes) bulk_load(zdst, rec + rg.zero_offset(2) + (size_t)it.unit0 * gpr, nr * gpr, &full[s]);
             }
           }
           const CUtensorMap* b = (MODE == 1 && it.shared) ? maps.b_shared : maps.b_routed;
@@ -204,6 +225,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
         }
         __syncwarp();
       }
+      zi += zp ? 1 : 0;
     }
     if (!ok && lane == 0) {
       // aborted: every stage issued so far lands before the CTA exits
@@ -222,80 +244,43 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
     // contiguous bytes per step and its swizzled stores fill every bank.
     const int tid = threadIdx.x;
     const int c = tid & 3, r0 = tid >> 2;
-    uint32_t kc = 0;
+    uint32_t kc = 0, zi = 0;  // k-blocks consumed; items with zero points consumed
     bool ok = true;
     for (int item = first_item; ok && item < total; item += item_stride) {
       TcItem it;
       if (!tc_item_at<MODE, 128, Geo::kUnits, TT>(t, pc, item, it)) break;
       if (!it.valid) continue;
-      const uint8_t* rec = t.arena + (size_t)it.slot * t.record_bytes;
-      const RecordGeom rg{t.g.fmt, t.g.H, t.g.I, t.g.group};
       const int kfull = MODE == 0 ? t.g.H : t.g.I;  // inputs per row of the routed matrix
       const int gpr = kfull / t.g.group;              // scale groups per row
+      // asymmetric records: the item's zero points arrive with its first
+      // stage in buffer zi % 2 (rows as in the A tile)
       const bool zp = !it.shared && t.g.fmt == ER_FMT_INT4_ZP;
-      if (zp) {
-        // the item's zero points, [row][group], staged once per item. A warp
-        // reads only the rows it transforms (8 w + 0..7, + 32 q), so it stages
-        // just those and needs no barrier beyond its own (none that could
-        // outlast an abort of the other warps).
-        // All of a batch's loads are issued before any store, so the batch
-        // costs one memory latency (a load-then-store loop would pay one per
-        // iteration).
-        __syncwarp();  // the previous item's values are no longer read
-        constexpr int kZB = 16;  // bytes per lane per batch
-        for (int base = 0; base < 32 * gpr; base += 32 * kZB) {
-          uint8_t zb[kZB];
-#pragma unroll
-          for (int u = 0; u < kZB; ++u) {
-            const int i = base + u * 32 + lane;
-            zb[u] = 0;
-            if (i < 32 * gpr) {
-              const int j = i / gpr, gi = i - j * gpr;
-              const int r = 8 * (warp & 3) + (j & 7) + 32 * (j >> 3);
-              const int which = MODE == 0 ? (r < 64 ? 0 : 1) : 2;
-              const int mrow = min(it.unit0 + (MODE == 0 ? (r & 63) : r), rg.rows(which) - 1);
-              zb[u] = __ldg(rec + rg.zero_offset(which) + (size_t)mrow * gpr + gi);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kZB; ++u) {
-            const int i = base + u * 32 + lane;
-            if (i < 32 * gpr) {
-              const int j = i / gpr, gi = i - j * gpr;
-              zsm[(8 * (warp & 3) + (j & 7) + 32 * (j >> 3)) * gpr + gi] = zb[u];
-            }
-          }
-        }
-        __syncwarp();
-      }
+      const uint8_t* zsrc = zbuf + (zi & 1) * Geo::kZeroBytes;
       for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
-        uint32_t zz[4] = {0x08080808u, 0x08080808u, 0x08080808u, 0x08080808u};
-        if (zp) {
-          const int grp = min(((it.kb0 + kb) * 128 + 32 * c) / t.g.group, gpr - 1);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) zz[q] = (uint32_t)zsm[(r0 + 32 * q) * gpr + grp] * 0x01010101u;
-        }
         bool w = true;
         w = warp_wait(&full[s], ph, abort_flag, lane, wait_ns);
         if (!w) {
           ok = false;
           break;
         }
+        const int grp = zp ? min(((it.kb0 + kb) * 128 + 32 * c) / t.g.group, gpr - 1) : 0;
         __syncwarp();
         if (!it.shared) {
           const uint32_t st = smem_u32(smem + (size_t)s * Geo::kStageBytes);
           const uint32_t sp = st + Geo::kABytes + Geo::kBBytes;
-#pragma unroll
+          // decode launches run this a few dozen times per CTA, mostly cold: one row per iteration
+#pragma unroll(TT == 16 ? 1 : 4)
           for (int q = 0; q < 4; ++q) {
             const int r = r0 + 32 * q;
+            const uint32_t zz = zp ? (uint32_t)zsrc[r * gpr + grp] * 0x01010101u : 0x08080808u;
             const uint4 p = lds128(sp + r * 64 + c * 16);
             uint32_t o[8];
-            unpack8(p.x, zz[q], o[0], o[1]);
-            unpack8(p.y, zz[q], o[2], o[3]);
-            unpack8(p.z, zz[q], o[4], o[5]);
-            unpack8(p.w, zz[q], o[6], o[7]);
+            unpack8(p.x, zz, o[0], o[1]);
+            unpack8(p.y, zz, o[2], o[3]);
+            unpack8(p.z, zz, o[4], o[5]);
+            unpack8(p.w, zz, o[6], o[7]);
             // 128-byte swizzle: 16-byte chunk j of row r sits at chunk j ^ (r % 8)
             const uint32_t row = st + r * 128;
             sts128(row + (((2 * c) ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
@@ -305,6 +290,11 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ready[s]);
+      }
+      if (!ok) break;
+      if (zp) {  // this warp no longer reads the item's zero points
+        if (lane == 0) mbar_arrive(&zempty[zi & 1]);
+        ++zi;
       }
     }
   } else if (warp == kGMmaWarp) {
@@ -418,6 +408,90 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
         const bool ok = tk < it.nvalid;
         xs_r[i] = ok ? __ldg(xsc + it.brow0 + tk) : 0.f;
         tw_r[i] = (MODE == 1 && ok) ? __ldg(tokw + it.brow0 + tk) : 0.f;
+      }
+      if constexpr (TT == 16) {
+        // 16-token tiles: warps of half h take tokens 8h .. 8h + 7, and the
+        // code is kept short (loops not unrolled where their bodies are
+        // long): a decode launch runs it once or twice per CTA, cold.
+        const int tk0 = half * 8;
+        float acc8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc8[j] = 0.f;
+        constexpr int kGB = 16;
+#pragma unroll 1
+        for (int g0 = 0; alive && g0 < sp.ngroups; g0 += kGB) {
+          float sc[kGB];
+#pragma unroll
+          for (int i = 0; i < kGB; ++i) sc[i] = g0 + i < sp.ngroups ? group_scale(g0 + i) : 0.f;
+#pragma unroll 1
+          for (int i = 0; i < kGB && g0 + i < sp.ngroups; ++i) {
+            float s_i = sc[0];  // register select, no local-memory indexing
+#pragma unroll
+            for (int q = 1; q < kGB; ++q)
+              if (i == q) s_i = sc[q];
+            const int slot = (int)(gc % NS);
+            if (!warp_wait(&acc_full[slot], (gc / NS) & 1, abort_flag, lane, wait_ns)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t tb = tmem_base + slot * Geo::kSlotCols + ((uint32_t)(quad * 32) << 16);
+            uint32_t v0[8], v1[8];
+            tmem_ld8(tb + tk0, v0);
+            tmem_ld8(tb + TT + tk0, v1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              acc8[j] = fmaf(s_i, fmaf((float)(int)v1[j], 1.f / 256.f, (float)(int)v0[j]), acc8[j]);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[slot]);
+            ++gc;
+          }
+        }
+        if (!alive) break;
+        const int ld_out = MODE == 0 ? (it.shared ? t.g.Is : t.g.I) : t.g.H;
+        float* out_base = it.shared ? t.out_s + (size_t)it.part * t.g.n * t.g.H : t.out_r;
+        const int orow0 = (MODE == 0 && it.shared) ? it.tok0 : it.brow0;
+        float val[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xs = __shfl_sync(0xffffffffu, xs_r[0], tk0 + j);
+          const float tw = MODE == 1 ? __shfl_sync(0xffffffffu, tw_r[0], tk0 + j) : 1.f;
+          val[j] = acc8[j] * xs * tw;
+        }
+        if (MODE == 0) {
+          const int b = chunk & 1;
+          const uint32_t use_ph = (chunk >> 1) & 1;
+          float* xb = xch + (xpb + b) * (16 * 32);
+          if (up_warp) {
+            if (!warp_wait(&xempty[xpb + b], use_ph ^ 1, abort_flag, lane, wait_ns)) break;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xb[j * 32 + lane] = val[j];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xfull[xpb + b]);
+          } else {
+            if (!warp_wait(&xfull[xpb + b], use_ph, abort_flag, lane, wait_ns)) break;
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+              float gv = val[0];
+#pragma unroll
+              for (int q = 1; q < 8; ++q)
+                if (j == q) gv = val[q];
+              const float u = xb[j * 32 + lane];
+              if (row_ok && tk0 + j < it.nvalid)
+                out_base[(size_t)(orow0 + tk0 + j) * ld_out + col] = __fdividef(gv, 1.f + __expf(-gv)) * u;  // silu(g) * u
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xempty[xpb + b]);
+          }
+        } else if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (tk0 + j < it.nvalid) out_base[(size_t)(orow0 + tk0 + j) * ld_out + col] = val[j];
+        }
+        ++chunk;
+        continue;
       }
       float acc[Geo::kChunks][16];
 #pragma unroll
