@@ -140,9 +140,10 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
 // One token per warp, 8 per CTA. With SLICE and rows of up to 2048
 // values, each warp first slices its token's h row (K = H values) into two
 // int8 words per lane and step, held in registers; the CTA then derives the
-// expert ranges from the tallies (CTA 0 also writes the plan). Then lane r < k of a token's warp claims the
-// position of slot r (its expert's range start plus an atomic count, from 0)
-// and the warp writes the slices to the k claimed rows and, for the shared
+// expert ranges from the tallies (CTA 0 also writes the plan). Then lane r < k
+// of a token's warp claims the position of slot r (its expert's range start,
+// plus the CTA's block of it, plus the pair's rank inside the CTA) and the
+// warp writes the slices to the k claimed rows and, for the shared
 // expert, to row nk + t. Longer rows are read twice after the scan. The row
 // loop is not unrolled: this kernel runs once per block, mostly from a cold
 // instruction cache, so its code is kept short.
@@ -159,6 +160,9 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
   __shared__ int act[kMaxExperts + 1];
   __shared__ int bad;
   __shared__ int scan_tmp[16];
+  __shared__ int ccount[kMaxExperts];  // this CTA's pairs per expert
+  __shared__ int cbase[kMaxExperts];   // their first position in the expert's range
+  for (int x = threadIdx.x; x < E; x += blockDim.x) ccount[x] = 0;  // ordered by plan_scan's barriers
   chain_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x * 8 + warp;
@@ -182,13 +186,30 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
     for (int i = 0; i < kRegVec; ++i) slice4(v[i], inv, q0[i], q1[i]);
   }
   plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad, scan_tmp);
-  if (t >= n || bad) return;  // nothing downstream reads positions of an inconsistent tally
+  // Positions: each (token, slot) pair takes a rank among this CTA's pairs
+  // of the same expert (shared-memory atomics), then one thread per expert
+  // claims the CTA's block of the expert's range with one global atomic (a
+  // popular expert would otherwise serialise hundreds of atomics on one
+  // address). Nothing downstream reads positions of an inconsistent tally.
+  const bool live = t < n && !bad;
+  int e = -1, li = 0;
+  if (live && lane < k) {
+    e = idx[(size_t)t * k + lane];
+    if (e >= 0 && e < E)
+      li = atomicAdd(&ccount[e], 1);
+    else
+      atomicOr(&plan->error, 1);
+  }
+  __syncthreads();
+  for (int x = threadIdx.x; x < E; x += blockDim.x)
+    if (ccount[x] > 0) cbase[x] = atomicAdd(&plan->cursor[x], ccount[x]);
+  __syncthreads();
+  if (!live) return;
   const int nk = n * k;
   int p = -1;
   if (lane < k) {
-    const int e = idx[(size_t)t * k + lane];
     if (e >= 0 && e < E) {
-      const int c = atomicAdd(&plan->cursor[e], 1);
+      const int c = cbase[e] + li;
       if (c >= hist[e]) {  // only an inconsistent tally gets here
         atomicOr(&plan->error, 2);
       } else {
@@ -196,8 +217,6 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
         perm_token[p] = t;
         perm_w[p] = w[(size_t)t * k + lane];
       }
-    } else {
-      atomicOr(&plan->error, 1);
     }
     pos_of[(size_t)t * k + lane] = p;
   }

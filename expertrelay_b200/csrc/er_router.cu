@@ -165,13 +165,28 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const XT* __res
   }
 }
 
-// One warp per token over logits summed from `nparts` K-slice partials.
+// One warp per token over logits summed from `nparts` K-slice partials. The
+// per-expert tallies are counted in shared memory and added to the plan's
+// once per CTA and expert: a popular expert (hundreds of tokens under Zipf
+// routing) would otherwise take one global atomic per token, serialised on
+// one address.
 template <int kPer>
-__global__ void __launch_bounds__(256) router_topk_kernel(TopkArgs a, int n, int E, int k) {
+__global__ void __launch_bounds__(512) router_topk_kernel(TopkArgs a, int n, int E, int k) {
+  __shared__ int stally[kMaxExperts];
+  int* const gtally = a.tally;  // the same for the whole CTA
+  if (gtally) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) stally[e] = 0;
+    __syncthreads();
+    a.tally = stally;
+  }
   chain_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (t >= n) return;
-  topk_token<kPer>(a, n, E, k, t, threadIdx.x & 31);
+  if (t < n) topk_token<kPer>(a, n, E, k, t, threadIdx.x & 31);
+  if (gtally) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      if (stally[e]) atomicAdd(&gtally[e], stally[e]);
+  }
 }
 
 __global__ void __launch_bounds__(256) gate_sigmoid_kernel(const float* __restrict__ gate_logit, int nparts, int n,
@@ -218,7 +233,7 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
 
 int launch_router_topk(const TopkArgs& a, int n, int E, int k, cudaStream_t st) {
   if (n <= 0) return ER_OK;
-  const int warps_per_block = 8;
+  const int warps_per_block = 16;
   const int blocks = (n + warps_per_block - 1) / warps_per_block;
   if (E <= 64)
     return launch_chained(router_topk_kernel<2>, dim3(blocks), dim3(warps_per_block * 32), 0, st,
