@@ -221,7 +221,7 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
       if (logits_sum == r.logits_in) logits_sum = nullptr;
     } else {
       if (int rc = launch_router_logits(r.h, r.h_dtype, n, H, w->router_w, w->shared_gate_w, E, logits, gate_logit,
-                                        &nparts, plan->tally, kPlanClear, st))
+                                        &nparts, plan->tally, kPlanClear, st, &plan->error))
         return rc;
       gparts = nparts;
     }

@@ -206,7 +206,8 @@ int launch_gate_sigmoid(const float* gate_logit, int nparts, int n, float* gate_
 }
 
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
-                         float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st) {
+                         float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st,
+                         int* error) {
   *nparts = 1;
   if (n <= 0) return ER_OK;
   // E == 0: only the shared-gate row (the caller supplies router logits); wg
@@ -223,6 +224,8 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
                           (const float*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally);
   }
   *nparts = kRouterKSplit;
+  if (h_dtype == ER_DTYPE_F32 && router_tc_ok(n, H, E, wr))
+    return launch_router_tc((const float*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally, error, st);
   const dim3 grid((n + kRgBM - 1) / kRgBM, kRouterKSplit);
   if (h_dtype == ER_DTYPE_BF16)
     return launch_chained(router_gemm_kernel<__nv_bfloat16>, grid, dim3(kRgThreads), 0, st, "router_gemm_kernel",

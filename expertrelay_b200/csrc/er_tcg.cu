@@ -80,14 +80,6 @@ __device__ __forceinline__ void unpack8(uint32_t w, uint32_t zz, uint32_t& o0, u
   o1 = ((__byte_perm(lo, hi, 0x7362) | 0x80808080u) - zz) ^ 0x80808080u;
 }
 
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
-}
 
 // The K range of an item and the length of its accumulation groups: routed
 // (int4) items accumulate per scale group, shared-expert (int8) items over

@@ -102,6 +102,25 @@ def test_decode8_bf16_activations(decode8, path):
     assert O.rel_l2(y, ref.y) < BF16_TOL
 
 
+@pytest.mark.parametrize("n", [65, 128, 129, 1000])
+def test_router_logits_fp32_accuracy(decode8, n):
+    """Batches of more than 64 fp32 tokens take the tensor-core router (three
+    tf32 products of exact hi/lo splits, fp32 accumulation): the logits stay
+    within fp32 rounding of the float64 product, and top-k ids follow them
+    (partial 128-token tiles included)."""
+    blk, _, dev, _ = decode8
+    x = synth.make_tokens(300 + n, n)
+    _, lg, idx, _ = _run(dev, x, _lib.PATH_TC)
+    ref = x.astype(np.float64) @ blk.router.astype(np.float64).T
+    np.testing.assert_allclose(lg, ref, rtol=1e-5, atol=2e-6)
+    order = np.argsort(-ref, axis=1, kind="stable")
+    srt = np.take_along_axis(ref, order, 1)
+    k = blk.top_k
+    clear = np.min(srt[:, :k] - srt[:, 1 : k + 1], axis=1) > 1e-5  # no near-tie inside or at the cut
+    assert clear.mean() > 0.99
+    np.testing.assert_array_equal(idx[clear], order[clear, :k])
+
+
 @pytest.mark.parametrize("n", [1, 3, 17, 70, 300])
 @pytest.mark.parametrize("path", list(PATHS_INT8))
 def test_decode_shapes_against_oracle(decode8, n, path):
