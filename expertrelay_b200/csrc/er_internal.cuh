@@ -117,7 +117,7 @@ constexpr int kRouterKSplit = 4;
 // (more than 64 tokens, at most 64 rows), one set otherwise
 inline int router_parts(int n, int rows) { return (n <= 64 || rows > 64) ? 1 : kRouterKSplit; }
 // `tally` (optional, `ntally` ints) is cleared for the top-k kernel's counts.
-// fp32 batches of more than 64 tokens with at most 64 router rows run on the
+// Batches of more than 64 tokens with at most 64 router rows run on the
 // tensor cores (er_router_tc.cu), which set bit 8 of `error` (optional) if
 // one of their waits gives up.
 int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E,
@@ -125,7 +125,7 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
                          int* error = nullptr);
 // the tensor-core router (er_router_tc.cu): whether it takes the batch, and its launch
 bool router_tc_ok(int n, int H, int E, const void* wr);
-int launch_router_tc(const float* h, int n, int H, const float* wr, const float* wg, int E, float* logits,
+int launch_router_tc(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E, float* logits,
                      float* gate_logit, int* tally, int ntally, int* error, cudaStream_t st);
 // The top-k step's inputs and outputs: softmax + top-k over the sum of
 // `nparts` partial logits (and the sigmoid of `gparts` partial shared-gate

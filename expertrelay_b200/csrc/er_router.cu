@@ -224,8 +224,8 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
                           (const float*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally);
   }
   *nparts = kRouterKSplit;
-  if (h_dtype == ER_DTYPE_F32 && router_tc_ok(n, H, E, wr))
-    return launch_router_tc((const float*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally, error, st);
+  if (router_tc_ok(n, H, E, wr))
+    return launch_router_tc(h, h_dtype, n, H, wr, wg, E, logits, gate_logit, tally, ntally, error, st);
   const dim3 grid((n + kRgBM - 1) / kRgBM, kRouterKSplit);
   if (h_dtype == ER_DTYPE_BF16)
     return launch_chained(router_gemm_kernel<__nv_bfloat16>, grid, dim3(kRgThreads), 0, st, "router_gemm_kernel",

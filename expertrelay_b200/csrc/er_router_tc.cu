@@ -117,6 +117,11 @@ __device__ __forceinline__ void split_tile(uint32_t hi_addr, uint32_t lo_addr, i
 
 }  // namespace
 
+// bf16 tokens: bf16 values are exact tf32 values, so a token tile needs no
+// lo part; TMA stages the 32 inputs of a k-block unswizzled (64 bytes per
+// row, in the lo tile's space) and warps 0-3 widen them into the hi tile's
+// swizzled fp32 layout. Two products per MMA step instead of three.
+template <bool BF>
 __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_constant__ RtMaps maps, RtArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -136,7 +141,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
   const int kbeg = blockIdx.y * slice;
   const int klen = max(0, min(slice, a.H - kbeg));
   const int nkb = (klen + kRtKBlock - 1) / kRtKBlock;
-  const uint32_t tx = kRtTxBytes - (a.has_gate ? 0 : kRtGateRows * 128);
+  const uint32_t tx = kRtTxBytes - (a.has_gate ? 0 : kRtGateRows * 128) - (BF ? kRtTokens * 64 : 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRtStages; ++s) {
       mbar_init(&full[s], 1);
@@ -176,7 +181,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
         uint8_t* st = smem + (size_t)s * kRtStageBytes;
         const int x = kbeg + kb * kRtKBlock;
         mbar_expect_tx(&full[s], tx);
-        tma_load_2d(st + kRtAHi, &maps.h, &full[s], x, m0);
+        tma_load_2d(st + (BF ? kRtALo : kRtAHi), &maps.h, &full[s], x, m0);
         tma_load_2d(st + kRtBHi, &maps.w, &full[s], x, 0);
         if (a.has_gate) tma_load_2d(st + kRtGHi, &maps.gate, &full[s], x, 0);
       }
@@ -209,11 +214,11 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
           const uint32_t acc = ks > 0 ? 1u : 0u;
           mma_tf32(d_r, ah, umma_desc_sw128(st + kRtBHi + o), id_r, acc);
           mma_tf32(d_r, ah, umma_desc_sw128(st + kRtBLo + o), id_r, 1u);
-          mma_tf32(d_r, al, umma_desc_sw128(st + kRtBHi + o), id_r, 1u);
+          if (!BF) mma_tf32(d_r, al, umma_desc_sw128(st + kRtBHi + o), id_r, 1u);
           if (a.has_gate) {
             mma_tf32(d_g, ah, umma_desc_sw128(st + kRtGHi + o), id_g, acc);
             mma_tf32(d_g, ah, umma_desc_sw128(st + kRtGLo + o), id_g, 1u);
-            mma_tf32(d_g, al, umma_desc_sw128(st + kRtGHi + o), id_g, 1u);
+            if (!BF) mma_tf32(d_g, al, umma_desc_sw128(st + kRtGHi + o), id_g, 1u);
           }
         }
         umma_commit<1>(&empty[s]);     // the stage is free once these MMAs have read it
@@ -269,7 +274,19 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
         break;
       }
       const uint32_t st = smem_u32(smem + (size_t)s * kRtStageBytes);
-      split_tile(st + kRtAHi, st + kRtALo, kRtTokens, tid, 128);
+      if (BF) {
+        // widen: 16-byte fp32 chunk j of row r (inputs 4j .. 4j + 3) from 8
+        // staged bytes, stored at chunk j ^ (r % 8) of the 128-byte-swizzled row
+        for (int c = tid; c < kRtTokens * 8; c += 128) {
+          const int r = c >> 3, j = c & 7;
+          uint32_t u0, u1;
+          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(u0), "=r"(u1) : "r"(st + kRtALo + r * 64 + j * 8));
+          sts128(st + kRtAHi + r * 128 + ((j ^ (r & 7)) << 4), u0 << 16, u0 & 0xffff0000u, u1 << 16,
+                 u1 & 0xffff0000u);
+        }
+      } else {
+        split_tile(st + kRtAHi, st + kRtALo, kRtTokens, tid, 128);
+      }
       split_tile(st + kRtBHi, st + kRtBLo, kRtRows, tid, 128);
       if (a.has_gate) split_tile(st + kRtGHi, st + kRtGLo, kRtGateRows, tid, 128);
       fence_async_smem();  // the split tiles are read by tcgen05.mma (async proxy)
@@ -317,25 +334,41 @@ static int make_map_f32(CUtensorMap* m, const float* base, uint64_t k, uint64_t 
 }
 
 bool router_tc_ok(int n, int H, int E, const void* wr) {
-  return wr && E >= 1 && E <= kRtRows && n > 64 && H % 4 == 0;
+  return wr && E >= 1 && E <= kRtRows && n > 64 && H % 8 == 0;
 }
 
-int launch_router_tc(const float* h, int n, int H, const float* wr, const float* wg, int E, float* logits,
+int launch_router_tc(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E, float* logits,
                      float* gate_logit, int* tally, int ntally, int* error, cudaStream_t st) {
   if (!router_tc_ok(n, H, E, wr)) return fail(ER_EINVAL, "tensor-core router: n %d, hidden %d, experts %d", n, H, E);
+  const bool bf = h_dtype == ER_DTYPE_BF16;
   static int done_dev = -1;
   int dev = 0;
   if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
   if (done_dev != dev) {
-    if (int rc = cuda_check(
-            cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRtSmem),
-            "router_tc smem attribute"))
-      return rc;
+    for (auto* k : {router_tc_kernel<false>, router_tc_kernel<true>})
+      if (int rc = cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRtSmem),
+                              "router_tc smem attribute"))
+        return rc;
     done_dev = dev;
   }
   RtMaps maps;
   memset(&maps, 0, sizeof(maps));
-  if (int rc = make_map_f32(&maps.h, h, H, n, kRtTokens, "router tokens")) return rc;
+  if (bf) {
+    // bf16 tokens: 32 inputs (64 bytes) per row and k-block, unswizzled
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(ER_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    if (((uintptr_t)h & 15) || ((H * 2) & 15)) return fail(ER_EINVAL, "tensor map router tokens: alignment");
+    const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)H * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kRtKBlock, (cuuint32_t)kRtTokens};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(&maps.h, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(h), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ER_ECUDA, "cuTensorMapEncodeTiled(router tokens) failed (%d)", (int)r);
+  } else if (int rc = make_map_f32(&maps.h, static_cast<const float*>(h), H, n, kRtTokens, "router tokens")) {
+    return rc;
+  }
   if (int rc = make_map_f32(&maps.w, wr, H, E, kRtRows, "router rows")) return rc;
   if (wg)
     if (int rc = make_map_f32(&maps.gate, wg, H, 1, kRtGateRows, "shared gate row")) return rc;
@@ -351,7 +384,8 @@ int launch_router_tc(const float* h, int n, int H, const float* wr, const float*
   a.error = error;
   a.wait_ns = kDefaultWaitNs;
   const dim3 grid((n + kRtTokens - 1) / kRtTokens, kRouterKSplit);
-  if (int rc = launch_chained(router_tc_kernel, grid, dim3(kRtThreads), kRtSmem, st, "router_tc_kernel", maps, a))
+  if (int rc = launch_chained(bf ? router_tc_kernel<true> : router_tc_kernel<false>, grid, dim3(kRtThreads), kRtSmem,
+                              st, "router_tc_kernel", maps, a))
     return rc;
   return launch_check("router_tc_kernel");
 }

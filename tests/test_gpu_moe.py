@@ -102,15 +102,21 @@ def test_decode8_bf16_activations(decode8, path):
     assert O.rel_l2(y, ref.y) < BF16_TOL
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("n", [65, 128, 129, 1000])
-def test_router_logits_fp32_accuracy(decode8, n):
-    """Batches of more than 64 fp32 tokens take the tensor-core router (three
-    tf32 products of exact hi/lo splits, fp32 accumulation): the logits stay
-    within fp32 rounding of the float64 product, and top-k ids follow them
-    (partial 128-token tiles included)."""
+def test_router_logits_accuracy(decode8, n, dtype):
+    """Batches of more than 64 tokens take the tensor-core router (tf32
+    products of exact hi/lo splits: three for fp32 tokens, two for bf16 ones,
+    which are exact in tf32; fp32 accumulation): the logits stay within fp32
+    rounding of the float64 product, and top-k ids follow them (partial
+    128-token tiles included)."""
     blk, _, dev, _ = decode8
     x = synth.make_tokens(300 + n, n)
-    _, lg, idx, _ = _run(dev, x, _lib.PATH_TC)
+    tdt = torch.float32
+    if dtype == "bf16":
+        tdt = torch.bfloat16
+        x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    _, lg, idx, _ = _run(dev, x, _lib.PATH_TC, dtype=tdt)
     ref = x.astype(np.float64) @ blk.router.astype(np.float64).T
     np.testing.assert_allclose(lg, ref, rtol=1e-5, atol=2e-6)
     order = np.argsort(-ref, axis=1, kind="stable")
