@@ -124,7 +124,7 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
                          float* logits, float* gate_logit, int* nparts, int* tally, int ntally, cudaStream_t st,
                          int* error = nullptr);
 // the tensor-core router (er_router_tc.cu): whether it takes the batch, and its launch
-bool router_tc_ok(int n, int H, int E, const void* wr);
+bool router_tc_ok(int n, int H, int E, const void* wr, const void* wg);
 int launch_router_tc(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E, float* logits,
                      float* gate_logit, int* tally, int ntally, int* error, cudaStream_t st);
 // The top-k step's inputs and outputs: softmax + top-k over the sum of

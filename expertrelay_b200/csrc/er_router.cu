@@ -224,7 +224,7 @@ int launch_router_logits(const void* h, int h_dtype, int n, int H, const float* 
                           (const float*)h, n, H, wr, wg, E, logits, gate_logit, tally, ntally);
   }
   *nparts = kRouterKSplit;
-  if (router_tc_ok(n, H, E, wr))
+  if (router_tc_ok(n, H, E, wr, wg))
     return launch_router_tc(h, h_dtype, n, H, wr, wg, E, logits, gate_logit, tally, ntally, error, st);
   const dim3 grid((n + kRgBM - 1) / kRgBM, kRouterKSplit);
   if (h_dtype == ER_DTYPE_BF16)

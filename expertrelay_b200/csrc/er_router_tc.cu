@@ -13,17 +13,20 @@
 // One CTA per 128-token tile and K slice (the same K slices, and the same
 // partial-logit layout, as the SIMT router_gemm_kernel, so the top-k kernel
 // adds them unchanged):
-//  * warp 4 (lane 0) TMA-loads per 32-input k-block the token tile (128 rows
+//  * warp 8 (lane 0) TMA-loads per 32-input k-block the token tile (128 rows
 //    x 128 bytes), the router rows (64-row box: rows past E read as zeros)
 //    and the gate row (16-row box: rows past 1 read as zeros), 128-byte
 //    swizzled, into a stage of a 4-deep ring;
-//  * warps 0-3 split every staged row into hi (in place) and lo (beside it):
-//    the split is elementwise, so the swizzled layout is kept as it is;
-//  * warp 5 issues per k-block 4 x 3 MMAs (M = 128 tokens, N = 64 router
-//    rows) into a fresh TMEM accumulator and 4 x 3 (N = 16, the gate row)
-//    into a second, and frees the stage;
-//  * warps 0-3 add each k-block's accumulators into fp32 registers (lane =
-//    token) and finally write the partial logits.
+//  * warps 0-7 split every staged row into hi (in place) and lo (beside it):
+//    the split is elementwise, so the swizzled layout is kept as it is; the
+//    gate row is split into row E of the router tile (E < 64), so one MMA
+//    covers both;
+//  * warp 9 issues per 8-input step A_hi x [W_hi; W_lo] (M = 128 tokens,
+//    N = 128) and A_lo x W_hi (N = 64) into a fresh TMEM accumulator per
+//    k-block, and frees the stage;
+//  * warps 0-7 add each k-block's accumulators into fp32 registers (lane =
+//    token; two warps per TMEM lane quadrant, 32 router columns each) and
+//    finally write the partial logits.
 // Every mbarrier wait is bounded: a CTA that gives up raises bit 8 of the
 // plan's error word (the combine then writes NaN rows), drains its copies
 // and frees its TMEM.
@@ -34,20 +37,26 @@ namespace er {
 namespace {
 
 constexpr int kRtTokens = 128;    // tokens per CTA (MMA M)
-constexpr int kRtRows = 64;       // router rows per MMA (N): E <= 64
-constexpr int kRtGateRows = 16;   // the gate MMA's N (row 0 is the gate, rows 1.. read as zeros)
+constexpr int kRtRows = 64;       // router rows of the B tile: E router rows, then the gate row (E < 64)
+constexpr int kRtGateRows = 16;   // the gate's staging box (row 0 is the gate, rows 1.. read as zeros)
 constexpr int kRtKBlock = 32;     // fp32 inputs per stage (128 bytes per row)
 constexpr int kRtStages = 4;
-constexpr int kRtThreads = 192;   // warps 0-3 split / epilogue, 4 TMA, 5 MMA
-constexpr int kRtTmaWarp = 4;
-constexpr int kRtMmaWarp = 5;
-// Two accumulator buffers of 128 columns ([0, 64) router rows, [64, 80) the
-// gate): each k-block's 12 (+ 12) MMAs start a fresh accumulator, which warps
-// 0-3 add into fp32 registers while the next block accumulates. The tensor
-// core's fp32 accumulation rounds less accurately than an fp32 add, and a
-// running accumulator over a whole K slice (384 MMAs) drifted to ~6e-6 of a
-// unit logit; a sum of 16 blocks rounded in registers stays at fp32 level.
-constexpr int kRtAccCols = 128;
+constexpr int kRtSplitWarps = 8;  // warps 0-7 split / add / epilogue, 8 TMA, 9 MMA
+constexpr int kRtSplitThreads = kRtSplitWarps * 32;
+constexpr int kRtThreads = kRtSplitThreads + 64;
+constexpr int kRtTmaWarp = kRtSplitWarps;
+constexpr int kRtMmaWarp = kRtSplitWarps + 1;
+// Per MMA step two MMAs: A_hi x [W_hi; W_lo] (N = 128: the hi and the lo
+// products side by side) and A_lo x W_hi (N = 64; not for bf16 tokens). Small
+// MMAs cost about the same as these regardless of N, so fewer and wider ones
+// (the gate row rides in the router tile) keep the tensor pipe fed. Two
+// accumulator buffers of 256 columns ([0, 128) the wide MMA, [128, 192) the
+// other): each k-block's MMAs start a fresh accumulator, which warps 0-7 add
+// into fp32 registers while the next block accumulates. The tensor core's fp32
+// accumulation rounds less accurately than an fp32 add, and a running
+// accumulator over a whole K slice drifted to ~6e-6 of a unit logit; a sum of
+// 16 blocks rounded in registers stays at fp32 level.
+constexpr int kRtAccCols = 256;
 constexpr int kRtTmemCols = 2 * kRtAccCols;
 
 // Stage layout (each tile 1024-byte aligned, as the 128-byte swizzle needs):
@@ -55,12 +64,11 @@ constexpr int kRtAHi = 0;                           // tokens, hi (TMA writes x,
 constexpr int kRtALo = kRtAHi + kRtTokens * 128;    // tokens, lo
 constexpr int kRtBHi = kRtALo + kRtTokens * 128;    // router rows, hi
 constexpr int kRtBLo = kRtBHi + kRtRows * 128;      // router rows, lo
-constexpr int kRtGHi = kRtBLo + kRtRows * 128;      // gate rows, hi
-constexpr int kRtGLo = kRtGHi + kRtGateRows * 128;  // gate rows, lo
-constexpr int kRtStageBytes = kRtGLo + kRtGateRows * 128;
-constexpr int kRtTxBytes = kRtStageBytes / 2;       // bytes TMA writes per stage (the hi tiles)
+constexpr int kRtGHi = kRtBLo + kRtRows * 128;      // the gate row as TMA stages it (moved into row E)
+constexpr int kRtStageBytes = kRtGHi + kRtGateRows * 128;
+constexpr int kRtTxBytes = (kRtTokens + kRtRows + kRtGateRows) * 128;  // bytes TMA writes per stage
 constexpr size_t kRtSmem = 1024 + (size_t)kRtStages * kRtStageBytes + 256;
-static_assert(kRtStageBytes % 1024 == 0 && kRtGHi % 1024 == 0 && kRtGLo % 1024 == 0, "tile alignment");
+static_assert(kRtStageBytes % 1024 == 0 && kRtGHi % 1024 == 0, "tile alignment");
 static_assert(kRtSmem <= 232448, "shared memory per CTA");
 
 struct RtMaps {
@@ -101,9 +109,13 @@ __device__ __forceinline__ void split_tf32(uint32_t x, uint32_t& hi, uint32_t& l
 
 // Splits `rows` staged rows of 128 bytes (hi tile at `hi_addr`, lo tile at
 // `lo_addr`, shared-memory addresses) by the calling thread's share: thread
-// `tid` of `nthreads` takes 16-byte chunks tid, tid + nthreads, ...
-__device__ __forceinline__ void split_tile(uint32_t hi_addr, uint32_t lo_addr, int rows, int tid, int nthreads) {
+// `tid` of `nthreads` takes 16-byte chunks tid, tid + nthreads, ...; row
+// `skip` (if any) is left to the caller.
+__device__ __forceinline__ void split_tile(uint32_t hi_addr, uint32_t lo_addr, int rows, int tid, int nthreads,
+                                           int skip = -1) {
+#pragma unroll 4
   for (int c = tid; c < rows * 8; c += nthreads) {
+    if ((c >> 3) == skip) continue;
     const uint4 v = lds128(hi_addr + c * 16);
     uint4 h, l;
     split_tf32(v.x, h.x, l.x);
@@ -119,7 +131,7 @@ __device__ __forceinline__ void split_tile(uint32_t hi_addr, uint32_t lo_addr, i
 
 // bf16 tokens: bf16 values are exact tf32 values, so a token tile needs no
 // lo part; TMA stages the 32 inputs of a k-block unswizzled (64 bytes per
-// row, in the lo tile's space) and warps 0-3 widen them into the hi tile's
+// row, in the lo tile's space) and warps 0-7 widen them into the hi tile's
 // swizzled fp32 layout. Two products per MMA step instead of three.
 template <bool BF>
 __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_constant__ RtMaps maps, RtArgs a) {
@@ -129,7 +141,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
   uint64_t* ready = full + kRtStages;
   uint64_t* empty = ready + kRtStages;
   uint64_t* acc_full = empty + kRtStages;   // [2]: a k-block's accumulators are complete
-  uint64_t* acc_empty = acc_full + 2;       // [2]: warps 0-3 have read them
+  uint64_t* acc_empty = acc_full + 2;       // [2]: warps 0-7 have read them
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -145,12 +157,12 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRtStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 4);
+      mbar_init(&ready[s], kRtSplitWarps);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kRtSplitWarps);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -197,7 +209,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
     __syncwarp();
   } else if (warp == kRtMmaWarp) {
     // ---------------- MMA issuer ----------------
-    const uint32_t id_r = idesc_tf32(kRtTokens, kRtRows), id_g = idesc_tf32(kRtTokens, kRtGateRows);
+    const uint32_t id_w = idesc_tf32(kRtTokens, 2 * kRtRows), id_r = idesc_tf32(kRtTokens, kRtRows);
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % kRtStages, b = kb & 1;
       const uint32_t ph = (kb / kRtStages) & 1, bph = (kb >> 1) & 1;
@@ -206,20 +218,14 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
       tc_fence_after();
       if (lane == 0) {
         const uint32_t st = smem_u32(smem + (size_t)s * kRtStageBytes);
-        const uint32_t d_r = tmem_base + b * kRtAccCols, d_g = d_r + kRtRows;
+        const uint32_t d_w = tmem_base + b * kRtAccCols, d_l = d_w + 2 * kRtRows;
 #pragma unroll 1
         for (int ks = 0; ks < kRtKBlock / 8; ++ks) {  // 8 fp32 inputs (32 bytes) per MMA
           const uint32_t o = ks * 32;
-          const uint64_t ah = umma_desc_sw128(st + kRtAHi + o), al = umma_desc_sw128(st + kRtALo + o);
           const uint32_t acc = ks > 0 ? 1u : 0u;
-          mma_tf32(d_r, ah, umma_desc_sw128(st + kRtBHi + o), id_r, acc);
-          mma_tf32(d_r, ah, umma_desc_sw128(st + kRtBLo + o), id_r, 1u);
-          if (!BF) mma_tf32(d_r, al, umma_desc_sw128(st + kRtBHi + o), id_r, 1u);
-          if (a.has_gate) {
-            mma_tf32(d_g, ah, umma_desc_sw128(st + kRtGHi + o), id_g, acc);
-            mma_tf32(d_g, ah, umma_desc_sw128(st + kRtGLo + o), id_g, 1u);
-            if (!BF) mma_tf32(d_g, al, umma_desc_sw128(st + kRtGHi + o), id_g, 1u);
-          }
+          // B = [W_hi; W_lo]: the lo tile follows the hi tile, 128 rows in 16 swizzle atoms
+          mma_tf32(d_w, umma_desc_sw128(st + kRtAHi + o), umma_desc_sw128(st + kRtBHi + o), id_w, acc);
+          if (!BF) mma_tf32(d_l, umma_desc_sw128(st + kRtALo + o), umma_desc_sw128(st + kRtBHi + o), id_r, acc);
         }
         umma_commit<1>(&empty[s]);     // the stage is free once these MMAs have read it
         umma_commit<1>(&acc_full[b]);  // and the block's accumulators are complete
@@ -233,32 +239,40 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
     }
     __syncwarp();
   } else {
-    // ---------------- split (warps 0-3), block sums, epilogue ----------------
-    // Split k-block kb, then add k-block kb - 1's accumulators (lane l of warp
-    // w: token m0 + 32 w + l, TMEM lanes 32 w ..), so the MMAs of block kb
-    // overlap the add of block kb - 1.
-    const int tid = threadIdx.x;  // 0..127
-    const uint32_t lanes = (uint32_t)(warp * 32) << 16;
-    float acc[kRtRows], gacc = 0.f;
+    // ---------------- split (warps 0-7), block sums, epilogue ----------------
+    // Split k-block kb, then add k-block kb - 1's accumulators, so the MMAs
+    // of block kb overlap the add of block kb - 1. Lane l of warp w holds
+    // token m0 + 32 (w % 4) + l (TMEM lanes of quadrant w % 4) and router
+    // columns 32 (w / 4) .. + 31.
+    constexpr int kCols = kRtRows / 2;
+    const int tid = threadIdx.x;  // 0..255
+    const int quad = warp & 3, col0 = (warp >> 2) * kCols;
+    // the gate logit is column E (held by the warp whose columns include it)
+    const bool gate_warp = a.has_gate && a.E >= col0 && a.E < col0 + kCols;
+    const uint32_t lanes = (uint32_t)(quad * 32) << 16;
+    float acc[kCols];
 #pragma unroll
-    for (int j = 0; j < kRtRows; ++j) acc[j] = 0.f;
+    for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
     auto add_block = [&](int kb) -> bool {
       const int b = kb & 1;
       if (!warp_wait(&acc_full[b], (kb >> 1) & 1, abort_flag, lane, a.wait_ns)) return false;
       tc_fence_after();
       const uint32_t tb = tmem_base + b * kRtAccCols + lanes;
+      // this warp's 32 columns of the three products: hi x hi at c, hi x lo
+      // at 64 + c, lo x hi at 128 + c (the block's partials, added in order)
 #pragma unroll
-      for (int c0 = 0; c0 < kRtRows; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tb + c0, v);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v0[16], v1[16], v2[16];
+        tmem_ld16(tb + col0 + 16 * h, v0);
+        tmem_ld16(tb + kRtRows + col0 + 16 * h, v1);
+        if (!BF) tmem_ld16(tb + 2 * kRtRows + col0 + 16 * h, v2);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[c0 + j] += __uint_as_float(v[j]);
-      }
-      if (a.has_gate) {
-        const uint32_t g = tmem_ld1(tb + kRtRows);
-        tmem_ld_wait();
-        gacc += __uint_as_float(g);
+        for (int j = 0; j < 16; ++j) {
+          float p = __uint_as_float(v0[j]) + __uint_as_float(v1[j]);
+          if (!BF) p += __uint_as_float(v2[j]);
+          acc[16 * h + j] += p;
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -277,7 +291,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
       if (BF) {
         // widen: 16-byte fp32 chunk j of row r (inputs 4j .. 4j + 3) from 8
         // staged bytes, stored at chunk j ^ (r % 8) of the 128-byte-swizzled row
-        for (int c = tid; c < kRtTokens * 8; c += 128) {
+#pragma unroll 4
+        for (int c = tid; c < kRtTokens * 8; c += kRtSplitThreads) {
           const int r = c >> 3, j = c & 7;
           uint32_t u0, u1;
           asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(u0), "=r"(u1) : "r"(st + kRtALo + r * 64 + j * 8));
@@ -285,10 +300,22 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
                  u1 & 0xffff0000u);
         }
       } else {
-        split_tile(st + kRtAHi, st + kRtALo, kRtTokens, tid, 128);
+        split_tile(st + kRtAHi, st + kRtALo, kRtTokens, tid, kRtSplitThreads);
       }
-      split_tile(st + kRtBHi, st + kRtBLo, kRtRows, tid, 128);
-      if (a.has_gate) split_tile(st + kRtGHi, st + kRtGLo, kRtGateRows, tid, 128);
+      // router rows (rows past E are zeros) and, in row E, the gate row from
+      // its staging tile: logical chunk j sits at chunk j ^ (row % 8)
+      split_tile(st + kRtBHi, st + kRtBLo, kRtRows, tid, kRtSplitThreads, a.has_gate ? a.E : -1);
+      if (a.has_gate && tid < 8) {
+        const uint4 v = lds128(st + kRtGHi + tid * 16);  // gate row 0: chunk j at j
+        uint4 h, l;
+        split_tf32(v.x, h.x, l.x);
+        split_tf32(v.y, h.y, l.y);
+        split_tf32(v.z, h.z, l.z);
+        split_tf32(v.w, h.w, l.w);
+        const uint32_t off = a.E * 128 + ((tid ^ (a.E & 7)) << 4);
+        sts128(st + kRtBHi + off, h.x, h.y, h.z, h.w);
+        sts128(st + kRtBLo + off, l.x, l.y, l.z, l.w);
+      }
       fence_async_smem();  // the split tiles are read by tcgen05.mma (async proxy)
       __syncwarp();
       if (lane == 0) mbar_arrive(&ready[s]);
@@ -296,13 +323,19 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
     }
     if (ok && nkb > 0) ok = add_block(nkb - 1);
     if (ok) {  // an empty K slice (a hidden size smaller than the slices) writes zeros
-      const int t = m0 + warp * 32 + lane;
+      const int t = m0 + quad * 32 + lane;
       if (t < a.n) {
         float* lrow = a.logits + ((size_t)blockIdx.y * a.n + t) * a.E;
 #pragma unroll
-        for (int j = 0; j < kRtRows; ++j)
-          if (j < a.E) lrow[j] = acc[j];
-        if (a.has_gate) a.gate_logit[(size_t)blockIdx.y * a.n + t] = gacc;
+        for (int j = 0; j < kCols; ++j)
+          if (col0 + j < a.E) lrow[col0 + j] = acc[j];
+        if (gate_warp) {
+          float g = acc[0];  // register select of column E, no local-memory indexing
+#pragma unroll
+          for (int j = 1; j < kCols; ++j)
+            if (col0 + j == a.E) g = acc[j];
+          a.gate_logit[(size_t)blockIdx.y * a.n + t] = g;
+        }
       }
     }
   }
@@ -333,13 +366,13 @@ static int make_map_f32(CUtensorMap* m, const float* base, uint64_t k, uint64_t 
   return ER_OK;
 }
 
-bool router_tc_ok(int n, int H, int E, const void* wr) {
-  return wr && E >= 1 && E <= kRtRows && n > 64 && H % 8 == 0;
+bool router_tc_ok(int n, int H, int E, const void* wr, const void* wg) {
+  return wr && E >= 1 && E + (wg ? 1 : 0) <= kRtRows && n > 64 && H % 8 == 0;
 }
 
 int launch_router_tc(const void* h, int h_dtype, int n, int H, const float* wr, const float* wg, int E, float* logits,
                      float* gate_logit, int* tally, int ntally, int* error, cudaStream_t st) {
-  if (!router_tc_ok(n, H, E, wr)) return fail(ER_EINVAL, "tensor-core router: n %d, hidden %d, experts %d", n, H, E);
+  if (!router_tc_ok(n, H, E, wr, wg)) return fail(ER_EINVAL, "tensor-core router: n %d, hidden %d, experts %d", n, H, E);
   const bool bf = h_dtype == ER_DTYPE_BF16;
   static int done_dev = -1;
   int dev = 0;
