@@ -95,14 +95,27 @@ __device__ __forceinline__ void warp_select(const float (&v)[kPer], int E, int k
 template <int kPer>
 __device__ __forceinline__ void topk_token(const TopkArgs& a, int n, int E, int k, int t, int lane) {
   const float* l = a.logits + (size_t)t * E;
+  // every partial of every entry is loaded before any is added (one memory
+  // latency, not one per partial), then added in partial order
+  float part[kPer][kRouterKSplit];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j)
+#pragma unroll
+    for (int p = 0; p < kRouterKSplit; ++p) {
+      const int e = lane + 32 * j;
+      part[j][p] = (e < E && p < a.nparts) ? l[(size_t)p * n * E + e] : 0.f;
+    }
   float v[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int e = lane + 32 * j;
     v[j] = -INFINITY;
     if (e < E) {
-      float s = l[e];
-      for (int p = 1; p < a.nparts; ++p) s += l[(size_t)p * n * E + e];
+      float s = part[j][0];
+#pragma unroll
+      for (int p = 1; p < kRouterKSplit; ++p)
+        if (p < a.nparts) s += part[j][p];
+      for (int p = kRouterKSplit; p < a.nparts; ++p) s += l[(size_t)p * n * E + e];  // more partials than kept
       v[j] = s;
       if (a.logits_sum) a.logits_sum[(size_t)t * E + e] = s;
     }
