@@ -113,8 +113,10 @@ ER_API int er_dequant_int4(const uint8_t* packed, const uint16_t* scales_f16, co
 ER_API int er_router_topk(const float* logits, int n, int num_experts, int k, int64_t* idx64, int32_t* idx32,
                    float* probs_out, void* stream);
 /* Routing straight from the tokens (runtime/qwen_moe.py:303-308): the router
- * logits h @ router_w^T in fp32 FMA (h fp32 or bf16, [n, hidden]; router_w
- * fp32 [num_experts, hidden]), then softmax + top-k as er_router_topk;
+ * logits h @ router_w^T at fp32 accuracy (h fp32 or bf16, [n, hidden];
+ * router_w fp32 [num_experts, hidden]: fp32 FMA for up to 64 tokens, tensor
+ * cores beyond, on exact tf32 hi/lo splits with fp32 accumulation), then
+ * softmax + top-k as er_router_topk;
  * logits_out [n, E] optional. scratch: device memory of
  * er_route_scratch_bytes(n, num_experts) bytes for the K-slice partial
  * logits. */
