@@ -9,7 +9,9 @@ One step = one MoE block forward over one batch of seeded synthetic tokens
 prints one JSON line. `value` is whole-job tokens/s with inputs resident in
 HBM; `e2e` is the same through the public API from pinned host buffers, with
 the host->device copy of the tokens and the device->host copy of the output
-inside the timed region. Each step is timed with CUDA events on the
+inside the timed region (HostPipeline: the copies of neighbouring steps
+overlap each step's compute; `e2e.serial_value` runs one step at a time).
+Each step is timed with CUDA events on the
 launching stream after an L2 flush (a 256 MiB write), and the dominant
 kernel is timed live through the block's stage events.
 
@@ -513,7 +515,7 @@ def main() -> None:
     import torch.distributed as dist
 
     from expertrelay_b200 import _lib, synth
-    from expertrelay_b200.moe import MoeBlock
+    from expertrelay_b200.moe import HostPipeline, MoeBlock
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -627,7 +629,32 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
-    e2e_value = world * n * args.steps / (float(t.item()) / 1e3)
+    e2e_serial_value = world * n * args.steps / (float(t.item()) / 1e3)
+
+    # the same host-to-host steps through HostPipeline: step i + 1's input copy
+    # and step i - 1's output copy overlap step i's compute (two graph slots,
+    # copy-in / compute / copy-out streams); every step's copies stay inside
+    # the timed region, from the first input copy to the last output copy
+    pipe = HostPipeline(mb, n, dtype=act_dtype, path=path, depth=2)
+    y_hosts = [y_host, torch.empty((n, block.hidden), dtype=torch.float32).pin_memory()]
+    for i in range(max(args.warmup, 3)):
+        pipe.submit(x_host, y_hosts[i % 2])
+    pipe.sync()
+    if world > 1:
+        dist.barrier()
+    p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p_start.record(pipe.s_in)
+    for i in range(args.steps):
+        pipe.submit(x_host, y_hosts[i % 2])
+    p_end.record(pipe.s_out)
+    pipe.sync()
+    t = torch.tensor([p_start.elapsed_time(p_end)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    e2e_pipe_ms = float(t.item())
+    e2e_value = world * n * args.steps / (e2e_pipe_ms / 1e3)
+    del pipe
 
     # roofline of the dominant stage
     peaks, peak_src = load_peaks()
@@ -680,7 +707,13 @@ def main() -> None:
             "l2": "flushed before every timed step (256 MiB write)",
         },
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(n * block.hidden * act_bytes),
-                "d2h_bytes_per_step": int(n * block.hidden * 4)},
+                "d2h_bytes_per_step": int(n * block.hidden * 4), "ms_per_step": e2e_pipe_ms / args.steps,
+                "how": "HostPipeline: pinned host tokens in, pinned host output back every step; step i+1's "
+                       "input copy and step i-1's output copy overlap step i's graph; timed from the first "
+                       "input copy to the last output copy; no flush (each step streams the expert weights, "
+                       "larger than L2)",
+                "serial_value": e2e_serial_value,
+                "serial_how": "one step at a time on one stream: copy in, graph, copy out; L2 flushed between steps"},
         "gpu_launches": int(launches.value),
         "roofline": roof,
         "stages_ms": stage_avg,
@@ -886,7 +919,57 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
         step_e2e()
         ends[i].record()
     torch.cuda.synchronize()
-    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+    e2e_serial_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+
+    # the same, pipelined over steps: step i+1's tokens are copied in (copy
+    # stream, second device buffer) and step i-1's output copied out (another
+    # stream) while step i runs; timed from the first input copy to the last
+    # output copy
+    cur = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    h_bufs = [h, torch.empty_like(h)]
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    run_done = [torch.cuda.Event() for _ in range(2)]
+    for s_ in (s_in, s_out):
+        s_.wait_stream(cur)
+
+    def copy_in(i):
+        b = i % 2
+        if i >= 2:
+            s_in.wait_event(run_done[b])  # step i-2 read this buffer
+        with torch.cuda.stream(s_in):
+            h_bufs[b].copy_(h_host, non_blocking=True)
+            in_done[b].record(s_in)
+
+    def run_pipelined(n_steps, start=None, end=None):
+        if start is not None:
+            start.record(s_in)
+        copy_in(0)
+        for i in range(n_steps):
+            if i + 1 < n_steps:
+                copy_in(i + 1)
+            b = i % 2
+            cur.wait_event(in_done[b])
+            out = ep.forward_many([h_bufs[b][c * mbatch:(c + 1) * mbatch] for c in range(chunks)])
+            run_done[b].record(cur)
+            s_out.wait_event(run_done[b])
+            with torch.cuda.stream(s_out):
+                for c, y in enumerate(out):
+                    y.record_stream(s_out)
+                    y_host[c * mbatch:(c + 1) * mbatch].copy_(y, non_blocking=True)
+        if end is not None:
+            end.record(s_out)
+        for s_ in (s_in, s_out):
+            cur.wait_stream(s_)
+
+    run_pipelined(2)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    run_pipelined(steps, p_start, p_end)
+    torch.cuda.synchronize()
+    e2e_ms = p_start.elapsed_time(p_end) / steps
 
     # one more step with its steps timed apart
     phases: dict = {}
@@ -895,11 +978,11 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
     ep.forward_many(parts, phases=phases)
     torch.cuda.synchronize()
     keys = ["route", "counts", "shared", "pack", "dispatch", "rows", "return", "combine"]
-    t = torch.tensor([step_ms, e2e_ms, stats[2], stats[0], stats[1]] + [phases.get(k, 0.0) for k in keys],
-                     dtype=torch.float64, device=dev)
+    t = torch.tensor([step_ms, e2e_ms, stats[2], stats[0], stats[1], e2e_serial_ms]
+                     + [phases.get(k, 0.0) for k in keys], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_max, rows_max, sent_max, got_max = (float(v) for v in t[:5].tolist())
+    ms, e2e_max, rows_max, sent_max, got_max, e2e_serial_max = (float(v) for v in t[:6].tolist())
     row_out = block.hidden * 2 + 8  # bf16 row + expert id + weight
     row_back = block.hidden * 2  # bf16 result
     link_bytes = sent_max * row_out + got_max * row_back  # bytes one rank pushes out over NVLink per step (max)
@@ -916,8 +999,13 @@ def expert_parallel_side(args, dev, block, world: int, rank: int, flush) -> dict
         "steps": steps,
         "scaling": "strong",
         "e2e": {"value": total / (e2e_max / 1e3), "unit": "tokens/s", "ms_per_step": e2e_max,
-                "h2d_bytes_per_step": int(per * block.hidden * 2), "d2h_bytes_per_step": int(per * block.hidden * 4)},
-        "phases_ms": {k: float(v) for k, v in zip(keys, t[5:].tolist())},
+                "h2d_bytes_per_step": int(per * block.hidden * 2), "d2h_bytes_per_step": int(per * block.hidden * 4),
+                "how": "each rank's tokens in from pinned host memory and its output back every step, step i+1's "
+                       "input copy and step i-1's output copy overlapping step i; first input copy to last "
+                       "output copy, max over ranks; no flush (each step streams the expert weights)",
+                "serial_value": total / (e2e_serial_max / 1e3),
+                "serial_how": "one step at a time, copies on the compute stream, L2 flushed between steps"},
+        "phases_ms": {k: float(v) for k, v in zip(keys, t[6:].tolist())},
         "phases_timing": "one step with its steps run one after another (not overlapped), max over ranks",
         "experts_per_rank": [hi - lo for lo, hi in expert_partition(block.num_experts, world)],
         "rows_computed_max_rank": int(rows_max),

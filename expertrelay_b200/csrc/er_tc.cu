@@ -212,6 +212,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kTcTmaWarp && lane == 0) prefetch_maps(maps, t.maps_used);
+  // decode tiles: the next kernel (slices or combine, a few small CTAs that
+  // fit beside this one) may launch now and wait in its chain_wait, so it
+  // starts the moment this grid completes
+  if constexpr (TT == 16) chain_trigger();
   // everything above touched only this CTA's shared memory; the plan and the
   // operands come from the kernels before this one
   chain_wait();

@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kGTmaWarp && lane == 0) prefetch_maps(maps, t.maps_used);
+  if constexpr (TT == 16) chain_trigger();  // decode tiles: the next kernel may launch and wait meanwhile
   chain_wait();
   tc_cache_plan(t, pc);
   if (warp == kGMmaWarp) tmem_alloc<1>(tmem_slot, 512);

@@ -300,3 +300,78 @@ class CapturedBlock:
         self.graph.replay()
         y_host.copy_(self.y, non_blocking=True)
         return y_host
+
+
+class HostPipeline:
+    """The MoE block over a stream of host batches (the serving loop of
+    `QwenMoe.forward` calls with numpy in and out, runtime/qwen_moe.py:293),
+    with the copies overlapped: `depth` captured graphs, each with its own
+    device input, output and workspace, and three streams, so the
+    host->device copy of batch i + 1 and the device->host copy of batch i - 1
+    run while batch i computes. Every batch's inputs are copied from the
+    caller's pinned host buffer and its result copied back into the caller's
+    pinned host buffer; `sync()` waits for all of them.
+
+    Ordering per slot b = i % depth: the input copy of batch i waits for the
+    compute of batch i - depth (which read the slot's input); the compute of
+    batch i waits for its input copy and for the output copy of batch
+    i - depth (which read the slot's output)."""
+
+    def __init__(self, block: MoeBlock, n: int, *, dtype: torch.dtype = torch.float32,
+                 path: int = _lib.PATH_AUTO, depth: int = 2):
+        if depth < 1:
+            raise ValueError("depth: at least one slot")
+        self.n, self.hidden, self.device = n, block.hidden, block.device
+        self.slots = [block.capture(n, dtype=dtype, path=path) for _ in range(depth)]
+        self.s_in, self.s_run, self.s_out = (torch.cuda.Stream(self.device) for _ in range(3))
+        self.ev_in = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_run = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_out = [torch.cuda.Event() for _ in range(depth)]
+        self.count = 0
+        # the slots' buffers were written on the capturing stream
+        for s in (self.s_in, self.s_run, self.s_out):
+            s.wait_stream(torch.cuda.current_stream(self.device))
+
+    def submit(self, h_host: torch.Tensor, y_host: torch.Tensor, before_run=None) -> torch.Tensor:
+        """Queue one batch: `h_host` [n, H] (pinned, the capture's dtype) in,
+        `y_host` [n, H] float32 (pinned) out. `before_run`, if given, is
+        called on the compute stream just before the graph replays (bench
+        hook: an L2 flush). Returns `y_host`, valid after `sync()`."""
+        if tuple(h_host.shape) != (self.n, self.hidden) or tuple(y_host.shape) != (self.n, self.hidden):
+            raise ValueError(f"host buffers must be [{self.n}, {self.hidden}]")
+        if h_host.is_cuda or y_host.is_cuda or not (h_host.is_pinned() and y_host.is_pinned()):
+            raise ValueError("host buffers must be pinned host memory")
+        depth = len(self.slots)
+        b = self.count % depth
+        slot = self.slots[b]
+        reuse = self.count >= depth
+        if reuse:
+            self.s_in.wait_event(self.ev_run[b])
+        with torch.cuda.stream(self.s_in):
+            slot.h.copy_(h_host, non_blocking=True)
+            self.ev_in[b].record(self.s_in)
+        self.s_run.wait_event(self.ev_in[b])
+        if reuse:
+            self.s_run.wait_event(self.ev_out[b])
+        with torch.cuda.stream(self.s_run):
+            if before_run is not None:
+                before_run()
+            slot.graph.replay()
+            self.ev_run[b].record(self.s_run)
+        self.s_out.wait_event(self.ev_run[b])
+        with torch.cuda.stream(self.s_out):
+            y_host.copy_(slot.y, non_blocking=True)
+            self.ev_out[b].record(self.s_out)
+        self.count += 1
+        return y_host
+
+    def join(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Make `stream` (default: the current one) wait for every queued batch."""
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        for s in (self.s_in, self.s_run, self.s_out):
+            st.wait_stream(s)
+
+    def sync(self) -> None:
+        """Wait on the host until every queued batch's output is in its host buffer."""
+        for s in (self.s_in, self.s_run, self.s_out):
+            s.synchronize()

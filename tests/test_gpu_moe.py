@@ -21,7 +21,7 @@ from conftest import golden
 from helpers import gptq_oracle_weights, oracle_weights
 
 from expertrelay_b200 import _lib, synth
-from expertrelay_b200.moe import MoeBlock
+from expertrelay_b200.moe import HostPipeline, MoeBlock
 from expertrelay_b200.store import FMT_INT4, FMT_INT8, RecordLayout
 from oracle import moe_oracle as O
 
@@ -190,6 +190,31 @@ def test_captured_graph_replays_and_follows_the_expert_table(decode8, path):
             assert not torch.equal(y_swap_graph, y_graph)
     finally:
         dev.set_expert_table(table)
+
+
+@pytest.mark.parametrize("path", ["tc", "gemv"])
+def test_host_pipeline_matches_the_graph(decode8, path):
+    """HostPipeline: host batches queued back to back (the copies of
+    neighbouring batches overlapping each batch's compute, two graph slots
+    reused in turn) come back in their own pinned host buffers, each equal to
+    the captured graph's output for that batch."""
+    _, x, dev, _ = decode8
+    rng = np.random.default_rng(5)
+    batches = [x] + [rng.standard_normal(x.shape).astype(np.float32) for _ in range(4)]
+    hs = [torch.from_numpy(b).pin_memory() for b in batches]
+    ys = [torch.full(b.shape, float("nan"), dtype=torch.float32).pin_memory() for b in batches]
+    pipe = HostPipeline(dev, x.shape[0], path=PATHS_INT8[path], depth=2)
+    for h, y in zip(hs, ys):
+        pipe.submit(h, y)
+    pipe.sync()
+    cap = dev.capture(x.shape[0], path=PATHS_INT8[path])
+    for h, y in zip(hs, ys):
+        want = cap(h.to(dev.device)).cpu()
+        assert torch.equal(y, want)
+    with pytest.raises(ValueError):
+        pipe.submit(hs[0][:4].clone().pin_memory(), ys[0][:4].clone().pin_memory())
+    with pytest.raises(ValueError):
+        pipe.submit(hs[0].clone(), ys[0])  # not pinned
 
 
 @pytest.mark.parametrize("path", list(PATHS_INT8))
