@@ -31,6 +31,12 @@ struct Plan {
   int offsets[kMaxExperts + 1];        // first expert-sorted position of each routed group
   int active[kMaxExperts + 1];         // active group ids: the shared expert first, then routed ascending
   int item_start[kNumSched][kMaxExperts + 2];  // prefix of items over active groups
+  // by active position, for the tensor-core kernels' one-round plan read:
+  // the group's tokens, first expert-sorted position and record address (0
+  // for the shared expert, or when the dispatch was given no expert table)
+  int act_rows[kMaxExperts + 1];
+  int act_off[kMaxExperts + 1];
+  unsigned long long act_rec[kMaxExperts + 1];
   SchedSpec sched[kNumSched];
   int tally[kMaxExperts];              // (token, slot) pairs routed to each expert
   int cursor[kMaxExperts];             // positions of each expert's range claimed so far
@@ -147,15 +153,17 @@ int launch_router_topk(const TopkArgs& a, int n, int E, int k, cudaStream_t st);
 constexpr int kFusedTopkMaxTok = 16;
 // The plan (groups, ranges, work-item schedules; the shared expert, all n
 // tokens, is the first group when `shared` is nonzero) from plan->tally, and
-// the scatter of the (token, slot) pairs to expert-sorted positions
+// the scatter of the (token, slot) pairs to expert-sorted positions; `records`
+// (nullable): the expert table, copied into the plan by active position
 // (perm_token, perm_w, pos_of). With s0 non-null also slices each token's h
 // row once and writes the slices to its k routed positions and, when
 // `shared` is nonzero, to shared row nk + t. With `topk` non-null (n <=
 // kFusedTopkMaxTok) the kernel first runs that top-k step itself, whose
 // idx32 / wout / tally must be idx / w / plan->tally.
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
-                    int Is, const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
-                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk, cudaStream_t st);
+                    int Is, const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records,
+                    int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale,
+                    const TopkArgs* topk, cudaStream_t st);
 // Upper bound of the items a schedule can produce (host side, for grid sizing).
 long long sched_items_bound(const SchedSpec& s, int n, int k, int E, int H, int I, int Is);
 

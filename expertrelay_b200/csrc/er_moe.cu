@@ -278,7 +278,8 @@ static int run_moe(const er_moe_weights* w, const Run& r, void* workspace, size_
   int8_t* xs1 = path == ER_PATH_TC ? reinterpret_cast<int8_t*>(ws + L.xs1) : nullptr;
   float* xscale = path == ER_PATH_TC ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
   if (int rc = launch_dispatch(r.h, r.h_dtype, idx32, topw, n, k, E, H, w->inter, w->shared_inter, specs, shared,
-                               plan, perm_token, perm_w, pos_of, xs0, xs1, xscale, fused_topk ? &topk : nullptr, st))
+                               plan, static_cast<const uint64_t*>(w->expert_records), perm_token, perm_w, pos_of, xs0,
+                               xs1, xscale, fused_topk ? &topk : nullptr, st))
     return rc;
   launches += 1;
   if (mode == kBlock && r.topk_w_out) {

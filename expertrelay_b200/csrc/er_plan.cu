@@ -52,14 +52,16 @@ __device__ __forceinline__ int cta_excl_scan(int v, int* tmp, int* total) {
 // schedules for the expert kernels. Ends with a __syncthreads.
 __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, int I, int Is, SchedSpec s0,
                           SchedSpec s1, int shared, bool write_plan, int* hist, int* offs, int* act, int* bad_out,
-                          int* tmp, const int* tally = nullptr) {
+                          int* tmp, const int* tally = nullptr, const uint64_t* records = nullptr) {
   const int tid = threadIdx.x;
   const int nk = n * k;
   int cnt[2], on[2];
+  uint64_t rec[2];  // the experts' record addresses, copied into the plan by active position
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int e = 2 * tid + j;
     cnt[j] = e < E ? (tally ? tally[e] : __ldcg(&plan->tally[e])) : 0;  // plan->tally: counted at L2 by atomics
+    rec[j] = (write_plan && records && e < E) ? records[e] : 0ull;
     on[j] = cnt[j] > 0;
     if (e < E) hist[e] = cnt[j];
   }
@@ -78,6 +80,11 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
       if (write_plan) {
         plan->counts[e] = cnt[j];
         plan->offsets[e] = off;
+        if (on[j]) {
+          plan->act_rows[pos] = cnt[j];
+          plan->act_off[pos] = off;
+          plan->act_rec[pos] = rec[j];
+        }
       }
       off += cnt[j];
       if (on[j]) act[pos++] = e;
@@ -92,7 +99,12 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
   }
   const int na = na_routed + first;
   if (tid == 0) {
-    if (first) act[0] = E;
+    if (first) {
+      act[0] = E;
+      plan->act_rows[0] = n;
+      plan->act_off[0] = 0;
+      plan->act_rec[0] = 0ull;
+    }
     plan->counts[E] = n;
     plan->offsets[E] = 0;
   }
@@ -151,7 +163,8 @@ template <typename XT, bool SLICE>
 __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h, const int32_t* __restrict__ idx,
                                                        const float* __restrict__ w, int n, int k, int E, int H, int I,
                                                        int Is, SchedSpec spec0, SchedSpec spec1, int shared,
-                                                       Plan* __restrict__ plan, int32_t* __restrict__ perm_token,
+                                                       Plan* __restrict__ plan, const uint64_t* __restrict__ records,
+                                                       int32_t* __restrict__ perm_token,
                                                        float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
                                                        int8_t* __restrict__ s0, int8_t* __restrict__ s1,
                                                        float* __restrict__ scale) {
@@ -185,7 +198,8 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
 #pragma unroll
     for (int i = 0; i < kRegVec; ++i) slice4(v[i], inv, q0[i], q1[i]);
   }
-  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad, scan_tmp);
+  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad, scan_tmp, nullptr,
+            records);
   // Positions: each (token, slot) pair takes a rank among this CTA's pairs
   // of the same expert (shared-memory atomics), then one thread per expert
   // claims the CTA's block of the expert's range with one global atomic (a
@@ -264,13 +278,18 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
 // shared memory and derives the plan from those tallies (CTA 0 writes it, the
 // top-k outputs of token c are written by CTA c), so the positions need no
 // atomics: slot j of token t goes to its expert's range start plus the
-// number of earlier (token, slot) pairs of the same expert. Warp 0 of CTA c
-// then slices token c's h row into its k rows and the shared row, so the
-// rows' stores spread over n SMs.
+// number of earlier (token, slot) pairs of the same expert. The whole CTA
+// slices token c's h row into its k rows and the shared row, so the rows'
+// stores spread over n SMs: the row is loaded right after the wait (thread i
+// holds values 4i + 4 blockDim j, in registers for rows of up to
+// 4 kSmallVec blockDim values), so its latency hides behind the top-k and
+// the plan, and its max is reduced across the warps on the way.
+constexpr int kSmallVec = 2;
 template <typename XT, bool SLICE, int KPER>
 __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restrict__ h, int n, int k, int E, int H,
                                                              int I, int Is, SchedSpec spec0, SchedSpec spec1,
                                                              int shared, Plan* __restrict__ plan,
+                                                             const uint64_t* __restrict__ records,
                                                              int32_t* __restrict__ perm_token,
                                                              float* __restrict__ perm_w, int32_t* __restrict__ pos_of,
                                                              int8_t* __restrict__ s0, int8_t* __restrict__ s1,
@@ -283,11 +302,33 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
   __shared__ float w_s[kFusedTopkMaxTok * kMaxTopK];
   __shared__ int bad;
   __shared__ int scan_tmp[16];
+  __shared__ float amax_s[16];       // per warp: max |h| over its values of the token's row
+  __shared__ int pos_s[kMaxTopK];    // the token's slots' expert-sorted positions
   chain_trigger();  // the gate/up GEMM's CTAs may start their prologue meanwhile
   chain_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nthr = blockDim.x;
   const int me = blockIdx.x;  // this CTA's token
-  for (int e = threadIdx.x; e < E; e += blockDim.x) tally_s[e] = 0;
+  const XT* x = SLICE ? h + (size_t)(me < n ? me : 0) * H : h;
+  const bool in_regs = H <= 4 * kSmallVec * nthr;
+  float4 hv[kSmallVec];
+  if (SLICE && me < n) {
+    float amax = 0.f;
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < kSmallVec; ++j) {
+        const int c = 4 * (threadIdx.x + nthr * j);
+        hv[j] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, abs_max4(hv[j]));
+      }
+    } else {
+      for (int c = 4 * threadIdx.x; c < H; c += 4 * nthr) amax = fmaxf(amax, abs_max4(load4(x + c)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) amax_s[warp] = amax;
+  }
+  for (int e = threadIdx.x; e < E; e += nthr) tally_s[e] = 0;
   __syncthreads();
   if (warp < n) {
     TopkArgs a = topk;
@@ -302,11 +343,11 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
     topk_token<KPER>(a, n, E, k, warp, lane);
   }
   __syncthreads();
-  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, me == 0, hist, offs, act, &bad, scan_tmp, tally_s);
-  if (me >= n || bad || warp != 0) return;
+  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, me == 0, hist, offs, act, &bad, scan_tmp, tally_s,
+            records);
+  if (me >= n || bad) return;  // uniform over the CTA
   const int nk = n * k;
-  int p = -1;
-  if (lane < k) {
+  if (warp == 0 && lane < k) {
     const int e = sel_s[me * k + lane];
     const float wt = w_s[me * k + lane];
     if (topk.idx32) topk.idx32[(size_t)me * k + lane] = e;
@@ -314,53 +355,36 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
     if (topk.wout) topk.wout[(size_t)me * k + lane] = wt;
     int before = 0;  // earlier (token, slot) pairs routed to e
     for (int i = 0; i < me * k + lane; ++i) before += sel_s[i] == e;
-    p = offs[e] + before;
+    const int p = offs[e] + before;
     perm_token[p] = me;
     perm_w[p] = wt;
     pos_of[(size_t)me * k + lane] = p;
+    pos_s[lane] = p;
   }
   if constexpr (SLICE) {
-    const XT* x = h + (size_t)me * H;
-    // rows of up to 2048 values: all of the lane's loads issued at once and
-    // held in registers (a loop of dependent loads costs a round trip each)
-    constexpr int kRegVec = 16;
-    const bool in_regs = H <= 128 * kRegVec;
-    float4 v[kRegVec];
+    __syncthreads();
     float amax = 0.f;
-    if (in_regs) {
-#pragma unroll
-      for (int i = 0; i < kRegVec; ++i) {
-        const int c = lane * 4 + 128 * i;
-        v[i] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int i = 0; i < kRegVec; ++i) amax = fmaxf(amax, abs_max4(v[i]));
-    } else {
-      for (int c = lane * 4; c < H; c += 128) amax = fmaxf(amax, abs_max4(load4(x + c)));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int w = 0; w < nthr / 32; ++w) amax = fmaxf(amax, amax_s[w]);
     const float inv = amax > 0.f ? 127.f / amax : 0.f;
 #pragma unroll 1
     for (int r = 0; r <= k; ++r) {  // rows r < k: the slots' positions; row k: the shared expert's row
-      const int pr = __shfl_sync(0xffffffffu, p, r < k ? r : 0);
-      const int row = r < k ? pr : (shared ? nk + me : -1);
+      const int row = r < k ? pos_s[r] : (shared ? nk + me : -1);
       if (row < 0) continue;
       int8_t* d0 = s0 + (size_t)row * H;
       int8_t* d1 = s1 + (size_t)row * H;
       if (in_regs) {
 #pragma unroll
-        for (int i = 0; i < kRegVec; ++i) {
-          const int c = lane * 4 + 128 * i;
+        for (int j = 0; j < kSmallVec; ++j) {
+          const int c = 4 * (threadIdx.x + nthr * j);
           if (c < H) {
             uint32_t w0, w1;
-            slice4(v[i], inv, w0, w1);
+            slice4(hv[j], inv, w0, w1);
             *reinterpret_cast<uint32_t*>(d0 + c) = w0;
             *reinterpret_cast<uint32_t*>(d1 + c) = w1;
           }
         }
       } else {
-        for (int c = lane * 4; c < H; c += 128) {
+        for (int c = 4 * threadIdx.x; c < H; c += 4 * nthr) {
           uint32_t w0, w1;
           slice4(load4(x + c), inv, w0, w1);
           *reinterpret_cast<uint32_t*>(d0 + c) = w0;
@@ -368,8 +392,8 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
         }
       }
     }
-    if (lane < k) scale[p] = amax / 127.f;
-    if (lane == 31 && shared) scale[nk + me] = amax / 127.f;
+    if (threadIdx.x < k) scale[pos_s[threadIdx.x]] = amax / 127.f;
+    if (threadIdx.x == 32 && shared) scale[nk + me] = amax / 127.f;
   }
 }
 
@@ -406,38 +430,39 @@ int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaS
 
 template <typename XT, bool SLICE>
 static int launch_dispatch_t(const XT* h, const int32_t* idx, const float* w, int n, int k, int E, int H, int I, int Is,
-                             const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
+                             const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records, int32_t* perm_token, float* perm_w,
                              int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk,
                              cudaStream_t st) {
   if (topk) {  // a CTA per token (at least one: CTA 0 writes the plan), a warp per token inside each
     const dim3 grid(n > 0 ? n : 1), block(32 * (n > 8 ? 16 : 8));
     if (E <= 64)
       return launch_chained(dispatch_small_kernel<XT, SLICE, 2>, grid, block, 0, st, "dispatch_small_kernel", h, n,
-                            k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1,
-                            scale, *topk);
+                            k, E, H, I, Is, specs[0], specs[1], shared, plan, records, perm_token, perm_w, pos_of, s0,
+                            s1, scale, *topk);
     return launch_chained(dispatch_small_kernel<XT, SLICE, kMaxExperts / 32>, grid, block, 0, st,
-                          "dispatch_small_kernel", h, n, k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token,
-                          perm_w, pos_of, s0, s1, scale, *topk);
+                          "dispatch_small_kernel", h, n, k, E, H, I, Is, specs[0], specs[1], shared, plan, records,
+                          perm_token, perm_w, pos_of, s0, s1, scale, *topk);
   }
   const int blocks = n > 0 ? (n + 7) / 8 : 1;  // CTA 0 writes the plan even for no tokens
   return launch_chained(dispatch_kernel<XT, SLICE>, dim3(blocks), dim3(256), 0, st, "dispatch_kernel", h, idx, w, n,
-                        k, E, H, I, Is, specs[0], specs[1], shared, plan, perm_token, perm_w, pos_of, s0, s1, scale);
+                        k, E, H, I, Is, specs[0], specs[1], shared, plan, records, perm_token, perm_w, pos_of, s0, s1,
+                        scale);
 }
 
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
-                    int Is, const SchedSpec* specs, int shared, Plan* plan, int32_t* perm_token, float* perm_w,
+                    int Is, const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records, int32_t* perm_token, float* perm_w,
                     int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk, cudaStream_t st) {
   if (topk && (n > kFusedTopkMaxTok || topk->idx32 != idx || topk->wout != w || topk->tally != plan->tally))
     return fail(ER_EINVAL, "dispatch: fused top-k needs n <= %d and its outputs as the dispatch inputs",
                 kFusedTopkMaxTok);
   if (!s0)
-    return launch_dispatch_t<float, false>(nullptr, idx, w, n, k, E, H, I, Is, specs, shared, plan, perm_token, perm_w,
-                                           pos_of, nullptr, nullptr, nullptr, topk, st);
+    return launch_dispatch_t<float, false>(nullptr, idx, w, n, k, E, H, I, Is, specs, shared, plan, records, perm_token,
+                                           perm_w, pos_of, nullptr, nullptr, nullptr, topk, st);
   if (h_dtype == ER_DTYPE_BF16)
     return launch_dispatch_t<__nv_bfloat16, true>((const __nv_bfloat16*)h, idx, w, n, k, E, H, I, Is, specs, shared,
-                                                  plan, perm_token, perm_w, pos_of, s0, s1, scale, topk, st);
-  return launch_dispatch_t<float, true>((const float*)h, idx, w, n, k, E, H, I, Is, specs, shared, plan, perm_token,
-                                        perm_w, pos_of, s0, s1, scale, topk, st);
+                                                  plan, records, perm_token, perm_w, pos_of, s0, s1, scale, topk, st);
+  return launch_dispatch_t<float, true>((const float*)h, idx, w, n, k, E, H, I, Is, specs, shared, plan, records,
+                                        perm_token, perm_w, pos_of, s0, s1, scale, topk, st);
 }
 
 }  // namespace er

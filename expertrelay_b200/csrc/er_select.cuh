@@ -95,6 +95,13 @@ __device__ __forceinline__ void warp_select(const float (&v)[kPer], int E, int k
 template <int kPer>
 __device__ __forceinline__ void topk_token(const TopkArgs& a, int n, int E, int k, int t, int lane) {
   const float* l = a.logits + (size_t)t * E;
+  // the shared gate's logit is loaded with the router's (added in part order)
+  const bool gate = lane == 0 && a.gate_sig && a.gate_logit;
+  float gl = 0.f;
+  if (gate) {
+    gl = a.gate_logit[t];
+    for (int p = 1; p < a.gparts; ++p) gl += a.gate_logit[(size_t)p * n + t];
+  }
   // every partial of every entry is loaded before any is added (one memory
   // latency, not one per partial), then added in partial order
   float part[kPer][kRouterKSplit];
@@ -121,11 +128,7 @@ __device__ __forceinline__ void topk_token(const TopkArgs& a, int n, int E, int 
     }
   }
   warp_select<kPer>(v, E, k, a.norm, t, lane, a.idx64, a.idx32, a.wout, a.tally);
-  if (lane == 0 && a.gate_sig && a.gate_logit) {
-    float gl = a.gate_logit[t];
-    for (int p = 1; p < a.gparts; ++p) gl += a.gate_logit[(size_t)p * n + t];
-    a.gate_sig[t] = sigmoid_f(gl);
-  }
+  if (gate) a.gate_sig[t] = sigmoid_f(gl);
 }
 
 }  // namespace er

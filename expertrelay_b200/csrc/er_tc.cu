@@ -216,6 +216,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   // fit beside this one) may launch now and wait in its chain_wait, so it
   // starts the moment this grid completes
   if constexpr (TT == 16) chain_trigger();
+  // Decode tiles: the shared expert's items come first in both schedules and
+  // are laid out from the launch's sizes alone, so a CTA whose first item is
+  // one of them loads that item's first weight stages now, while the kernels
+  // before this one (routing, plan) still run. The full barriers get the
+  // weight bytes without an arrival; the producer adds the activation bytes
+  // and arrives once the plan is read, and checks that the plan agrees.
+  int pre_n = 0, pre_unit0 = 0, pre_kb0 = 0;  // producer: first-item k-blocks whose weights are in flight
+  if constexpr (TT == 16) {
+    __syncthreads();  // the barriers are initialised
+    if (warp == kTcTmaWarp && t.pre_shared && first_item < tc_shared_items<MODE, Geo::kUnits, TT>(t)) {
+      TcItem p;
+      tc_item_local<MODE, 128 * Geo::kKC, Geo::kUnits, TT>(t, true, t.g.n, first_item, p);
+      pre_n = min(p.nkb, S);
+      pre_unit0 = p.unit0;
+      pre_kb0 = p.kb0;
+      if (lane == 0) {
+#pragma unroll 1
+        for (int kb = 0; kb < pre_n; ++kb) {
+          uint8_t* st = smem + kb * Geo::kStageBytes;
+          mbar_expect_tx_only(&full[kb], Geo::kABytes);
+#pragma unroll 1
+          for (int c = 0; c < Geo::kKC; ++c) {
+            const int x = ((p.kb0 + kb) * Geo::kKC + c) * 128;
+            uint8_t* sa = st + c * Geo::kAChunkBytes;
+            tma_2d<CG>(sa, &maps.a_shared[0], &full[kb], 0u, x, p.unit0);
+            if (MODE == 0) tma_2d<CG>(sa + 8192, &maps.a_shared[1], &full[kb], 0u, x, p.unit0);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
   // everything above touched only this CTA's shared memory; the plan and the
   // operands come from the kernels before this one
   chain_wait();
@@ -238,6 +270,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     // ---------------- TMA producer (lane 0 issues; the warp moves in step) ----------------
     uint32_t kc = 0;  // k-blocks issued so far
     bool ok = true;
+    if (pre_n > 0) {
+      // the plan must place the item whose weights are in flight first; if
+      // not (an inconsistent tally leaves no items), report it, let the
+      // copies land (the arrivals complete the phases) and stop
+      TcItem it0;
+      const bool same = tc_item<MODE, TT, CG>(t, pc, first_item, it0) && it0.valid && it0.shared &&
+                        it0.unit0 == pre_unit0 && it0.kb0 == pre_kb0 && it0.nkb >= pre_n;
+      if (!same) {
+        ok = false;
+        if (lane == 0) {
+          atomicOr(&t.plan_rw->error, 8);
+          *abort_flag = 1;
+          for (int s = 0; s < pre_n; ++s) mbar_arrive(&full[s]);
+          for (int s = 0; s < pre_n; ++s) mbar_drain(&full[s], 0, 100000000ull);
+        }
+        __syncwarp();
+      }
+    }
     for (int item = first_item; ok && item < total; item += item_stride) {
       TcItem it;
       if (!tc_item<MODE, TT, CG>(t, pc, item, it)) break;
@@ -257,7 +307,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           // CTA 0 expects the whole pair's bytes; the peer's copies may land
           // before that (the barrier's transaction count goes negative until
           // then, and the phase cannot complete without CTA 0's arrival)
-          if (leader) mbar_expect_tx(&full[s], Geo::kTxBytes);
+          // a stage whose weights were loaded before the plan still expects its activations
+          const bool pre = kc < (uint32_t)pre_n;
+          if (leader) mbar_expect_tx(&full[s], pre ? Geo::kTxBytes - Geo::kABytes : Geo::kTxBytes);
           const uint32_t fc = CG == 2 ? mapa_shared(smem_u32(&full[s]), 0) : 0u;
           const CUtensorMap* b = (MODE == 1 && it.shared) ? maps.b_shared : maps.b_routed;
 #pragma unroll(TT == 16 ? 1 : Geo::kKC)
@@ -266,7 +318,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
             const int x = ((it.kb0 + kb) * Geo::kKC + c) * 128;
             uint8_t* sa = st + c * Geo::kAChunkBytes;
             uint8_t* sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
-            if (MODE == 0) {
+            if (pre) {
+            } else if (MODE == 0) {
               if (it.shared) {
                 tma_2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow);
                 tma_2d<CG>(sa + 8192, &maps.a_shared[1], &full[s], fc, x, arow);
@@ -795,6 +848,7 @@ int launch_tc_grouped(const TcLaunch& L, cudaStream_t st) {
   t.plan_rw = const_cast<Plan*>(a.plan);
   t.wait_ns = L.wait_ns ? L.wait_ns : kDefaultWaitNs;
   t.stall_last = L.stall_last;
+  t.pre_shared = TT == 16 && L.has_shared && L.n > 0 && a.shared_record != nullptr;
   t.maps_used = maps_used_bits(maps);
   // 16-token tiles on single SMs, 128-token tiles on SM pairs (tc_cta_group)
   if (L.mode == 0)

@@ -30,6 +30,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// raise the phase's expected transaction bytes without arriving
+__device__ __forceinline__ void mbar_expect_tx_only(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -307,6 +311,9 @@ struct TcArgs {
   unsigned long long wait_ns;  // bound of every mbarrier wait (kDefaultWaitNs unless a test shortens it)
   uint32_t maps_used;        // bit i: map i of TcMaps (a_routed 0-1, a_shared 2-3, b_routed 4-5, b_shared 6-7)
                              // is encoded (prefetched at the kernel's start)
+  int pre_shared;            // 16-token tiles: the shared expert runs in this launch (its items come first), so
+                             // CTAs whose first item is one of its load that item's first weight stages
+                             // before waiting for the kernels before them
   int stall_last;            // test hook: nonzero -> the MMA issuer never completes the accumulator of the
                              // launch's last item, so its epilogue wait runs out (that item is its CTA's
                              // last: no copy is in flight when the wait gives up)
@@ -342,29 +349,32 @@ struct TcItem {
 
 // Copies the schedule `t.sched` of the plan into `pc` (every thread takes
 // part; at least kMaxExperts + 2 threads; a __syncthreads must follow before
-// any lookup). Two dependent rounds of loads: every entry that can be active
-// is read together with num_active (entries past it are read and dropped),
-// then each active group's rows, range and record. Group ids are clamped to
-// 0..E, so every load stays inside its array.
+// any lookup). One round of loads: every entry that can be active is read
+// together with num_active (the dispatch wrote each active group's rows,
+// range and record by active position; entries past num_active are read and
+// dropped). Group ids are clamped to 0..E.
 __device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) {
   const Plan* P = t.g.plan;
   const int E = t.g.E;
   const int a = threadIdx.x;
-  const int na = min(P->num_active, kMaxExperts + 1);
+  const int na_raw = P->num_active;
+  const int nk = P->nk;
   const int start = a < kMaxExperts + 2 ? P->item_start[t.sched][a] : 0;
-  const int g_raw = a < kMaxExperts + 1 ? P->active[a] : E;
+  const bool in_list = a < kMaxExperts + 1;
+  const int g_raw = in_list ? P->active[a] : E;
+  const int rows_raw = in_list ? P->act_rows[a] : 0;
+  const int off_raw = in_list ? P->act_off[a] : 0;
+  const uint64_t addr = in_list ? P->act_rec[a] : 0ull;
+  const int na = min(na_raw, kMaxExperts + 1);
   const int g = g_raw < 0 ? 0 : (g_raw > E ? E : g_raw);
   const bool shared = g == E;
   const bool live = a < na;
-  const int rows = live ? P->counts[g] : 0;
-  const int offset = (live && !shared) ? P->offsets[g] : 0;
-  const uint64_t addr = (live && !shared) ? t.g.expert_records[g] : 0;
   if (a <= na) pc->item_start[a] = start;
   if (a == na) pc->total = start;
   if (live) {
     pc->group[a] = g;
-    pc->rows[a] = rows;
-    pc->offset[a] = offset;
+    pc->rows[a] = rows_raw;
+    pc->offset[a] = shared ? 0 : off_raw;
     int slot = 0;
     if (!shared) {
       const uint64_t base = (uint64_t)t.arena;
@@ -376,30 +386,17 @@ __device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) 
   }
   if (a == 0) {
     pc->num_active = na;
-    pc->nk = P->nk;
+    pc->nk = nk;
   }
 }
 
-// Locate work item `item`: the group (binary search over the item prefix),
-// its token tile and output-unit tile, and the item's k-blocks of KBLK K
-// elements (the shared expert's down tiles in `t.shared_parts` K parts).
-// UNITS = output units per item. Returns false past the last item.
+// Item `local` of a group with `rows` tokens (shared: the shared expert):
+// its token tile and output-unit tile, and its k-blocks of KBLK K elements
+// (the shared expert's down tiles in `t.shared_parts` K parts). Depends on
+// the launch's sizes only, not on the plan.
 template <int MODE, int KBLK, int UNITS, int TT>
-__device__ __forceinline__ bool tc_item_at(const TcArgs& t, const TcPlanCache* pc, int item, TcItem& it) {
-  const int na = pc->num_active;
-  if (item >= pc->total || na <= 0) return false;
-  int lo = 0, hi = na - 1;  // largest a with item_start[a] <= item
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (pc->item_start[mid] <= item)
-      lo = mid;
-    else
-      hi = mid - 1;
-  }
-  const int local = item - pc->item_start[lo];
-  const int g = pc->group[lo];
-  it.g = g;
-  it.shared = (g == t.g.E);
+__device__ __forceinline__ void tc_item_local(const TcArgs& t, bool shared, int rows, int local, TcItem& it) {
+  it.shared = shared;
   const int inter = it.shared ? t.g.Is : t.g.I;
   it.units = MODE == 0 ? inter : t.g.H;
   const int K = MODE == 0 ? t.g.H : inter;
@@ -420,8 +417,37 @@ __device__ __forceinline__ bool tc_item_at(const TcArgs& t, const TcPlanCache* p
   }
   it.tok0 = (tile / ntiles) * TT;
   it.unit0 = (tile % ntiles) * UNITS;
-  it.nvalid = min(TT, pc->rows[lo] - it.tok0);
+  it.nvalid = min(TT, rows - it.tok0);
   it.npad = (it.nvalid + 15) & ~15;
+}
+
+// Work items of the shared expert (the first group of every schedule when it
+// runs), from the launch's sizes; the same count as the plan's scan.
+template <int MODE, int UNITS, int TT>
+__device__ __forceinline__ int tc_shared_items(const TcArgs& t) {
+  const int units = MODE == 0 ? t.g.Is : t.g.H;
+  const int parts = (MODE == 1 && t.shared_parts > 1) ? t.shared_parts : 1;
+  return ((t.g.n + TT - 1) / TT) * ((units + UNITS - 1) / UNITS) * parts;
+}
+
+// Locate work item `item`: the group (binary search over the item prefix),
+// then tc_item_local. UNITS = output units per item. Returns false past the
+// last item.
+template <int MODE, int KBLK, int UNITS, int TT>
+__device__ __forceinline__ bool tc_item_at(const TcArgs& t, const TcPlanCache* pc, int item, TcItem& it) {
+  const int na = pc->num_active;
+  if (item >= pc->total || na <= 0) return false;
+  int lo = 0, hi = na - 1;  // largest a with item_start[a] <= item
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pc->item_start[mid] <= item)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  const int g = pc->group[lo];
+  it.g = g;
+  tc_item_local<MODE, KBLK, UNITS, TT>(t, g == t.g.E, pc->rows[lo], item - pc->item_start[lo], it);
   if (MODE == 0)
     it.brow0 = (it.shared ? pc->nk : pc->offset[lo]) + it.tok0;
   else

@@ -143,6 +143,34 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
   }
   if (warp == kGTmaWarp && lane == 0) prefetch_maps(maps, t.maps_used);
   if constexpr (TT == 16) chain_trigger();  // decode tiles: the next kernel may launch and wait meanwhile
+  const int first_item = blockIdx.x, item_stride = gridDim.x;
+  // decode tiles: a CTA whose first item is one of the int8 shared expert's
+  // (first in both schedules, laid out from the launch's sizes) loads that
+  // item's first weight stages before waiting for the routing, as in
+  // tc_expert_gemm_kernel; the producer adds the activation bytes and
+  // arrives once the plan is read, and checks that the plan agrees
+  int pre_n = 0, pre_unit0 = 0, pre_kb0 = 0;
+  if constexpr (TT == 16) {
+    __syncthreads();  // the barriers are initialised
+    if (warp == kGTmaWarp && t.pre_shared && first_item < tc_shared_items<MODE, Geo::kUnits, TT>(t)) {
+      TcItem p;
+      tc_item_local<MODE, 128, Geo::kUnits, TT>(t, true, t.g.n, first_item, p);
+      pre_n = min(p.nkb, S);
+      pre_unit0 = p.unit0;
+      pre_kb0 = p.kb0;
+      if (lane == 0) {
+#pragma unroll 1
+        for (int kb = 0; kb < pre_n; ++kb) {
+          uint8_t* sa = smem + (size_t)kb * Geo::kStageBytes;
+          const int x = (p.kb0 + kb) * 128;
+          mbar_expect_tx_only(&full[kb], Geo::kABytes);
+          tma_load_2d(sa, &maps.a_shared[0], &full[kb], x, p.unit0);
+          if (MODE == 0) tma_load_2d(sa + 8192, &maps.a_shared[1], &full[kb], x, p.unit0);
+        }
+      }
+      __syncwarp();
+    }
+  }
   chain_wait();
   tc_cache_plan(t, pc);
   if (warp == kGMmaWarp) tmem_alloc<1>(tmem_slot, 512);
@@ -151,13 +179,30 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total = pc->total;
-  const int first_item = blockIdx.x, item_stride = gridDim.x;
   const unsigned long long wait_ns = t.wait_ns;
 
   if (warp == kGTmaWarp) {
     // ---------------- TMA producer ----------------
     uint32_t kc = 0, zi = 0;  // k-blocks issued; items with zero points issued
     bool ok = true;
+    if (pre_n > 0) {
+      // the plan must place the item whose weights are in flight first; if
+      // not (an inconsistent tally leaves no items), report it, let the
+      // copies land (the arrivals complete the phases) and stop
+      TcItem it0;
+      const bool same = tc_item_at<MODE, 128, Geo::kUnits, TT>(t, pc, first_item, it0) && it0.valid &&
+                        it0.shared && it0.unit0 == pre_unit0 && it0.kb0 == pre_kb0 && it0.nkb >= pre_n;
+      if (!same) {
+        ok = false;
+        if (lane == 0) {
+          atomicOr(&t.plan_rw->error, 8);
+          *abort_flag = 1;
+          for (int s = 0; s < pre_n; ++s) mbar_arrive(&full[s]);
+          for (int s = 0; s < pre_n; ++s) mbar_drain(&full[s], 0, 100000000ull);
+        }
+        __syncwarp();
+      }
+    }
     for (int item = first_item; ok && item < total; item += item_stride) {
       TcItem it;
       if (!tc_item_at<MODE, 128, Geo::kUnits, TT>(t, pc, item, it)) break;
@@ -183,7 +228,9 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
           uint8_t* sb = st + Geo::kABytes;
           uint8_t* sp = sb + Geo::kBBytes;
           const int x = (it.kb0 + kb) * 128;  // first K element of the block
-          if (it.shared) {
+          if (kc < (uint32_t)pre_n) {
+            mbar_expect_tx(&full[s], Geo::kBBytes);  // weights loaded before the plan was read
+          } else if (it.shared) {
             mbar_expect_tx(&full[s], Geo::kABytes + Geo::kBBytes);
             if (MODE == 0) {
               tma_load_2d(sa, &maps.a_shared[0], &full[s], x, it.unit0);
@@ -693,6 +740,7 @@ int launch_tcg_grouped(const TcLaunch& L, cudaStream_t st) {
   t.plan_rw = const_cast<Plan*>(a.plan);
   t.wait_ns = L.wait_ns ? L.wait_ns : kDefaultWaitNs;
   t.stall_last = 0;
+  t.pre_shared = TT == 16 && L.has_shared && L.n > 0 && a.shared_record != nullptr;
   t.maps_used = maps_used_bits(maps);
   if (L.mode == 0)
     return TT == 16 ? launch_tcg_mode<0, 16>(maps, t, L.items_bound, st) : launch_tcg_mode<0, 64>(maps, t, L.items_bound, st);
