@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       pre_unit0 = p.unit0;
       pre_kb0 = p.kb0;
       if (lane == 0) {
+        const uint64_t pol = l2_evict_first();
 #pragma unroll 1
         for (int kb = 0; kb < pre_n; ++kb) {
           uint8_t* st = smem + kb * Geo::kStageBytes;
@@ -240,8 +241,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           for (int c = 0; c < Geo::kKC; ++c) {
             const int x = ((p.kb0 + kb) * Geo::kKC + c) * 128;
             uint8_t* sa = st + c * Geo::kAChunkBytes;
-            tma_2d<CG>(sa, &maps.a_shared[0], &full[kb], 0u, x, p.unit0);
-            if (MODE == 0) tma_2d<CG>(sa + 8192, &maps.a_shared[1], &full[kb], 0u, x, p.unit0);
+            tma_w2d<CG>(sa, &maps.a_shared[0], &full[kb], 0u, x, p.unit0, pol);
+            if (MODE == 0) tma_w2d<CG>(sa + 8192, &maps.a_shared[1], &full[kb], 0u, x, p.unit0, pol);
           }
         }
       }
@@ -268,6 +269,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
 
   if (warp == kTcTmaWarp) {
     // ---------------- TMA producer (lane 0 issues; the warp moves in step) ----------------
+    // decode streams each weight byte once: evict-first, so the L2 keeps the
+    // small kernels' code and data between replays
+    const uint64_t wpol = TT == 16 ? l2_evict_first() : 0ull;
     uint32_t kc = 0;  // k-blocks issued so far
     bool ok = true;
     if (pre_n > 0) {
@@ -321,17 +325,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
             if (pre) {
             } else if (MODE == 0) {
               if (it.shared) {
-                tma_2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow);
-                tma_2d<CG>(sa + 8192, &maps.a_shared[1], &full[s], fc, x, arow);
+                tma_w2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow, wpol);
+                tma_w2d<CG>(sa + 8192, &maps.a_shared[1], &full[s], fc, x, arow, wpol);
               } else {
-                tma_3d<CG>(sa, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
-                tma_3d<CG>(sa + 8192, &maps.a_routed[1], &full[s], fc, x, arow, it.slot);
+                tma_w3d<CG>(sa, &maps.a_routed[0], &full[s], fc, x, arow, it.slot, wpol);
+                tma_w3d<CG>(sa + 8192, &maps.a_routed[1], &full[s], fc, x, arow, it.slot, wpol);
               }
             } else {
               if (it.shared)
-                tma_2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow);
+                tma_w2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow, wpol);
               else
-                tma_3d<CG>(sa, &maps.a_routed[0], &full[s], fc, x, arow, it.slot);
+                tma_w3d<CG>(sa, &maps.a_routed[0], &full[s], fc, x, arow, it.slot, wpol);
             }
             if (CG == 1) {
               tma_2d<CG>(sb, &b[0], &full[s], fc, x, it.brow0);

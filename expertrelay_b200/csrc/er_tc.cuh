@@ -146,6 +146,54 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m
       "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// L2 policy for streamed weights (decode): evicted first, so the small
+// kernels' code and data stay in L2 across the weight stream
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_2d_ef(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                               uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], "
+      "[%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_ef(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                               uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4, "
+      "%5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(pol)
+      : "memory");
+}
+// weight tiles: with the evict-first policy on single SMs when `pol` is nonzero
+template <int CG>
+__device__ __forceinline__ void tma_w2d(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int x, int y,
+                                        uint64_t pol) {
+  if constexpr (CG == 1) {
+    if (pol)
+      tma_load_2d_ef(dst, map, bar, x, y, pol);
+    else
+      tma_load_2d(dst, map, bar, x, y);
+  } else {
+    tma_load_2d_pair(dst, map, bar_c, x, y);
+  }
+}
+template <int CG>
+__device__ __forceinline__ void tma_w3d(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int x, int y,
+                                        int z, uint64_t pol) {
+  if constexpr (CG == 1) {
+    if (pol)
+      tma_load_3d_ef(dst, map, bar, x, y, z, pol);
+    else
+      tma_load_3d(dst, map, bar, x, y, z);
+  } else {
+    tma_load_3d_pair(dst, map, bar_c, x, y, z);
+  }
+}
 template <int CG>
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int x, int y) {
   if constexpr (CG == 1)

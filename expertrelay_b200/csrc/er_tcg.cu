@@ -159,13 +159,14 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
       pre_unit0 = p.unit0;
       pre_kb0 = p.kb0;
       if (lane == 0) {
+        const uint64_t pol = l2_evict_first();
 #pragma unroll 1
         for (int kb = 0; kb < pre_n; ++kb) {
           uint8_t* sa = smem + (size_t)kb * Geo::kStageBytes;
           const int x = (p.kb0 + kb) * 128;
           mbar_expect_tx_only(&full[kb], Geo::kABytes);
-          tma_load_2d(sa, &maps.a_shared[0], &full[kb], x, p.unit0);
-          if (MODE == 0) tma_load_2d(sa + 8192, &maps.a_shared[1], &full[kb], x, p.unit0);
+          tma_w2d<1>(sa, &maps.a_shared[0], &full[kb], 0u, x, p.unit0, pol);
+          if (MODE == 0) tma_w2d<1>(sa + 8192, &maps.a_shared[1], &full[kb], 0u, x, p.unit0, pol);
         }
       }
       __syncwarp();
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
 
   if (warp == kGTmaWarp) {
     // ---------------- TMA producer ----------------
+    const uint64_t wpol = TT == 16 ? l2_evict_first() : 0ull;  // decode: weights streamed once, evicted first
     uint32_t kc = 0, zi = 0;  // k-blocks issued; items with zero points issued
     bool ok = true;
     if (pre_n > 0) {
@@ -233,10 +235,10 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
           } else if (it.shared) {
             mbar_expect_tx(&full[s], Geo::kABytes + Geo::kBBytes);
             if (MODE == 0) {
-              tma_load_2d(sa, &maps.a_shared[0], &full[s], x, it.unit0);
-              tma_load_2d(sa + 8192, &maps.a_shared[1], &full[s], x, it.unit0);
+              tma_w2d<1>(sa, &maps.a_shared[0], &full[s], 0u, x, it.unit0, wpol);
+              tma_w2d<1>(sa + 8192, &maps.a_shared[1], &full[s], 0u, x, it.unit0, wpol);
             } else {
-              tma_load_2d(sa, &maps.a_shared[0], &full[s], x, it.unit0);
+              tma_w2d<1>(sa, &maps.a_shared[0], &full[s], 0u, x, it.unit0, wpol);
             }
           } else {
             // packed nibbles: 64 bytes per row per k-block, x / 2 a multiple of 64
@@ -248,14 +250,14 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
             mbar_expect_tx(&full[s], Geo::kPackBytes + Geo::kBBytes + zbytes);
             const uint8_t* rec = t.arena + (size_t)it.slot * t.record_bytes;
             if (MODE == 0) {
-              tma_load_3d(sp, &maps.a_routed[0], &full[s], x / 2, it.unit0, it.slot);
-              tma_load_3d(sp + 4096, &maps.a_routed[1], &full[s], x / 2, it.unit0, it.slot);
+              tma_w3d<1>(sp, &maps.a_routed[0], &full[s], 0u, x / 2, it.unit0, it.slot, wpol);
+              tma_w3d<1>(sp + 4096, &maps.a_routed[1], &full[s], 0u, x / 2, it.unit0, it.slot, wpol);
               if (zbytes) {  // gate rows' zero points to buffer rows 0..63, up rows' to 64..127
                 bulk_load(zdst, rec + rg.zero_offset(0) + (size_t)it.unit0 * gpr, nr * gpr, &full[s]);
                 bulk_load(zdst + 64 * gpr, rec + rg.zero_offset(1) + (size_t)it.unit0 * gpr, nr * gpr, &full[s]);
               }
             } else {
-              tma_load_3d(sp, &maps.a_routed[0], &full[s], x / 2, it.unit0, it.slot);
+              tma_w3d<1>(sp, &maps.a_routed[0], &full[s], 0u, x / 2, it.unit0, it.slot, wpol);
               if (zbytes) bulk_load(zdst, rec + rg.zero_offset(2) + (size_t)it.unit0 * gpr, nr * gpr, &full[s]);
             }
           }
