@@ -30,12 +30,12 @@ __device__ __forceinline__ void warp_select(const float (&v)[kPer], int E, int k
   s = warp_sum(s);
 
   uint32_t taken = 0;  // bit j: entry lane + 32 j already selected
-  int sel[kMaxTopK];
-  float pw[kMaxTopK];
-  float wsum = 0.f;
-#pragma unroll
-  for (int r = 0; r < kMaxTopK; ++r) {  // unrolled so that sel / pw stay in registers
-    if (r >= k) break;
+  // lane r < k keeps slot r's expert and probability; the rounds are not
+  // unrolled (the dispatch kernel of decode batches runs this code cold)
+  int my_sel = 0;
+  float my_p = 0.f, wsum = 0.f;
+#pragma unroll 1
+  for (int r = 0; r < k; ++r) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
@@ -70,23 +70,18 @@ __device__ __forceinline__ void warp_select(const float (&v)[kPer], int E, int k
         }
     }
     p = __shfl_sync(0xffffffffu, p, owner);
-    sel[r] = bi;
-    pw[r] = p;
+    if (lane == r) {
+      my_sel = bi;
+      my_p = p;
+    }
     wsum += p;
   }
-  if (tally)  // lane r counts slot r's expert
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r)
-      if (r < k && lane == r) atomicAdd(&tally[sel[r]], 1);
-  if (lane == 0) {
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
-      if (r >= k) break;
-      const float w = norm ? pw[r] / wsum : pw[r];
-      if (idx64) idx64[(size_t)t * k + r] = sel[r];
-      if (idx32) idx32[(size_t)t * k + r] = sel[r];
-      if (wout) wout[(size_t)t * k + r] = w;
-    }
+  if (lane < k) {
+    if (tally) atomicAdd(&tally[my_sel], 1);
+    const float w = norm ? my_p / wsum : my_p;
+    if (idx64) idx64[(size_t)t * k + lane] = my_sel;
+    if (idx32) idx32[(size_t)t * k + lane] = my_sel;
+    if (wout) wout[(size_t)t * k + lane] = w;
   }
 }
 
