@@ -44,6 +44,16 @@ __device__ __forceinline__ int cta_excl_scan(int v, int* tmp, int* total) {
   return base + incl - v;
 }
 
+// The record addresses thread `tid` hands plan_scan (experts 2 tid, 2 tid + 1;
+// zero unless this CTA writes the plan), loaded at a kernel's start so their
+// latency hides behind its other work.
+__device__ __forceinline__ void plan_records(const uint64_t* records, bool write_plan, int E, uint64_t& r0,
+                                             uint64_t& r1) {
+  const int e = 2 * (int)threadIdx.x;
+  r0 = (write_plan && records && e < E) ? records[e] : 0ull;
+  r1 = (write_plan && records && e + 1 < E) ? records[e + 1] : 0ull;
+}
+
 // The plan from the per-expert tallies, by the whole CTA (at least 256
 // threads; thread i owns entries 2i, 2i+1 of the per-expert and per-group
 // lists, enough for E + 2 <= 258). Every caller gets the expert ranges' first
@@ -52,16 +62,17 @@ __device__ __forceinline__ int cta_excl_scan(int v, int* tmp, int* total) {
 // schedules for the expert kernels. Ends with a __syncthreads.
 __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, int I, int Is, SchedSpec s0,
                           SchedSpec s1, int shared, bool write_plan, int* hist, int* offs, int* act, int* bad_out,
-                          int* tmp, const int* tally = nullptr, const uint64_t* records = nullptr) {
+                          int* tmp, const int* tally = nullptr, uint64_t rec0 = 0ull, uint64_t rec1 = 0ull) {
   const int tid = threadIdx.x;
   const int nk = n * k;
   int cnt[2], on[2];
-  uint64_t rec[2];  // the experts' record addresses, copied into the plan by active position
+  // rec0 / rec1: the record addresses of experts 2 tid and 2 tid + 1 (loaded
+  // by the caller early, see plan_records), copied into the plan by active position
+  const uint64_t rec[2] = {rec0, rec1};
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int e = 2 * tid + j;
     cnt[j] = e < E ? (tally ? tally[e] : __ldcg(&plan->tally[e])) : 0;  // plan->tally: counted at L2 by atomics
-    rec[j] = (write_plan && records && e < E) ? records[e] : 0ull;
     on[j] = cnt[j] > 0;
     if (e < E) hist[e] = cnt[j];
   }
@@ -177,6 +188,8 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
   __shared__ int cbase[kMaxExperts];   // their first position in the expert's range
   for (int x = threadIdx.x; x < E; x += blockDim.x) ccount[x] = 0;  // ordered by plan_scan's barriers
   chain_wait();
+  uint64_t rec0, rec1;
+  plan_records(records, blockIdx.x == 0, E, rec0, rec1);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x * 8 + warp;
   constexpr int kRegVec = 16;  // float4 per lane held in registers: H <= 2048
@@ -199,7 +212,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
     for (int i = 0; i < kRegVec; ++i) slice4(v[i], inv, q0[i], q1[i]);
   }
   plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad, scan_tmp, nullptr,
-            records);
+            rec0, rec1);
   // Positions: each (token, slot) pair takes a rank among this CTA's pairs
   // of the same expert (shared-memory atomics), then one thread per expert
   // claims the CTA's block of the expert's range with one global atomic (a
@@ -312,22 +325,16 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
   const XT* x = SLICE ? h + (size_t)(me < n ? me : 0) * H : h;
   const bool in_regs = H <= 4 * kSmallVec * nthr;
   float4 hv[kSmallVec];
-  if (SLICE && me < n) {
-    float amax = 0.f;
-    if (in_regs) {
+  // issued now, used after the top-k: the row's latency overlaps it
+  if (SLICE && me < n && in_regs) {
 #pragma unroll
-      for (int j = 0; j < kSmallVec; ++j) {
-        const int c = 4 * (threadIdx.x + nthr * j);
-        hv[j] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        amax = fmaxf(amax, abs_max4(hv[j]));
-      }
-    } else {
-      for (int c = 4 * threadIdx.x; c < H; c += 4 * nthr) amax = fmaxf(amax, abs_max4(load4(x + c)));
+    for (int j = 0; j < kSmallVec; ++j) {
+      const int c = 4 * (threadIdx.x + nthr * j);
+      hv[j] = c < H ? load4(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) amax_s[warp] = amax;
   }
+  uint64_t rec0, rec1;
+  plan_records(records, me == 0, E, rec0, rec1);
   for (int e = threadIdx.x; e < E; e += nthr) tally_s[e] = 0;
   __syncthreads();
   if (warp < n) {
@@ -342,9 +349,21 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
     }
     topk_token<KPER>(a, n, E, k, warp, lane);
   }
+  if (SLICE && me < n) {
+    float amax = 0.f;
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < kSmallVec; ++j) amax = fmaxf(amax, abs_max4(hv[j]));
+    } else {
+      for (int c = 4 * threadIdx.x; c < H; c += 4 * nthr) amax = fmaxf(amax, abs_max4(load4(x + c)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) amax_s[warp] = amax;
+  }
   __syncthreads();
-  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, me == 0, hist, offs, act, &bad, scan_tmp, tally_s,
-            records);
+  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, me == 0, hist, offs, act, &bad, scan_tmp, tally_s, rec0,
+            rec1);
   if (me >= n || bad) return;  // uniform over the CTA
   const int nk = n * k;
   if (warp == 0 && lane < k) {
@@ -430,9 +449,9 @@ int launch_tally(const int32_t* ids, int m, int E, int* tally, int nclear, cudaS
 
 template <typename XT, bool SLICE>
 static int launch_dispatch_t(const XT* h, const int32_t* idx, const float* w, int n, int k, int E, int H, int I, int Is,
-                             const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records, int32_t* perm_token, float* perm_w,
-                             int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk,
-                             cudaStream_t st) {
+                             const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records,
+                             int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1,
+                             float* scale, const TopkArgs* topk, cudaStream_t st) {
   if (topk) {  // a CTA per token (at least one: CTA 0 writes the plan), a warp per token inside each
     const dim3 grid(n > 0 ? n : 1), block(32 * (n > 8 ? 16 : 8));
     if (E <= 64)
@@ -450,8 +469,9 @@ static int launch_dispatch_t(const XT* h, const int32_t* idx, const float* w, in
 }
 
 int launch_dispatch(const void* h, int h_dtype, const int32_t* idx, const float* w, int n, int k, int E, int H, int I,
-                    int Is, const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records, int32_t* perm_token, float* perm_w,
-                    int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale, const TopkArgs* topk, cudaStream_t st) {
+                    int Is, const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records,
+                    int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1, float* scale,
+                    const TopkArgs* topk, cudaStream_t st) {
   if (topk && (n > kFusedTopkMaxTok || topk->idx32 != idx || topk->wout != w || topk->tally != plan->tally))
     return fail(ER_EINVAL, "dispatch: fused top-k needs n <= %d and its outputs as the dispatch inputs",
                 kFusedTopkMaxTok);

@@ -212,20 +212,56 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kTcTmaWarp && lane == 0) prefetch_maps(maps, t.maps_used);
-  // decode tiles: the next kernel (slices or combine, a few small CTAs that
-  // fit beside this one) may launch now and wait in its chain_wait, so it
-  // starts the moment this grid completes
-  if constexpr (TT == 16) chain_trigger();
-  // Decode tiles: the shared expert's items come first in both schedules and
-  // are laid out from the launch's sizes alone, so a CTA whose first item is
-  // one of them loads that item's first weight stages now, while the kernels
-  // before this one (routing, plan) still run. The full barriers get the
-  // weight bytes without an arrival; the producer adds the activation bytes
-  // and arrives once the plan is read, and checks that the plan agrees.
+  // Decode tiles: the next kernel (slices or combine, a few small CTAs that
+  // fit beside this one) may launch early and wait in its chain_wait, so it
+  // starts the moment this grid completes. The down GEMM lets the combine
+  // launch now; the gate/up GEMM lets the slice launch only after its own
+  // wait, i.e. once the dispatch (and with it the plan) is complete, so the
+  // down GEMM launched after the slice reads the plan before its wait.
+  if constexpr (TT == 16 && MODE == 1) chain_trigger();
+  // Decode tiles: a CTA loads its first item's first weight stages before
+  // its wait, while the kernels before it still run. Gate/up: the shared
+  // expert's items come first in both schedules and are laid out from the
+  // launch's sizes alone, so CTAs whose first item is one of them do. Down:
+  // the plan is complete (above), so every CTA reads it first and does. The
+  // full barriers get the weight bytes without an arrival; the producer adds
+  // the activation bytes and arrives after the wait, and checks that the
+  // plan agrees.
   int pre_n = 0, pre_unit0 = 0, pre_kb0 = 0;  // producer: first-item k-blocks whose weights are in flight
+  bool plan_read = false;
   if constexpr (TT == 16) {
     __syncthreads();  // the barriers are initialised
-    if (warp == kTcTmaWarp && t.pre_shared && first_item < tc_shared_items<MODE, Geo::kUnits, TT>(t)) {
+    if constexpr (MODE == 1) {
+      tc_cache_plan<true>(t, pc);
+      __syncthreads();
+      plan_read = true;
+      if (warp == kTcTmaWarp) {
+        TcItem p;
+        if (tc_item<MODE, TT, CG>(t, pc, first_item, p) && p.valid) {
+          pre_n = min(p.nkb, S);
+          pre_unit0 = p.unit0;
+          pre_kb0 = p.kb0;
+          if (lane == 0) {
+            const uint64_t pol = l2_evict_first();
+#pragma unroll 1
+            for (int kb = 0; kb < pre_n; ++kb) {
+              uint8_t* st = smem + kb * Geo::kStageBytes;
+              mbar_expect_tx_only(&full[kb], Geo::kABytes);
+#pragma unroll 1
+              for (int c = 0; c < Geo::kKC; ++c) {
+                const int x = ((p.kb0 + kb) * Geo::kKC + c) * 128;
+                uint8_t* sa = st + c * Geo::kAChunkBytes;
+                if (p.shared)
+                  tma_w2d<CG>(sa, &maps.a_shared[0], &full[kb], 0u, x, p.unit0, pol);
+                else
+                  tma_w3d<CG>(sa, &maps.a_routed[0], &full[kb], 0u, x, p.unit0, p.slot, pol);
+              }
+            }
+          }
+        }
+        __syncwarp();
+      }
+    } else if (warp == kTcTmaWarp && t.pre_shared && first_item < tc_shared_items<MODE, Geo::kUnits, TT>(t)) {
       TcItem p;
       tc_item_local<MODE, 128 * Geo::kKC, Geo::kUnits, TT>(t, true, t.g.n, first_item, p);
       pre_n = min(p.nkb, S);
@@ -249,10 +285,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       __syncwarp();
     }
   }
-  // everything above touched only this CTA's shared memory; the plan and the
-  // operands come from the kernels before this one
+  // everything above touched only this CTA's shared memory (and read the
+  // weights, and on decode down the complete plan); the operands come from
+  // the kernels before this one
   chain_wait();
-  tc_cache_plan(t, pc);
+  if constexpr (TT == 16 && MODE == 0) chain_trigger();
+  if (!plan_read) tc_cache_plan(t, pc);
   if constexpr (CG == 2) {
     // the peer's loads and arrivals target CTA 0's barriers: both CTAs'
     // barriers are initialised, and both CTAs running, before either goes on
@@ -279,8 +317,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       // not (an inconsistent tally leaves no items), report it, let the
       // copies land (the arrivals complete the phases) and stop
       TcItem it0;
-      const bool same = tc_item<MODE, TT, CG>(t, pc, first_item, it0) && it0.valid && it0.shared &&
-                        it0.unit0 == pre_unit0 && it0.kb0 == pre_kb0 && it0.nkb >= pre_n;
+      const bool same = tc_item<MODE, TT, CG>(t, pc, first_item, it0) && it0.valid &&
+                        (MODE == 1 || it0.shared) && it0.unit0 == pre_unit0 && it0.kb0 == pre_kb0 &&
+                        it0.nkb >= pre_n;
       if (!same) {
         ok = false;
         if (lane == 0) {

@@ -400,19 +400,22 @@ struct TcItem {
 // any lookup). One round of loads: every entry that can be active is read
 // together with num_active (the dispatch wrote each active group's rows,
 // range and record by active position; entries past num_active are read and
-// dropped). Group ids are clamped to 0..E.
+// dropped). Group ids are clamped to 0..E. L2: loads that bypass L1 (for a
+// kernel that reads the plan before its griddepcontrol.wait).
+template <bool L2 = false>
 __device__ __forceinline__ void tc_cache_plan(const TcArgs& t, TcPlanCache* pc) {
   const Plan* P = t.g.plan;
   const int E = t.g.E;
   const int a = threadIdx.x;
-  const int na_raw = P->num_active;
-  const int nk = P->nk;
-  const int start = a < kMaxExperts + 2 ? P->item_start[t.sched][a] : 0;
+  auto ld = [](const int* q) { return L2 ? __ldcg(q) : *q; };
+  const int na_raw = ld(&P->num_active);
+  const int nk = ld(&P->nk);
+  const int start = a < kMaxExperts + 2 ? ld(&P->item_start[t.sched][a]) : 0;
   const bool in_list = a < kMaxExperts + 1;
-  const int g_raw = in_list ? P->active[a] : E;
-  const int rows_raw = in_list ? P->act_rows[a] : 0;
-  const int off_raw = in_list ? P->act_off[a] : 0;
-  const uint64_t addr = in_list ? P->act_rec[a] : 0ull;
+  const int g_raw = in_list ? ld(&P->active[a]) : E;
+  const int rows_raw = in_list ? ld(&P->act_rows[a]) : 0;
+  const int off_raw = in_list ? ld(&P->act_off[a]) : 0;
+  const uint64_t addr = in_list ? (L2 ? __ldcg(&P->act_rec[a]) : P->act_rec[a]) : 0ull;
   const int na = min(na_raw, kMaxExperts + 1);
   const int g = g_raw < 0 ? 0 : (g_raw > E ? E : g_raw);
   const bool shared = g == E;
