@@ -227,7 +227,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
   // full barriers get the weight bytes without an arrival; the producer adds
   // the activation bytes and arrives after the wait, and checks that the
   // plan agrees.
-  int pre_n = 0, pre_unit0 = 0, pre_kb0 = 0;  // producer: first-item k-blocks whose weights are in flight
+  // producer: first-item k-blocks whose weights are in flight, and where
+  // their activation rows start (down: the row; gate/up: the token tile)
+  int pre_n = 0, pre_kb0 = 0, pre_row = 0, pre_sh = 1;
   bool plan_read = false;
   if constexpr (TT == 16) {
     __syncthreads();  // the barriers are initialised
@@ -239,8 +241,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
         TcItem p;
         if (tc_item<MODE, TT, CG>(t, pc, first_item, p) && p.valid) {
           pre_n = min(p.nkb, S);
-          pre_unit0 = p.unit0;
           pre_kb0 = p.kb0;
+          pre_row = p.brow0;
+          pre_sh = p.shared;
           if (lane == 0) {
             const uint64_t pol = l2_evict_first();
 #pragma unroll 1
@@ -265,8 +268,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       TcItem p;
       tc_item_local<MODE, 128 * Geo::kKC, Geo::kUnits, TT>(t, true, t.g.n, first_item, p);
       pre_n = min(p.nkb, S);
-      pre_unit0 = p.unit0;
       pre_kb0 = p.kb0;
+      pre_row = p.tok0;
       if (lane == 0) {
         const uint64_t pol = l2_evict_first();
 #pragma unroll 1
@@ -312,14 +315,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
     const uint64_t wpol = TT == 16 ? l2_evict_first() : 0ull;
     uint32_t kc = 0;  // k-blocks issued so far
     bool ok = true;
+    int skip = 0;  // k-blocks of the first item issued here, before the loop
     if (pre_n > 0) {
-      // the plan must place the item whose weights are in flight first; if
-      // not (an inconsistent tally leaves no items), report it, let the
-      // copies land (the arrivals complete the phases) and stop
-      TcItem it0;
-      const bool same = tc_item<MODE, TT, CG>(t, pc, first_item, it0) && it0.valid &&
-                        (MODE == 1 || it0.shared) && it0.unit0 == pre_unit0 && it0.kb0 == pre_kb0 &&
-                        it0.nkb >= pre_n;
+      // gate/up: the plan must make the shared expert the first group with
+      // this CTA's first item among its items (the geometry then follows
+      // from the launch's sizes, as above); if not (an inconsistent tally
+      // leaves no items), report it, let the copies land (the arrivals
+      // complete the phases) and stop. Down read the plan before issuing.
+      bool same = true;
+      if constexpr (MODE == 0)
+        same = pc->num_active > 0 && pc->group[0] == t.g.E && first_item < pc->item_start[1] &&
+               pc->rows[0] == t.g.n;
       if (!same) {
         ok = false;
         if (lane == 0) {
@@ -329,6 +335,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           for (int s = 0; s < pre_n; ++s) mbar_drain(&full[s], 0, 100000000ull);
         }
         __syncwarp();
+      } else {
+        // the activation tiles of the stages in flight, straight after the
+        // wait (this code runs once per launch, from a cold cache: short)
+        const int brow0 = MODE == 0 ? pc->nk + pre_row : pre_row;
+        const CUtensorMap* b = (MODE == 1 && pre_sh) ? maps.b_shared : maps.b_routed;
+        if (lane == 0) {
+#pragma unroll 1
+          for (int kb = 0; kb < pre_n; ++kb) {
+            uint8_t* sb = smem + kb * Geo::kStageBytes + Geo::kABytes;
+            mbar_expect_tx(&full[kb], Geo::kTxBytes - Geo::kABytes);
+#pragma unroll 1
+            for (int c = 0; c < Geo::kKC; ++c) {
+              const int x = ((pre_kb0 + kb) * Geo::kKC + c) * 128;
+              tma_2d<CG>(sb + c * Geo::kBChunkBytes, &b[0], &full[kb], 0u, x, brow0);
+              tma_2d<CG>(sb + c * Geo::kBChunkBytes + Geo::kBSliceBytes, &b[1], &full[kb], 0u, x, brow0);
+            }
+          }
+        }
+        __syncwarp();
+        skip = pre_n;
+        kc = pre_n;
       }
     }
     for (int item = first_item; ok && item < total; item += item_stride) {
@@ -336,7 +363,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
       if (!tc_item<MODE, TT, CG>(t, pc, item, it)) break;
       if (!it.valid) continue;
       const int arow = it.unit0 + (int)rank * Geo::kCtaUnits;  // this CTA's first weight row
-      for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
+      for (int kb = item == first_item ? skip : 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
         bool w = true;
@@ -350,9 +377,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
           // CTA 0 expects the whole pair's bytes; the peer's copies may land
           // before that (the barrier's transaction count goes negative until
           // then, and the phase cannot complete without CTA 0's arrival)
-          // a stage whose weights were loaded before the plan still expects its activations
-          const bool pre = kc < (uint32_t)pre_n;
-          if (leader) mbar_expect_tx(&full[s], pre ? Geo::kTxBytes - Geo::kABytes : Geo::kTxBytes);
+          if (leader) mbar_expect_tx(&full[s], Geo::kTxBytes);
           const uint32_t fc = CG == 2 ? mapa_shared(smem_u32(&full[s]), 0) : 0u;
           const CUtensorMap* b = (MODE == 1 && it.shared) ? maps.b_shared : maps.b_routed;
 #pragma unroll(TT == 16 ? 1 : Geo::kKC)
@@ -361,8 +386,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_gemm_kernel(const __g
             const int x = ((it.kb0 + kb) * Geo::kKC + c) * 128;
             uint8_t* sa = st + c * Geo::kAChunkBytes;
             uint8_t* sb = st + Geo::kABytes + c * Geo::kBChunkBytes;
-            if (pre) {
-            } else if (MODE == 0) {
+            if (MODE == 0) {
               if (it.shared) {
                 tma_w2d<CG>(sa, &maps.a_shared[0], &full[s], fc, x, arow, wpol);
                 tma_w2d<CG>(sa + 8192, &maps.a_shared[1], &full[s], fc, x, arow, wpol);

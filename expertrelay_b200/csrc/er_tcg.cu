@@ -149,15 +149,15 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
   // item's first weight stages before waiting for the routing, as in
   // tc_expert_gemm_kernel; the producer adds the activation bytes and
   // arrives once the plan is read, and checks that the plan agrees
-  int pre_n = 0, pre_unit0 = 0, pre_kb0 = 0;
+  int pre_n = 0, pre_kb0 = 0, pre_tok0 = 0;
   if constexpr (TT == 16) {
     __syncthreads();  // the barriers are initialised
     if (warp == kGTmaWarp && t.pre_shared && first_item < tc_shared_items<MODE, Geo::kUnits, TT>(t)) {
       TcItem p;
       tc_item_local<MODE, 128, Geo::kUnits, TT>(t, true, t.g.n, first_item, p);
       pre_n = min(p.nkb, S);
-      pre_unit0 = p.unit0;
       pre_kb0 = p.kb0;
+      pre_tok0 = p.tok0;
       if (lane == 0) {
         const uint64_t pol = l2_evict_first();
 #pragma unroll 1
@@ -187,13 +187,15 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
     const uint64_t wpol = TT == 16 ? l2_evict_first() : 0ull;  // decode: weights streamed once, evicted first
     uint32_t kc = 0, zi = 0;  // k-blocks issued; items with zero points issued
     bool ok = true;
+    int skip = 0;  // k-blocks of the first item issued here, before the loop
     if (pre_n > 0) {
-      // the plan must place the item whose weights are in flight first; if
-      // not (an inconsistent tally leaves no items), report it, let the
-      // copies land (the arrivals complete the phases) and stop
-      TcItem it0;
-      const bool same = tc_item_at<MODE, 128, Geo::kUnits, TT>(t, pc, first_item, it0) && it0.valid &&
-                        it0.shared && it0.unit0 == pre_unit0 && it0.kb0 == pre_kb0 && it0.nkb >= pre_n;
+      // the plan must make the shared expert the first group with this CTA's
+      // first item among its items (the geometry then follows from the
+      // launch's sizes); if not (an inconsistent tally leaves no items),
+      // report it, let the copies land (the arrivals complete the phases)
+      // and stop
+      const bool same = pc->num_active > 0 && pc->group[0] == t.g.E && first_item < pc->item_start[1] &&
+                        pc->rows[0] == t.g.n;
       if (!same) {
         ok = false;
         if (lane == 0) {
@@ -203,6 +205,24 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
           for (int s = 0; s < pre_n; ++s) mbar_drain(&full[s], 0, 100000000ull);
         }
         __syncwarp();
+      } else {
+        // the activation tiles of the stages in flight, straight after the
+        // wait (this code runs once per launch, from a cold cache: short)
+        const int brow0 = (MODE == 0 ? pc->nk : 0) + pre_tok0;
+        const CUtensorMap* b = MODE == 1 ? maps.b_shared : maps.b_routed;
+        if (lane == 0) {
+#pragma unroll 1
+          for (int kb = 0; kb < pre_n; ++kb) {
+            uint8_t* sb = smem + (size_t)kb * Geo::kStageBytes + Geo::kABytes;
+            const int x = (pre_kb0 + kb) * 128;
+            mbar_expect_tx(&full[kb], Geo::kBBytes);
+            tma_load_2d(sb, &b[0], &full[kb], x, brow0);
+            tma_load_2d(sb + Geo::kBSliceBytes, &b[1], &full[kb], x, brow0);
+          }
+        }
+        __syncwarp();
+        skip = pre_n;
+        kc = pre_n;
       }
     }
     for (int item = first_item; ok && item < total; item += item_stride) {
@@ -215,7 +235,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
       const bool zp = !it.shared && t.g.fmt == ER_FMT_INT4_ZP;
       uint8_t* zdst = zbuf + (zi & 1) * Geo::kZeroBytes;
       if (zp && !warp_wait(&zempty[zi & 1], ((zi >> 1) & 1) ^ 1, abort_flag, lane, wait_ns)) break;
-      for (int kb = 0; kb < it.nkb; ++kb, ++kc) {
+      for (int kb = item == first_item ? skip : 0; kb < it.nkb; ++kb, ++kc) {
         const int s = kc % S;
         const uint32_t ph = (kc / S) & 1;
         bool w = true;
@@ -230,9 +250,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
           uint8_t* sb = st + Geo::kABytes;
           uint8_t* sp = sb + Geo::kBBytes;
           const int x = (it.kb0 + kb) * 128;  // first K element of the block
-          if (kc < (uint32_t)pre_n) {
-            mbar_expect_tx(&full[s], Geo::kBBytes);  // weights loaded before the plan was read
-          } else if (it.shared) {
+          if (it.shared) {
             mbar_expect_tx(&full[s], Geo::kABytes + Geo::kBBytes);
             if (MODE == 0) {
               tma_w2d<1>(sa, &maps.a_shared[0], &full[s], 0u, x, it.unit0, wpol);
