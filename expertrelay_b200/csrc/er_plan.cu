@@ -288,7 +288,8 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
 
 // Small batches (n <= kFusedTopkMaxTok), top-k fused: CTA c of n owns token
 // c. Every CTA runs the softmax + top-k of all n tokens (a warp each) into
-// shared memory and derives the plan from those tallies (CTA 0 writes it, the
+// shared memory and derives the plan from those tallies (an extra CTA n
+// writes it, so the plan's writes and the row slicing run side by side; the
 // top-k outputs of token c are written by CTA c), so the positions need no
 // atomics: slot j of token t goes to its expert's range start plus the
 // number of earlier (token, slot) pairs of the same expert. The whole CTA
@@ -321,7 +322,7 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
   chain_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nthr = blockDim.x;
-  const int me = blockIdx.x;  // this CTA's token
+  const int me = blockIdx.x;  // this CTA's token; CTA n has none and writes the plan
   const XT* x = SLICE ? h + (size_t)(me < n ? me : 0) * H : h;
   const bool in_regs = H <= 4 * kSmallVec * nthr;
   float4 hv[kSmallVec];
@@ -334,7 +335,7 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
     }
   }
   uint64_t rec0, rec1;
-  plan_records(records, me == 0, E, rec0, rec1);
+  plan_records(records, me == n, E, rec0, rec1);
   for (int e = threadIdx.x; e < E; e += nthr) tally_s[e] = 0;
   __syncthreads();
   if (warp < n) {
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(512) dispatch_small_kernel(const XT* __restric
     if (lane == 0) amax_s[warp] = amax;
   }
   __syncthreads();
-  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, me == 0, hist, offs, act, &bad, scan_tmp, tally_s, rec0,
+  plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, me == n, hist, offs, act, &bad, scan_tmp, tally_s, rec0,
             rec1);
   if (me >= n || bad) return;  // uniform over the CTA
   const int nk = n * k;
@@ -452,8 +453,8 @@ static int launch_dispatch_t(const XT* h, const int32_t* idx, const float* w, in
                              const SchedSpec* specs, int shared, Plan* plan, const uint64_t* records,
                              int32_t* perm_token, float* perm_w, int32_t* pos_of, int8_t* s0, int8_t* s1,
                              float* scale, const TopkArgs* topk, cudaStream_t st) {
-  if (topk) {  // a CTA per token (at least one: CTA 0 writes the plan), a warp per token inside each
-    const dim3 grid(n > 0 ? n : 1), block(32 * (n > 8 ? 16 : 8));
+  if (topk) {  // a CTA per token and one more that writes the plan, a warp per token inside each
+    const dim3 grid(n + 1), block(32 * (n > 8 ? 16 : 8));
     if (E <= 64)
       return launch_chained(dispatch_small_kernel<XT, SLICE, 2>, grid, block, 0, st, "dispatch_small_kernel", h, n,
                             k, E, H, I, Is, specs[0], specs[1], shared, plan, records, perm_token, perm_w, pos_of, s0,
