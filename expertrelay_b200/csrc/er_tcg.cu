@@ -36,15 +36,19 @@
 
 namespace er {
 
-// Warp roles: 0..3 transform (one per SM sub-partition), 4 MMA issuer, 5 TMA
-// producer, 6..13 epilogue (warp w reads TMEM lanes 32 * (w % 4) .. +31; two
-// warps per lane quadrant, each every other 16-token chunk).
+// Warp roles: 0..3 transform (one per SM sub-partition), 4..11 epilogue
+// (warp w reads TMEM lanes 32 * (w % 4) .. +31; two warps per lane quadrant,
+// each every other 16-token chunk), 14 MMA issuer and 15 TMA producer; 12
+// and 13 have no role. A warp runs on sub-partition w % 4: the MMA and TMA
+// warps share sub-partitions 2 and 3 with the gate/up epilogue's up-row
+// warps, which only hand values over, not with the gate rows' SiLU math.
 constexpr int kGXfmWarps = 4;
-constexpr int kGMmaWarp = 4;
-constexpr int kGTmaWarp = 5;
-constexpr int kGEpiWarp0 = 6;
+constexpr int kGEpiWarp0 = 4;
 constexpr int kGEpiWarps = 8;
-constexpr int kGThreads = (kGEpiWarp0 + kGEpiWarps) * 32;
+constexpr int kGMmaWarp = 14;
+constexpr int kGTmaWarp = 15;
+constexpr int kGThreads = 16 * 32;
+static_assert(kGEpiWarp0 + kGEpiWarps <= 12 && kGMmaWarp % 4 == 2 && kGTmaWarp % 4 == 3, "warp roles");
 static_assert(kGThreads >= kMaxExperts + 2, "tc_cache_plan reads one plan entry per thread");
 
 template <int MODE, int TT>
@@ -418,7 +422,7 @@ __global__ void __launch_bounds__(kGThreads, 1) tcg_expert_gemm_kernel(const __g
       mbar_drain(drain_bar, 0, 100000000ull);
     }
     __syncwarp();
-  } else if (warp >= kGEpiWarp0) {
+  } else if (warp >= kGEpiWarp0 && warp < kGEpiWarp0 + kGEpiWarps) {
     // ---------------- epilogue ----------------
     // Warp w reads TMEM lanes 32 (w % 4) .. +31 and every other 16-token
     // chunk (half). Mode 0: lanes 0..63 hold gate rows, 64..127 the up rows
