@@ -166,8 +166,9 @@ __device__ void plan_scan(Plan* __restrict__ plan, int n, int k, int E, int H, i
 // expert ranges from the tallies (CTA 0 also writes the plan). Then lane r < k
 // of a token's warp claims the position of slot r (its expert's range start,
 // plus the CTA's block of it, plus the pair's rank inside the CTA) and the
-// warp writes the slices to the k claimed rows and, for the shared
-// expert, to row nk + t. Longer rows are read twice after the scan. The row
+// warp writes the slices to the k claimed rows; the shared expert's row
+// nk + t needs no position and is written before the scan. Longer rows are
+// read twice after the scan. The row
 // loop is not unrolled: this kernel runs once per block, mostly from a cold
 // instruction cache, so its code is kept short.
 template <typename XT, bool SLICE>
@@ -210,6 +211,20 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
     const float inv = amax > 0.f ? 127.f / amax : 0.f;
 #pragma unroll
     for (int i = 0; i < kRegVec; ++i) slice4(v[i], inv, q0[i], q1[i]);
+    if (shared) {
+      // the shared expert's row (nk + t) needs no position: written now, so
+      // its stores overlap the scan and the position claims below
+      const size_t row = (size_t)n * k + t;
+#pragma unroll
+      for (int i = 0; i < kRegVec; ++i) {
+        const int c = lane * 4 + 128 * i;
+        if (c < H) {
+          *reinterpret_cast<uint32_t*>(s0 + row * H + c) = q0[i];
+          *reinterpret_cast<uint32_t*>(s1 + row * H + c) = q1[i];
+        }
+      }
+      if (lane == 31) scale[row] = amax / 127.f;
+    }
   }
   plan_scan(plan, n, k, E, H, I, Is, spec0, spec1, shared, blockIdx.x == 0, hist, offs, act, &bad, scan_tmp, nullptr,
             rec0, rec1);
@@ -256,10 +271,11 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
     }
     const float inv = amax > 0.f ? 127.f / amax : 0.f;
     // rows r < k: the claimed positions; row k: the shared expert's row
+    // (already written when the slices are held in registers)
 #pragma unroll 1
     for (int r = 0; r <= k; ++r) {
       const int pr = __shfl_sync(0xffffffffu, p, r < k ? r : 0);
-      const int row = r < k ? pr : (shared ? nk + t : -1);
+      const int row = r < k ? pr : (shared && !in_regs ? nk + t : -1);
       if (row < 0) continue;
       int8_t* d0 = s0 + (size_t)row * H;
       int8_t* d1 = s1 + (size_t)row * H;
@@ -282,7 +298,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const XT* __restrict__ h,
       }
     }
     if (lane < k && p >= 0) scale[p] = amax / 127.f;
-    if (lane == 31 && shared) scale[nk + t] = amax / 127.f;
+    if (lane == 31 && shared && !in_regs) scale[nk + t] = amax / 127.f;
   }
 }
 
