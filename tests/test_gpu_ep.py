@@ -33,6 +33,31 @@ def _expected(block, h, path, device, ep):
     return mb.forward(h, logits=ep.ops.route(h)[0], path=path)
 
 
+@pytest.mark.parametrize("m", [8, 200])
+@pytest.mark.parametrize("path", ["tc", "gemv", "gemm"])
+def test_rows_with_an_expert_id_out_of_range_come_back_nan(cuda, path, m):
+    """A row bound for an expert this rank does not hold (id = the rank's
+    expert count) makes the tallies disagree with the rows: the plan reports
+    it and holds no work items, no expert kernel reads a record, and every
+    row comes back NaN rather than a silent partial result. The same rows
+    with valid ids come back finite, before and after."""
+    block = synth.make_block(4, num_experts=16)
+    ops = EpCudaOps(block, 0, 1, cuda, PATHS[path])
+    x = torch.from_numpy(synth.make_tokens(5, m)).to(cuda)
+    meta = torch.zeros((m, 2), dtype=torch.int32, device=cuda)
+    meta[:, 0] = torch.arange(m, dtype=torch.int32, device=cuda) % 16
+    meta[:, 1] = torch.full((m,), 0.25, device=cuda).view(torch.int32)
+    y_ok = ops.rows(x, meta).clone()
+    bad = meta.clone()
+    bad[m // 2, 0] = 16
+    y_bad = ops.rows(x, bad).clone()
+    y_again = ops.rows(x, meta).clone()
+    torch.cuda.synchronize()
+    assert torch.isfinite(y_ok).all()
+    assert torch.isnan(y_bad).all()
+    assert torch.equal(y_again, y_ok)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("path", list(PATHS))
 def test_one_rank_equals_the_block(cuda, path, dtype):
