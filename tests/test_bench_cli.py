@@ -51,3 +51,32 @@ def test_reference_arm_uses_every_core_under_a_launcher_limit():
     cores = line["cpu_baseline"]["cores"]
     assert cores == len(os.sched_getaffinity(0))
     assert line["cpu_baseline"]["threads"]["blas"] == cores
+
+
+def test_expert_parallel_microbatch_sizes():
+    """Microbatches of the expert-parallel layer: half a rank's tokens within
+    4096..16384, a power of two that divides the rank's share, unless
+    --ep-microbatch names one."""
+    import argparse
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    args = argparse.Namespace(ep_tokens=65536, ep_microbatch=0)
+    assert [bench.ep_microbatch(args, w) for w in (1, 2, 4, 8)] == [16384, 16384, 8192, 4096]
+    for w in (1, 2, 4, 8):
+        assert (65536 // w) % bench.ep_microbatch(args, w) == 0
+    assert bench.ep_microbatch(argparse.Namespace(ep_tokens=65536, ep_microbatch=2048), 2) == 2048
+
+
+def test_roofline_traffic_comes_from_the_profiles():
+    """The DRAM traffic a bench line carries is the per-launch figure of an
+    ncu capture summarised under profiles/, named with the file it came from."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    for workload in ("prefill4096_int8_zipf", "decode8_int8"):
+        value, src = bench.traffic_from_profiles(workload, "gate_up")
+        assert value and value > 1e8 and src.startswith("profiles/")
+        assert f"traffic_per_launch_bytes[{workload}/gate_up]" in (ROOT / src).read_text()
+    assert bench.traffic_from_profiles("no_such_workload", "gate_up") == (None, None)
